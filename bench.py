@@ -1,0 +1,452 @@
+#!/usr/bin/env python
+"""Benchmark of the paged KV-cache decode path on B200.
+
+One *step* = one full 28-layer decode step of a Qwen3-ASR-0.6B-shaped decoder
+(random-init bf16 weights) for 64 sequences with seeded context lengths
+~U[200, 1500]: per layer one ``reshape_and_cache`` + one ``paged_attention``
+through the sm_100a kernels, the rest (GEMMs, norms, RoPE, lm_head, argmax)
+through torch; the step is a captured CUDA graph replayed per token, as in
+the reference (vasr-paged-attn/src/cuda_graph.rs).
+
+  value      tokens/s over all ranks, metadata already resident in HBM
+             (per step: device-side copy of that step's metadata into the
+             graph buffers + replay).
+  e2e        tokens/s through the engine's host-facing call: per step the
+             host builds the step metadata, copies it from pinned memory,
+             replays, and reads the next token ids back (synchronising).
+  roofline   the paged decode kernel alone: algorithmic KV bytes per launch
+             / CUDA-event launch time vs the measured HBM copy bandwidth.
+
+Multi-GPU (torchrun): request-level data parallelism, each rank holds its own
+decoder replica and page pool and decodes its own 64 sequences (weak
+scaling, no collective on the hot path; one all-reduce of the elapsed time
+outside the timed region).
+
+``--impl reference`` times the reference's CPU attention path (the C
+restatement in oracle/, all host threads) on the same contexts.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "qwen3asr.rs_b200"))
+
+METRIC = "decode tok/s & paged-attn KV-read GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+BATCH = 64
+CTX_LO, CTX_HI = 200, 1500
+BLOCK_SIZE = 16
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="target CPU time of the bounded cpu_baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------ helpers
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def context_lens(seed: int, rank: int):
+    import numpy as np
+
+    rng = np.random.default_rng(seed + 1000 * rank)
+    return rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int64)
+
+
+def load_peaks():
+    f = REPO / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_attention_sample(seed: int, target_seconds: float, steps: int | None = None):
+    """Time the oracle's f32 decode attention (reference CPU path restated in C, all threads).
+
+    A step is 28 layers of decode attention over the config-2 context set;
+    one layer's cache is generated and attended 28 times per step (the cost
+    per layer is identical). GEMMs are excluded, so this is an upper bound on
+    the CPU's decode tok/s.
+    """
+    import numpy as np
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import paged_ref as ref
+
+    lens = context_lens(seed, 0)
+    hq, hkv, d, bs = 16, 8, 128, BLOCK_SIZE
+    blocks = [-(-int(n) // bs) for n in lens]
+    nb = sum(blocks) + 1
+    rng = np.random.default_rng(seed)
+    kc = rng.standard_normal((nb, hkv, d // 4, bs, 4), dtype=np.float32)
+    vc = rng.standard_normal((nb, hkv, d, bs), dtype=np.float32)
+    perm = rng.permutation(np.arange(1, nb))
+    tables = np.zeros((BATCH, max(blocks)), np.uint32)
+    off = 0
+    for i, n in enumerate(blocks):
+        tables[i, :n] = perm[off:off + n]
+        off += n
+    q = rng.standard_normal((BATCH, hq, d), dtype=np.float32)
+    ctx = lens.astype(np.uint32)
+    threads = ref.max_threads()
+    ref.paged_attention(q, kc, vc, tables, ctx, d ** -0.5, use_double=False, threads=threads)
+    t0 = time.perf_counter()
+    ref.paged_attention(q, kc, vc, tables, ctx, d ** -0.5, use_double=False, threads=threads)
+    t_layer = time.perf_counter() - t0
+    n_layers = 28
+    if steps is None:
+        reps = max(1, int(target_seconds / max(t_layer, 1e-6)))
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            ref.paged_attention(q, kc, vc, tables, ctx, d ** -0.5, use_double=False, threads=threads)
+        t_layer = (time.perf_counter() - t0) / reps
+        return dict(tok_s=BATCH / (n_layers * t_layer), t_layer=t_layer, reps=reps, threads=threads)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        for _ in range(n_layers):
+            ref.paged_attention(q, kc, vc, tables, ctx, d ** -0.5, use_double=False, threads=threads)
+        times.append(time.perf_counter() - t0)
+    return dict(step_times=times, threads=threads)
+
+
+def cpu_info() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return  # other ranks exit without work
+    k, w = args.steps, args.warmup
+    # bounded: the reference arm runs min(steps, 3) timed steps of 28 CPU layers
+    ks = max(1, min(k, 3))
+    r = cpu_attention_sample(args.seed, args.cpu_seconds, steps=ks + min(w, 1))
+    times = r["step_times"][min(w, 1):]
+    step_s = statistics.mean(times)
+    value = BATCH / step_s
+    sample = (f"{ks} timed steps x 28 layers of decode attention, {BATCH} seqs, ctx U[{CTX_LO},{CTX_HI}], "
+              f"f32 C/OpenMP restatement of attention.rs, GEMMs excluded; {cpu_info()}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": ks, "warmup": min(w, 1), "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "config2: qwen3-asr-0.6B decode step attention, B=64, ctx U[200,1500]",
+                   "global_batch": BATCH, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": r["threads"], "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------- our arm
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from vasr_paged_attn import engine as eng
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+
+    rank, world, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device for --impl ours")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    cfg = eng.DecoderConfig.qwen3_asr_0_6b()
+    model = eng.RandomQwen3Decoder(cfg, dev, torch.bfloat16, seed=args.seed)
+    k_steps, w_steps = args.steps, max(3, args.warmup)
+    total_steps = 2 * (w_steps + k_steps) + 2  # device loop + e2e loop
+    lens0 = context_lens(args.seed, rank)
+    need_tok = lens0 + total_steps
+    blocks = np.array([-(-int(n) // BLOCK_SIZE) for n in need_tok])
+    nb = int(blocks.sum()) + 1
+    rng = np.random.default_rng(args.seed + 7 + rank)
+    perm = rng.permutation(np.arange(1, nb))
+    raw_cols = int(blocks.max())
+    from vasr_paged_attn import host
+    cols = host.bucket_block_table_cols(raw_cols, BLOCK_SIZE)
+    tables = np.zeros((BATCH, cols), np.int32)
+    off = 0
+    for i, n in enumerate(blocks):
+        tables[i, :n] = perm[off:off + n]
+        off += n
+    caches = eng.allocate_paged_cache(cfg, nb, BLOCK_SIZE, dev)
+    gen = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    for kc, vc in caches:  # prefilled synthetic cache contents
+        kc.normal_(generator=gen)
+        vc.normal_(generator=gen)
+
+    graph = eng.DecodeGraph(model, caches, BATCH, cols, BLOCK_SIZE)
+    graph.capture()
+
+    # per-step metadata, device resident: positions advance by one per step
+    steps_all = np.arange(total_steps)[:, None]
+    pos = lens0[None, :] + steps_all                                    # [S, B]
+    slots = tables[np.arange(BATCH)[None, :], pos // BLOCK_SIZE].astype(np.int64) * BLOCK_SIZE + pos % BLOCK_SIZE
+    ctx = (pos + 1).astype(np.int32)
+    d_pos = torch.from_numpy(pos.astype(np.int64)).to(dev)
+    d_slots = torch.from_numpy(slots).to(dev)
+    d_ctx = torch.from_numpy(ctx).to(dev)
+    d_tables = torch.from_numpy(tables).to(dev)
+    d_ids = torch.zeros(BATCH, dtype=torch.int64, device=dev)
+
+    def device_step(s):
+        graph.input_ids.copy_(graph.next_ids if s > 0 else d_ids)
+        graph.positions.copy_(d_pos[s])
+        graph.slot_mapping.copy_(d_slots[s])
+        graph.context_lens.copy_(d_ctx[s])
+        if s == 0:
+            graph.block_tables.copy_(d_tables)
+        graph.replay()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    s_idx = 0
+    for _ in range(w_steps):
+        device_step(s_idx)
+        s_idx += 1
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(k_steps):
+        device_step(s_idx)
+        s_idx += 1
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    dev_ms = max_over_ranks(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    value = world * BATCH * k_steps / (dev_ms / 1e3)
+
+    # ---- e2e: host-built metadata, pinned H2D, replay, D2H of next ids
+    meta_cache = host.metadata_cache(nb, cfg.num_kv_heads, cfg.head_dim, BLOCK_SIZE, "bf16")
+    h_ids = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
+    h_pos = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
+    h_slots = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
+    h_ctx = torch.zeros(BATCH, dtype=torch.int32).pin_memory()
+    h_tables = torch.zeros(BATCH, cols, dtype=torch.int32).pin_memory()
+    h_next = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
+    prompt_lens = [int(x) for x in lens0]
+    table_rows = [list(map(int, r[:n])) for r, n in zip(tables, blocks)]
+    stream = torch.cuda.current_stream()
+
+    def e2e_step(s):
+        # host metadata through the C++ mirror of decode_metadata_for_batch_step
+        meta = meta_cache.decode_metadata_for_batch_step(table_rows, prompt_lens, s, True)
+        h_slots.numpy()[:] = meta.slot_mapping
+        h_ctx.numpy()[:] = meta.context_lens
+        h_pos.numpy()[:] = np.asarray(meta.context_lens, dtype=np.int64) - 1
+        h_tables.numpy().reshape(-1)[:] = meta.block_tables_flat
+        graph.input_ids.copy_(h_ids, non_blocking=True)
+        graph.positions.copy_(h_pos, non_blocking=True)
+        graph.slot_mapping.copy_(h_slots, non_blocking=True)
+        graph.context_lens.copy_(h_ctx, non_blocking=True)
+        graph.block_tables.copy_(h_tables, non_blocking=True)
+        graph.replay()
+        h_next.copy_(graph.next_ids, non_blocking=True)
+        stream.synchronize()
+        h_ids.copy_(h_next)
+
+    for _ in range(w_steps):
+        e2e_step(s_idx)
+        s_idx += 1
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(k_steps):
+        e2e_step(s_idx)
+        s_idx += 1
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e_value = world * BATCH * k_steps / e2e_s
+    h2d = (h_ids.numel() * 8 + h_pos.numel() * 8 + h_slots.numel() * 8 + h_ctx.numel() * 4 +
+           h_tables.numel() * 4)
+    d2h = h_next.numel() * 8
+
+    # ---- roofline of the paged decode kernel: one launch per layer, events on its stream
+    last = s_idx - 1
+    ctx_last = torch.from_numpy(ctx[min(last, total_steps - 1)]).to(dev)
+    q = torch.randn(BATCH, cfg.num_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    mcl = cols * BLOCK_SIZE
+    for kc, vc in caches[:2]:
+        pa.paged_attention(q, None, None, kc, vc, d_tables, ctx_last, None, mcl, cfg.head_dim ** -0.5, 1.0,
+                           None, out=out)
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(3):
+        for kc, vc in caches:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            pa.paged_attention(q, None, None, kc, vc, d_tables, ctx_last, None, mcl, cfg.head_dim ** -0.5,
+                               1.0, None, out=out)
+            b.record()
+            evs.append((a, b))
+    torch.cuda.synchronize()
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    ctx_sum = int(ctx[min(last, total_steps - 1)].astype(np.int64).sum())
+    kv_bytes = ctx_sum * cfg.num_kv_heads * cfg.head_dim * 2 * 2
+    qo_bytes = BATCH * cfg.num_heads * cfg.head_dim * 2 * 2
+    alg_bytes = kv_bytes + qo_bytes
+    achieved = alg_bytes / (launch_ms / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    traffic = None
+    tf = REPO / "profiles" / "paged_decode_traffic.json"
+    if tf.exists():
+        ratio = json.loads(tf.read_text()).get("dram_bytes_per_algorithmic_byte")
+        if ratio:
+            traffic = ratio * alg_bytes
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_attention_sample(args.seed, args.cpu_seconds)
+        cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
+               "sample": (f"{r['reps']} x one decode-attention layer ({BATCH} seqs, ctx U[{CTX_LO},{CTX_HI}], "
+                          f"f32 C/OpenMP oracle), scaled to 28 layers per token step; GEMMs excluded; "
+                          f"{cpu_info()}")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": k_steps,
+            "warmup": w_steps, "ms_per_step": dev_ms / k_steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded contexts, random-init weights, N(0,1) cache)",
+            "config": {"workload": "config2: qwen3-asr-0.6B decode step, 28 layers, B=64 per GPU, "
+                                   "ctx U[200,1500], block_size 16",
+                       "model": "Qwen3-ASR-0.6B text decoder (random init)", "global_batch": BATCH * world,
+                       "seq_len": int(lens0.mean()), "parallelism": f"dp{world} (request-sharded)",
+                       "graph_cols": cols, "l2": "inputs larger than L2 (per step ~6.2 GB KV + 1.2 GB weights)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "kernel": "paged_decode_kernel",
+                         "peak_source": peak_kind, "launch_us": launch_ms * 1e3,
+                         "algorithmic_bytes_per_launch": alg_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 2 * cfg.num_layers * k_steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    graph.release()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

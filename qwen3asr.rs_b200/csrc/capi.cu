@@ -1,0 +1,246 @@
+// capi.cu — the extern "C" boundary declared in include/vasr_pa.h.
+//
+// Every entry point validates sizes, dtype, block size and pointer alignment
+// on the host (mirroring the candle_core::bail! checks of
+// vasr-paged-attn/src/paged_kv_cache.rs:241-272 and the block-size rule of
+// paged_cache_runtime.rs:406-411) before anything is enqueued, then launches
+// on the caller's stream. Nothing here allocates or synchronises.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "launch.h"
+
+namespace {
+
+using vasr::AppendArgs;
+using vasr::DecodeArgs;
+using vasr::GatherArgs;
+using vasr::PrefillArgs;
+
+int elem_size(int32_t dtype) {
+  switch (dtype) {
+    case VASR_PA_F32: return 4;
+    case VASR_PA_BF16: return 2;
+    case VASR_PA_F16: return 2;
+    default: return 0;
+  }
+}
+bool block_size_ok(int32_t bs) { return bs == 8 || bs == 16 || bs == 32; }
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+cudaStream_t to_stream(vasr_pa_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Common cache-geometry checks shared by all page readers / writers.
+int check_geometry(int32_t dtype, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                   int64_t num_blocks) {
+  const int es = elem_size(dtype);
+  if (es == 0) return VASR_PA_EINVAL_DTYPE;
+  if (!block_size_ok(block_size)) return VASR_PA_EINVAL_BLOCKSIZE;
+  if (num_kv_heads <= 0 || head_dim <= 0 || num_blocks <= 0) return VASR_PA_EINVAL_SHAPE;
+  if (head_dim % (16 / es) != 0) return VASR_PA_EINVAL_SHAPE;  // key pack x must divide D
+  return VASR_PA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t vasr_pa_abi_version(void) { return VASR_PA_ABI_VERSION; }
+
+const char *vasr_pa_status_string(int32_t status) {
+  switch (status) {
+    case VASR_PA_OK: return "ok";
+    case VASR_PA_EINVAL_SHAPE: return "invalid shape";
+    case VASR_PA_EINVAL_DTYPE: return "invalid dtype";
+    case VASR_PA_EINVAL_BLOCKSIZE: return "paged cache block size must be 8, 16, or 32";
+    case VASR_PA_EINVAL_ALIGN: return "pointer or stride not 16-byte aligned";
+    case VASR_PA_EINVAL_WORKSPACE: return "workspace missing or too small";
+    case VASR_PA_ENOT_SUPPORTED: return "configuration not supported by the sm_100a kernels";
+    case VASR_PA_ELAUNCH: return "CUDA launch failed";
+    case VASR_PA_EDEVICE: return "no usable CUDA device";
+    case VASR_PA_EINVAL_POINTER: return "null or inaccessible pointer";
+    default: return "unknown status";
+  }
+}
+
+int32_t vasr_pa_reshape_and_cache(const void *key, const void *value, void *key_cache,
+                                  void *value_cache, const int64_t *slot_mapping,
+                                  int64_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                                  int32_t block_size, int64_t num_blocks, int64_t key_token_stride,
+                                  int64_t value_token_stride, int32_t dtype, const float *k_scale,
+                                  const float *v_scale, vasr_pa_stream_t stream) {
+  (void)k_scale;
+  (void)v_scale;
+  const int g = check_geometry(dtype, num_kv_heads, head_dim, block_size, num_blocks);
+  if (g != VASR_PA_OK) return g;
+  if (num_tokens < 0) return VASR_PA_EINVAL_SHAPE;
+  if (num_tokens == 0) return VASR_PA_OK;
+  if (num_tokens > 0x7fffffffLL * 16) return VASR_PA_EINVAL_SHAPE;
+  const int es = elem_size(dtype);
+  if (key_token_stride < (int64_t)num_kv_heads * head_dim ||
+      value_token_stride < (int64_t)num_kv_heads * head_dim)
+    return VASR_PA_EINVAL_SHAPE;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping) return VASR_PA_EINVAL_POINTER;
+  if (!aligned16(key) || !aligned16(value) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      (key_token_stride * es) % 16 != 0 || (value_token_stride * es) % 16 != 0 ||
+      !aligned(slot_mapping, 8))
+    return VASR_PA_EINVAL_ALIGN;
+  AppendArgs a{key, value, key_cache, value_cache, slot_mapping, num_tokens, num_kv_heads,
+               head_dim, block_size, num_blocks, key_token_stride, value_token_stride, dtype};
+  return vasr::launch_append(a, to_stream(stream));
+}
+
+size_t vasr_pa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads,
+                                              int32_t num_kv_heads, int32_t head_dim,
+                                              int32_t block_size, int32_t max_context_len,
+                                              int32_t dtype) {
+  (void)dtype;
+  if (num_seqs <= 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      !block_size_ok(block_size) || num_heads % num_kv_heads != 0)
+    return 0;
+  const int ctx = max_context_len > 0 ? max_context_len : 1;
+  return vasr::decode_workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, block_size,
+                                       ctx)
+      .total;
+}
+
+int32_t vasr_pa_paged_attention(void *out, const void *query, const void *key_cache,
+                                const void *value_cache, const uint32_t *block_tables,
+                                const uint32_t *context_lens, int32_t num_seqs, int32_t num_heads,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                int64_t num_blocks, int32_t max_num_blocks_per_seq,
+                                int32_t max_context_len, float scale, float softcapping,
+                                int64_t q_seq_stride, int32_t dtype, void *workspace,
+                                size_t workspace_bytes, vasr_pa_stream_t stream) {
+  const int g = check_geometry(dtype, num_kv_heads, head_dim, block_size, num_blocks);
+  if (g != VASR_PA_OK) return g;
+  if (num_seqs < 0 || num_heads <= 0 || num_heads % num_kv_heads != 0 ||
+      max_num_blocks_per_seq <= 0 || max_context_len < 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0) return VASR_PA_OK;
+  if (num_seqs > 65535 || num_kv_heads > 65535) return VASR_PA_EINVAL_SHAPE;
+  if (q_seq_stride < (int64_t)num_heads * head_dim) return VASR_PA_EINVAL_SHAPE;
+  if (!(softcapping > 0.f)) return VASR_PA_EINVAL_SHAPE;
+  const int es = elem_size(dtype);
+  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned16(query) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      (q_seq_stride * es) % 16 != 0 || !aligned(out, es) || !aligned(block_tables, 4) ||
+      !aligned(context_lens, 4) || (workspace && !aligned(workspace, 256)))
+    return VASR_PA_EINVAL_ALIGN;
+  DecodeArgs a{out, query, key_cache, value_cache, block_tables, context_lens, num_seqs,
+               num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_num_blocks_per_seq,
+               max_context_len > 0 ? max_context_len : 1, scale, softcapping, q_seq_stride, dtype,
+               workspace, workspace_bytes};
+  return vasr::launch_decode(a, to_stream(stream));
+}
+
+int32_t vasr_pa_gather_kv_cache(void *key_out, void *value_out, const void *key_cache,
+                                const void *value_cache, const uint32_t *block_tables,
+                                const uint32_t *cu_seqlens_kv, int32_t num_seqs,
+                                int32_t max_num_blocks_per_seq, int64_t total_tokens,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                int64_t num_blocks, int32_t dtype, vasr_pa_stream_t stream) {
+  const int g = check_geometry(dtype, num_kv_heads, head_dim, block_size, num_blocks);
+  if (g != VASR_PA_OK) return g;
+  if (num_seqs < 0 || max_num_blocks_per_seq <= 0 || total_tokens < 0) return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0 || total_tokens == 0) return VASR_PA_OK;
+  if (num_seqs > 65535) return VASR_PA_EINVAL_SHAPE;
+  if (!key_out || !value_out || !key_cache || !value_cache || !block_tables || !cu_seqlens_kv)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned16(key_out) || !aligned16(value_out) || !aligned16(key_cache) ||
+      !aligned16(value_cache) || !aligned(block_tables, 4) || !aligned(cu_seqlens_kv, 4))
+    return VASR_PA_EINVAL_ALIGN;
+  GatherArgs a{key_out, value_out, key_cache, value_cache, block_tables, cu_seqlens_kv, num_seqs,
+               max_num_blocks_per_seq, total_tokens, num_kv_heads, head_dim, block_size,
+               num_blocks, dtype};
+  return vasr::launch_gather(a, to_stream(stream));
+}
+
+int32_t vasr_pa_paged_attention_varlen_prefill(
+    void *out, const void *query, const void *key_cache, const void *value_cache,
+    const uint32_t *block_tables, const uint32_t *context_lens, const uint32_t *cu_seqlens_q,
+    int32_t num_seqs, int64_t total_q_tokens, int32_t max_query_len, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int64_t num_blocks,
+    int32_t max_num_blocks_per_seq, float scale, float softcapping, int64_t q_token_stride,
+    int32_t dtype, vasr_pa_stream_t stream) {
+  const int g = check_geometry(dtype, num_kv_heads, head_dim, block_size, num_blocks);
+  if (g != VASR_PA_OK) return g;
+  if (num_seqs < 0 || total_q_tokens < 0 || max_query_len < 0 || num_heads <= 0 ||
+      num_heads % num_kv_heads != 0 || max_num_blocks_per_seq <= 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0 || total_q_tokens == 0) return VASR_PA_OK;
+  if (q_token_stride < (int64_t)num_heads * head_dim) return VASR_PA_EINVAL_SHAPE;
+  if (!(softcapping > 0.f)) return VASR_PA_EINVAL_SHAPE;
+  const int es = elem_size(dtype);
+  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens ||
+      !cu_seqlens_q)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned16(query) || !aligned16(out) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      (q_token_stride * es) % 16 != 0 || !aligned(block_tables, 4) || !aligned(context_lens, 4) ||
+      !aligned(cu_seqlens_q, 4))
+    return VASR_PA_EINVAL_ALIGN;
+  PrefillArgs a{out, query, key_cache, value_cache, block_tables, context_lens, cu_seqlens_q,
+                num_seqs, total_q_tokens, max_query_len, num_heads, num_kv_heads, head_dim,
+                block_size, num_blocks, max_num_blocks_per_seq, scale, softcapping,
+                q_token_stride, dtype};
+  return vasr::launch_prefill(a, to_stream(stream));
+}
+
+int32_t vasr_pa_copy_blocks(void *const *key_caches, void *const *value_caches,
+                            int32_t num_layers, const int64_t *block_mapping, int64_t num_pairs,
+                            int64_t num_blocks, int64_t block_bytes, vasr_pa_stream_t stream) {
+  if (num_layers <= 0 || num_layers > 128 || num_pairs < 0 || num_blocks <= 0 ||
+      block_bytes <= 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_pairs == 0) return VASR_PA_OK;
+  if (num_pairs > 0x7fffffffLL) return VASR_PA_EINVAL_SHAPE;
+  if (!key_caches || !value_caches || !block_mapping) return VASR_PA_EINVAL_POINTER;
+  if (block_bytes % 16 != 0 || !aligned(block_mapping, 8)) return VASR_PA_EINVAL_ALIGN;
+  for (int l = 0; l < num_layers; ++l) {
+    if (!key_caches[l] || !value_caches[l]) return VASR_PA_EINVAL_POINTER;
+    if (!aligned16(key_caches[l]) || !aligned16(value_caches[l])) return VASR_PA_EINVAL_ALIGN;
+  }
+  return vasr::launch_copy_blocks(key_caches, value_caches, num_layers, block_mapping, num_pairs,
+                                  num_blocks, block_bytes, to_stream(stream));
+}
+
+int32_t vasr_pa_swap_blocks(void *dst, const void *src, const int64_t *block_mapping,
+                            int64_t num_pairs, int64_t src_num_blocks, int64_t dst_num_blocks,
+                            int64_t block_bytes, vasr_pa_stream_t stream) {
+  if (num_pairs < 0 || src_num_blocks <= 0 || dst_num_blocks <= 0 || block_bytes <= 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_pairs == 0) return VASR_PA_OK;
+  if (num_pairs > 0x7fffffffLL) return VASR_PA_EINVAL_SHAPE;
+  if (!dst || !src || !block_mapping) return VASR_PA_EINVAL_POINTER;
+  if (block_bytes % 16 != 0 || !aligned16(dst) || !aligned16(src) || !aligned(block_mapping, 8))
+    return VASR_PA_EINVAL_ALIGN;
+  // All three buffers must be reachable from the device: device memory or
+  // page-locked host memory. Pageable host memory is rejected here.
+  const void *ptrs[3] = {dst, src, block_mapping};
+  for (const void *p : ptrs) {
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+      cudaGetLastError();
+      return VASR_PA_EINVAL_POINTER;
+    }
+    if (attr.type == cudaMemoryTypeUnregistered) return VASR_PA_EINVAL_POINTER;
+    if (attr.type == cudaMemoryTypeHost && attr.devicePointer != p) return VASR_PA_EINVAL_POINTER;
+  }
+  return vasr::launch_swap_blocks(dst, src, block_mapping, num_pairs, src_num_blocks,
+                                  dst_num_blocks, block_bytes, to_stream(stream));
+}
+
+int32_t vasr_pa_get_device_error(int32_t *out_bits, int32_t clear, vasr_pa_stream_t stream) {
+  if (!out_bits) return VASR_PA_EINVAL_POINTER;
+  uint32_t a = 0, b = 0, c = 0;
+  int r;
+  if ((r = vasr::read_error_kv_ops(&a, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
+  if ((r = vasr::read_error_decode(&b, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
+  if ((r = vasr::read_error_prefill(&c, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
+  *out_bits = (int32_t)(a | b | c);
+  return VASR_PA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,118 @@
+// decode.cu — launchers and instantiations of the paged decode kernel.
+#include "decode.cuh"
+#include "launch.h"
+
+namespace vasr {
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_heads,
+                                        int head_dim, int block_size, int max_context_len) {
+  DecodeWorkspace w;
+  w.pages_per_split = decode_pages_per_split(num_seqs, num_kv_heads, block_size, max_context_len);
+  const int P = w.pages_per_split * block_size;
+  w.max_splits = (max_context_len + P - 1) / P;
+  if (w.max_splits < 1) w.max_splits = 1;
+  const size_t slots = (size_t)num_seqs * num_kv_heads * w.max_splits;
+  const int G = num_heads / num_kv_heads;
+  // The arrival counters sit in a fixed region at offset 0 that every call
+  // returns to zero, so one zero-filled workspace stays valid across calls of
+  // any shape (partials of an earlier call never overlap a later call's
+  // counters).
+  w.off_counters = 0;
+  w.off_o = align256(kDecodeMaxCounters * sizeof(uint32_t));
+  w.off_ml = align256(w.off_o + slots * G * head_dim * sizeof(float));
+  w.total = align256(w.off_ml + slots * G * sizeof(float2));
+  return w;
+}
+
+namespace {
+
+template <typename T, int BS, int D, int G>
+int launch_decode_t(const DecodeArgs &a, cudaStream_t stream) {
+  using C = DecodeCfg<T, BS, D, G>;
+  const DecodeWorkspace w = decode_workspace_layout(a.num_seqs, a.num_heads, a.num_kv_heads,
+                                                    a.head_dim, a.block_size, a.max_context_len);
+  if ((size_t)a.num_seqs * a.num_kv_heads > kDecodeMaxCounters) return VASR_PA_ENOT_SUPPORTED;
+  if (a.workspace == nullptr || a.workspace_bytes < w.total) return VASR_PA_EINVAL_WORKSPACE;
+  if (w.pages_per_split > C::kMaxPagesPerSplit) return VASR_PA_ENOT_SUPPORTED;
+  DecodeParams p;
+  p.out = a.out;
+  p.q = a.query;
+  p.k_cache = a.key_cache;
+  p.v_cache = a.value_cache;
+  p.block_tables = a.block_tables;
+  p.context_lens = a.context_lens;
+  unsigned char *ws = static_cast<unsigned char *>(a.workspace);
+  p.ws_o = reinterpret_cast<float *>(ws + w.off_o);
+  p.ws_ml = reinterpret_cast<float2 *>(ws + w.off_ml);
+  p.counters = reinterpret_cast<uint32_t *>(ws + w.off_counters);
+  p.q_seq_stride = a.q_seq_stride;
+  p.num_blocks = a.num_blocks;
+  p.num_seqs = a.num_seqs;
+  p.num_heads = a.num_heads;
+  p.num_kv_heads = a.num_kv_heads;
+  p.cols = a.max_num_blocks_per_seq;
+  p.pages_per_split = w.pages_per_split;
+  p.max_splits = w.max_splits;
+  p.scale = a.scale;
+  p.softcap = a.softcapping;
+  static std::atomic<uint64_t> attr_done{0};
+  if (!ensure_smem_attr(paged_decode_kernel<T, BS, D, G>, C::kSmemBytes, attr_done))
+    return VASR_PA_ELAUNCH;
+  dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+  paged_decode_kernel<T, BS, D, G><<<grid, C::kThreads, C::kSmemBytes, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
+template <typename T, int D, int G>
+int dispatch_bs(const DecodeArgs &a, cudaStream_t s) {
+  switch (a.block_size) {
+    case 8: return launch_decode_t<T, 8, D, G>(a, s);
+    case 16: return launch_decode_t<T, 16, D, G>(a, s);
+    case 32: return launch_decode_t<T, 32, D, G>(a, s);
+    default: return VASR_PA_EINVAL_BLOCKSIZE;
+  }
+}
+
+template <typename T>
+int dispatch_g(const DecodeArgs &a, cudaStream_t s) {
+  const int G = a.num_heads / a.num_kv_heads;
+  if (a.head_dim != 128) return VASR_PA_ENOT_SUPPORTED;
+  switch (G) {
+    case 1: return dispatch_bs<T, 128, 1>(a, s);
+    case 2: return dispatch_bs<T, 128, 2>(a, s);
+    case 4: return dispatch_bs<T, 128, 4>(a, s);
+    default: return VASR_PA_ENOT_SUPPORTED;
+  }
+}
+
+}  // namespace
+
+int launch_decode(const DecodeArgs &a, cudaStream_t s) {
+  switch (a.dtype) {
+    case VASR_PA_F32: return dispatch_g<float>(a, s);
+    case VASR_PA_BF16: return dispatch_g<__nv_bfloat16>(a, s);
+    case VASR_PA_F16: return dispatch_g<__half>(a, s);
+    default: return VASR_PA_EINVAL_DTYPE;
+  }
+}
+
+int read_error_decode(uint32_t *bits, bool clear, cudaStream_t s) {
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_device_error, sizeof(v), 0, cudaMemcpyDeviceToHost, s) !=
+      cudaSuccess)
+    return VASR_PA_ELAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return VASR_PA_ELAUNCH;
+  if (clear) {
+    const uint32_t z = 0;
+    if (cudaMemcpyToSymbolAsync(g_device_error, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s) !=
+        cudaSuccess)
+      return VASR_PA_ELAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return VASR_PA_ELAUNCH;
+  }
+  *bits = v;
+  return VASR_PA_OK;
+}
+
+}  // namespace vasr

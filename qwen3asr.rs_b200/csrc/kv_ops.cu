@@ -1,0 +1,414 @@
+// kv_ops.cu — HBM-bound cache kernels for sm_100a: KV append
+// (reshape_and_cache), gather_kv_cache, copy_blocks and swap_blocks.
+//
+// None of these does arithmetic on the values: every kernel is a byte-exact
+// permutation of its input, moved in 16-byte vectors wherever the cache
+// layout allows it.
+#include "common.cuh"
+#include "launch.h"
+
+namespace vasr {
+namespace {
+
+// ======================================================== reshape_and_cache
+// Reference semantics: mistralrs_paged_attn::reshape_and_cache as called at
+// vasr-models/src/model/thinker_text.rs:1101-1109 / :1324-1332; layout from
+// vasr-paged-attn/src/paged_kv_cache.rs:285-294.
+//
+// A CTA stages a tile of up to 16 tokens x (up to 2 KB of heads) of K and V
+// in shared memory with coalesced 16-byte loads, then
+//  - writes K as 16-byte chunks K[blk, h, c, off, 0:x], threads ordered
+//    token-fastest so consecutive offsets of one page form contiguous runs;
+//  - writes V by runs: a run is up to 16/sizeof(T) tokens with consecutive
+//    slots inside one aligned 16-byte group of a page row V[blk, h, d, :].
+//    A full aligned run is one 16-byte store; anything else falls back to
+//    element stores. Prefill chunks therefore store V in 16-byte vectors;
+//    decode (one token per page) cannot, by the layout.
+constexpr int kAppendThreads = 256;
+constexpr int kAppendMaxTokens = 16;
+constexpr int kAppendRowBytes = 2048;                 // bytes of heads per tile row
+constexpr int kAppendRowPitch = kAppendRowBytes + 16;  // +16 B: conflict-free columns
+
+struct AppendParams {
+  const unsigned char *key;
+  const unsigned char *value;
+  unsigned char *k_cache;
+  unsigned char *v_cache;
+  const int64_t *slots;
+  int64_t num_tokens;
+  int64_t k_stride_bytes;
+  int64_t v_stride_bytes;
+  int64_t num_blocks;
+  int num_kv_heads;
+  int tile_tokens;
+  int heads_per_tile;
+};
+
+template <typename T, int BS, int D>
+__global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(const AppendParams p) {
+  constexpr int kX = Elem<T>::kX;
+  constexpr int kCH = D / kX;          // 16-byte chunks per (token, head)
+  constexpr int kTPS = kX;             // tokens per 16-byte V group
+  constexpr int kES = (int)sizeof(T);
+  extern __shared__ __align__(16) unsigned char sm[];
+  unsigned char *kt = sm;
+  unsigned char *vt = sm + kAppendMaxTokens * kAppendRowPitch;
+  int64_t *s_slot = reinterpret_cast<int64_t *>(vt + kAppendMaxTokens * kAppendRowPitch);
+  int *s_run_start = reinterpret_cast<int *>(s_slot + kAppendMaxTokens);
+  int *s_run_len = s_run_start + kAppendMaxTokens;
+  int *s_nruns = s_run_len + kAppendMaxTokens;
+
+  const int TT = p.tile_tokens;
+  const int64_t t0 = (int64_t)blockIdx.x * TT;
+  const int h0 = blockIdx.y * p.heads_per_tile;
+  const int HC = min(p.heads_per_tile, p.num_kv_heads - h0);
+  const int ntok = (int)min((int64_t)TT, p.num_tokens - t0);
+  const int64_t max_slot = p.num_blocks * BS;
+  const int tid = threadIdx.x;
+
+  if (tid < ntok) {
+    int64_t s = p.slots[t0 + tid];
+    if (s >= max_slot) {
+      raise_device_error(VASR_PA_DERR_SLOT_RANGE);
+      s = -1;
+    }
+    s_slot[tid] = s;
+  }
+  // coalesced 16-byte loads of the tile
+  const int row_chunks = HC * kCH;
+  for (int i = tid; i < ntok * row_chunks; i += kAppendThreads) {
+    const int tt = i / row_chunks;
+    const int r = i - tt * row_chunks;
+    const int64_t col = (int64_t)h0 * D * kES + (int64_t)r * 16;
+    const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(p.key + (t0 + tt) * p.k_stride_bytes + col));
+    const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(p.value + (t0 + tt) * p.v_stride_bytes + col));
+    *reinterpret_cast<uint4 *>(kt + tt * kAppendRowPitch + r * 16) = kv;
+    *reinterpret_cast<uint4 *>(vt + tt * kAppendRowPitch + r * 16) = vv;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // split the tile into V runs (consecutive slots, same aligned group)
+    int n = 0;
+    int tt = 0;
+    while (tt < ntok) {
+      const int64_t s = s_slot[tt];
+      if (s < 0) {
+        ++tt;
+        continue;
+      }
+      int len = 1;
+      while (tt + len < ntok && len < kTPS && s_slot[tt + len] == s + len && ((s + len) % kTPS) != 0)
+        ++len;
+      s_run_start[n] = tt;
+      s_run_len[n] = len;
+      ++n;
+      tt += len;
+    }
+    s_nruns[0] = n;
+  }
+  // K: (head, chunk, token) with token fastest
+  for (int i = tid; i < ntok * row_chunks; i += kAppendThreads) {
+    const int tt = i % ntok;
+    const int r = i / ntok;
+    const int64_t s = s_slot[tt];
+    if (s < 0) continue;
+    const int hc = r / kCH;
+    const int c = r - hc * kCH;
+    const int64_t blk = s / BS;
+    const int off = (int)(s - blk * BS);
+    const int64_t dst = ((((blk * p.num_kv_heads + h0 + hc) * kCH + c) * BS) + off) * 16;
+    *reinterpret_cast<uint4 *>(p.k_cache + dst) =
+        *reinterpret_cast<const uint4 *>(kt + tt * kAppendRowPitch + r * 16);
+  }
+  __syncthreads();
+  // V: (head, dim, run) with run fastest
+  const int nruns = s_nruns[0];
+  const int nitems = nruns * HC * D;
+  for (int i = tid; i < nitems; i += kAppendThreads) {
+    const int j = i % nruns;
+    const int hd = i / nruns;
+    const int hc = hd / D;
+    const int d = hd - hc * D;
+    const int tt0 = s_run_start[j];
+    const int len = s_run_len[j];
+    const int64_t s = s_slot[tt0];
+    const int64_t blk = s / BS;
+    const int off = (int)(s - blk * BS);
+    const int64_t row = ((blk * p.num_kv_heads + h0 + hc) * D + d) * BS;
+    const unsigned char *src = vt + tt0 * kAppendRowPitch + (hc * D + d) * kES;
+    T *dst = reinterpret_cast<T *>(p.v_cache) + row + off;
+    if (len == kTPS && (off % kTPS) == 0) {
+      T vals[kTPS];
+#pragma unroll
+      for (int e = 0; e < kTPS; ++e) vals[e] = *reinterpret_cast<const T *>(src + e * kAppendRowPitch);
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(vals);
+    } else {
+      for (int e = 0; e < len; ++e) dst[e] = *reinterpret_cast<const T *>(src + e * kAppendRowPitch);
+    }
+  }
+}
+
+template <typename T, int BS, int D>
+int launch_append_t(const AppendArgs &a, cudaStream_t stream) {
+  AppendParams p;
+  p.key = static_cast<const unsigned char *>(a.key);
+  p.value = static_cast<const unsigned char *>(a.value);
+  p.k_cache = static_cast<unsigned char *>(a.key_cache);
+  p.v_cache = static_cast<unsigned char *>(a.value_cache);
+  p.slots = a.slot_mapping;
+  p.num_tokens = a.num_tokens;
+  p.k_stride_bytes = a.key_token_stride * (int64_t)sizeof(T);
+  p.v_stride_bytes = a.value_token_stride * (int64_t)sizeof(T);
+  p.num_blocks = a.num_blocks;
+  p.num_kv_heads = a.num_kv_heads;
+  // Decode-sized calls (one token per page) get one token per CTA for
+  // parallelism; prefill-sized calls get 8/16-token tiles so V runs form
+  // 16-byte stores.
+  int tt = 1;
+  if (a.num_tokens >= 4096) tt = 16;
+  else if (a.num_tokens >= 128) tt = 8;
+  p.tile_tokens = tt;
+  p.heads_per_tile = kAppendRowBytes / (D * (int)sizeof(T));
+  const int smem = 2 * kAppendMaxTokens * kAppendRowPitch + kAppendMaxTokens * 8 +
+                   2 * kAppendMaxTokens * 4 + 16;
+  static std::atomic<uint64_t> attr_done{0};
+  if (!ensure_smem_attr(kv_append_kernel<T, BS, D>, smem, attr_done)) return VASR_PA_ELAUNCH;
+  dim3 grid((unsigned)((a.num_tokens + tt - 1) / tt),
+            (unsigned)((a.num_kv_heads + p.heads_per_tile - 1) / p.heads_per_tile));
+  kv_append_kernel<T, BS, D><<<grid, kAppendThreads, smem, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
+// ========================================================== gather_kv_cache
+// Reference semantics: mistralrs_paged_attn::gather_kv_cache as called at
+// thinker_text.rs:190-198 / :1344-1352: packed [sum kv, Hkv, D] K and V.
+// One CTA per (page, sequence): K chunks are copied as 16-byte vectors;
+// V pages [D][BS] are transposed through shared memory.
+struct GatherParams {
+  unsigned char *k_out;
+  unsigned char *v_out;
+  const unsigned char *k_cache;
+  const unsigned char *v_cache;
+  const uint32_t *block_tables;
+  const uint32_t *cu;
+  int64_t num_blocks;
+  int cols;
+  int num_kv_heads;
+};
+
+template <typename T, int BS, int D>
+__global__ void __launch_bounds__(256) gather_kernel(const GatherParams p) {
+  constexpr int kX = Elem<T>::kX;
+  constexpr int kCH = D / kX;
+  constexpr int kES = (int)sizeof(T);
+  constexpr int kRowWords = BS * kES / 4 + 1;  // padded V row, in 32-bit words
+  extern __shared__ __align__(16) uint32_t vsm[];
+  const int page = blockIdx.x;
+  const int b = blockIdx.y;
+  const int64_t start = p.cu[b];
+  const int64_t len = (int64_t)p.cu[b + 1] - start;
+  if ((int64_t)page * BS >= len) return;
+  const int n = (int)min((int64_t)BS, len - (int64_t)page * BS);
+  uint32_t blk = p.block_tables[(int64_t)b * p.cols + page];
+  if ((int64_t)blk >= p.num_blocks) {
+    if (threadIdx.x == 0) raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
+    blk = 0;
+  }
+  const int H = p.num_kv_heads;
+  const int64_t tok0 = start + (int64_t)page * BS;
+  const int64_t page_bytes = (int64_t)D * BS * kES;
+  // K
+  for (int i = threadIdx.x; i < n * H * kCH; i += blockDim.x) {
+    const int c = i % kCH;
+    const int h = (i / kCH) % H;
+    const int t = i / (kCH * H);
+    const unsigned char *src = p.k_cache + ((int64_t)blk * H + h) * page_bytes + ((int64_t)c * BS + t) * 16;
+    unsigned char *dst = p.k_out + ((tok0 + t) * H + h) * (int64_t)D * kES + c * 16;
+    *reinterpret_cast<uint4 *>(dst) = __ldg(reinterpret_cast<const uint4 *>(src));
+  }
+  // V, one head at a time through shared memory
+  for (int h = 0; h < H; ++h) {
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(p.v_cache + ((int64_t)blk * H + h) * page_bytes);
+    for (int w = threadIdx.x; w < D * BS * kES / 4; w += blockDim.x) {
+      const int d = w / (BS * kES / 4);
+      const int r = w - d * (BS * kES / 4);
+      vsm[d * kRowWords + r] = __ldg(src + w);
+    }
+    __syncthreads();
+    const unsigned char *vb = reinterpret_cast<const unsigned char *>(vsm);
+    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
+      const int d = i % D;
+      const int t = i / D;
+      const T v = *reinterpret_cast<const T *>(vb + d * kRowWords * 4 + t * kES);
+      reinterpret_cast<T *>(p.v_out)[((tok0 + t) * H + h) * (int64_t)D + d] = v;
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T, int BS, int D>
+int launch_gather_t(const GatherArgs &a, cudaStream_t stream) {
+  GatherParams p;
+  p.k_out = static_cast<unsigned char *>(a.key_out);
+  p.v_out = static_cast<unsigned char *>(a.value_out);
+  p.k_cache = static_cast<const unsigned char *>(a.key_cache);
+  p.v_cache = static_cast<const unsigned char *>(a.value_cache);
+  p.block_tables = a.block_tables;
+  p.cu = a.cu_seqlens_kv;
+  p.num_blocks = a.num_blocks;
+  p.cols = a.max_num_blocks_per_seq;
+  p.num_kv_heads = a.num_kv_heads;
+  const int smem = D * (BS * (int)sizeof(T) / 4 + 1) * 4;
+  dim3 grid((unsigned)a.max_num_blocks_per_seq, (unsigned)a.num_seqs);
+  gather_kernel<T, BS, D><<<grid, 256, smem, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
+// ============================================================ block copies
+// copy_blocks: one CTA per (pair, layer, K|V) moves one block with 16-byte
+// loads; each thread keeps kCopyUnroll loads in flight.
+constexpr int kMaxLayers = 128;
+constexpr int kCopyThreads = 256;
+constexpr int kCopyUnroll = 8;
+
+struct CopyBlocksParams {
+  unsigned char *k[kMaxLayers];
+  unsigned char *v[kMaxLayers];
+  const int64_t *mapping;
+  int64_t num_blocks;
+  int64_t block_bytes;
+};
+
+__device__ __forceinline__ void copy_block_bytes(unsigned char *dst, const unsigned char *src,
+                                                 int64_t bytes) {
+  const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+  uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+  const int64_t n = bytes / 16;
+  const int64_t step = (int64_t)kCopyThreads * kCopyUnroll;
+  int64_t base = 0;
+  for (; base + step <= n; base += step) {
+    uint4 r[kCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) r[u] = __ldcs(s4 + base + u * kCopyThreads + threadIdx.x);
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) __stcs(d4 + base + u * kCopyThreads + threadIdx.x, r[u]);
+  }
+  for (int64_t i = base + threadIdx.x; i < n; i += kCopyThreads) __stcs(d4 + i, __ldcs(s4 + i));
+}
+
+__global__ void __launch_bounds__(kCopyThreads) copy_blocks_kernel(const CopyBlocksParams p) {
+  const int64_t pair = blockIdx.x;
+  const int layer = blockIdx.y;
+  const int64_t src = p.mapping[2 * pair];
+  const int64_t dst = p.mapping[2 * pair + 1];
+  if (src < 0 || dst < 0 || src >= p.num_blocks || dst >= p.num_blocks) {
+    if (threadIdx.x == 0) raise_device_error(VASR_PA_DERR_MAPPING_RANGE);
+    return;
+  }
+  unsigned char *base = (blockIdx.z == 0) ? p.k[layer] : p.v[layer];
+  copy_block_bytes(base + dst * p.block_bytes, base + src * p.block_bytes, p.block_bytes);
+}
+
+struct SwapParams {
+  unsigned char *dst;
+  const unsigned char *src;
+  const int64_t *mapping;
+  int64_t src_blocks;
+  int64_t dst_blocks;
+  int64_t block_bytes;
+};
+
+__global__ void __launch_bounds__(kCopyThreads) swap_blocks_kernel(const SwapParams p) {
+  const int64_t pair = blockIdx.x;
+  const int64_t src = p.mapping[2 * pair];
+  const int64_t dst = p.mapping[2 * pair + 1];
+  if (src < 0 || dst < 0 || src >= p.src_blocks || dst >= p.dst_blocks) {
+    if (threadIdx.x == 0) raise_device_error(VASR_PA_DERR_MAPPING_RANGE);
+    return;
+  }
+  copy_block_bytes(p.dst + dst * p.block_bytes, p.src + src * p.block_bytes, p.block_bytes);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- launchers
+int launch_append(const AppendArgs &a, cudaStream_t s) {
+#define VASR_APPEND_CASE(T, BS_, D_) \
+  if (a.block_size == BS_ && a.head_dim == D_) return launch_append_t<T, BS_, D_>(a, s);
+#define VASR_APPEND_T(T)                                                            \
+  VASR_APPEND_CASE(T, 8, 64) VASR_APPEND_CASE(T, 16, 64) VASR_APPEND_CASE(T, 32, 64) \
+  VASR_APPEND_CASE(T, 8, 128) VASR_APPEND_CASE(T, 16, 128) VASR_APPEND_CASE(T, 32, 128) \
+  VASR_APPEND_CASE(T, 8, 256) VASR_APPEND_CASE(T, 16, 256) VASR_APPEND_CASE(T, 32, 256)
+  if (a.dtype == VASR_PA_F32) { VASR_APPEND_T(float) }
+  if (a.dtype == VASR_PA_BF16) { VASR_APPEND_T(__nv_bfloat16) }
+  if (a.dtype == VASR_PA_F16) { VASR_APPEND_T(__half) }
+#undef VASR_APPEND_T
+#undef VASR_APPEND_CASE
+  return VASR_PA_ENOT_SUPPORTED;
+}
+
+int launch_gather(const GatherArgs &a, cudaStream_t s) {
+#define VASR_GATHER_CASE(T, BS_, D_) \
+  if (a.block_size == BS_ && a.head_dim == D_) return launch_gather_t<T, BS_, D_>(a, s);
+#define VASR_GATHER_T(T)                                                             \
+  VASR_GATHER_CASE(T, 8, 64) VASR_GATHER_CASE(T, 16, 64) VASR_GATHER_CASE(T, 32, 64) \
+  VASR_GATHER_CASE(T, 8, 128) VASR_GATHER_CASE(T, 16, 128) VASR_GATHER_CASE(T, 32, 128) \
+  VASR_GATHER_CASE(T, 8, 256) VASR_GATHER_CASE(T, 16, 256) VASR_GATHER_CASE(T, 32, 256)
+  if (a.dtype == VASR_PA_F32) { VASR_GATHER_T(float) }
+  if (a.dtype == VASR_PA_BF16) { VASR_GATHER_T(__nv_bfloat16) }
+  if (a.dtype == VASR_PA_F16) { VASR_GATHER_T(__half) }
+#undef VASR_GATHER_T
+#undef VASR_GATHER_CASE
+  return VASR_PA_ENOT_SUPPORTED;
+}
+
+int launch_copy_blocks(void *const *k, void *const *v, int layers, const int64_t *mapping,
+                       int64_t pairs, int64_t num_blocks, int64_t block_bytes, cudaStream_t s) {
+  if (layers > kMaxLayers) return VASR_PA_EINVAL_SHAPE;
+  CopyBlocksParams p;
+  for (int l = 0; l < layers; ++l) {
+    p.k[l] = static_cast<unsigned char *>(k[l]);
+    p.v[l] = static_cast<unsigned char *>(v[l]);
+  }
+  for (int l = layers; l < kMaxLayers; ++l) p.k[l] = p.v[l] = nullptr;
+  p.mapping = mapping;
+  p.num_blocks = num_blocks;
+  p.block_bytes = block_bytes;
+  // pairs on x (up to 2^31-1), layers on y, K/V on z
+  dim3 grid((unsigned)pairs, (unsigned)layers, 2);
+  copy_blocks_kernel<<<grid, kCopyThreads, 0, s>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
+int launch_swap_blocks(void *dst, const void *src, const int64_t *mapping, int64_t pairs,
+                       int64_t src_blocks, int64_t dst_blocks, int64_t block_bytes,
+                       cudaStream_t s) {
+  SwapParams p;
+  p.dst = static_cast<unsigned char *>(dst);
+  p.src = static_cast<const unsigned char *>(src);
+  p.mapping = mapping;
+  p.src_blocks = src_blocks;
+  p.dst_blocks = dst_blocks;
+  p.block_bytes = block_bytes;
+  swap_blocks_kernel<<<(unsigned)pairs, kCopyThreads, 0, s>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
+int read_error_kv_ops(uint32_t *bits, bool clear, cudaStream_t s) {
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_device_error, sizeof(v), 0, cudaMemcpyDeviceToHost, s) !=
+      cudaSuccess)
+    return VASR_PA_ELAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return VASR_PA_ELAUNCH;
+  if (clear) {
+    const uint32_t z = 0;
+    if (cudaMemcpyToSymbolAsync(g_device_error, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s) !=
+        cudaSuccess)
+      return VASR_PA_ELAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return VASR_PA_ELAUNCH;
+  }
+  *bits = v;
+  return VASR_PA_OK;
+}
+
+}  // namespace vasr

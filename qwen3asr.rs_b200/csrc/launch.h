@@ -1,0 +1,133 @@
+// launch.h — internal interface between the C ABI (capi.cu) and the kernel
+// translation units. Argument structs carry already-validated values.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+#include "../../include/vasr_pa.h"
+
+namespace vasr {
+
+struct AppendArgs {
+  const void *key;
+  const void *value;
+  void *key_cache;
+  void *value_cache;
+  const int64_t *slot_mapping;
+  int64_t num_tokens;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  int64_t num_blocks;
+  int64_t key_token_stride;
+  int64_t value_token_stride;
+  int dtype;
+};
+
+struct DecodeArgs {
+  void *out;
+  const void *query;
+  const void *key_cache;
+  const void *value_cache;
+  const uint32_t *block_tables;
+  const uint32_t *context_lens;
+  int num_seqs;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  int64_t num_blocks;
+  int max_num_blocks_per_seq;
+  int max_context_len;
+  float scale;
+  float softcapping;
+  int64_t q_seq_stride;
+  int dtype;
+  void *workspace;
+  size_t workspace_bytes;
+};
+
+struct GatherArgs {
+  void *key_out;
+  void *value_out;
+  const void *key_cache;
+  const void *value_cache;
+  const uint32_t *block_tables;
+  const uint32_t *cu_seqlens_kv;
+  int num_seqs;
+  int max_num_blocks_per_seq;
+  int64_t total_tokens;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  int64_t num_blocks;
+  int dtype;
+};
+
+struct PrefillArgs {
+  void *out;
+  const void *query;
+  const void *key_cache;
+  const void *value_cache;
+  const uint32_t *block_tables;
+  const uint32_t *context_lens;
+  const uint32_t *cu_seqlens_q;
+  int num_seqs;
+  int64_t total_q_tokens;
+  int max_query_len;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  int64_t num_blocks;
+  int max_num_blocks_per_seq;
+  float scale;
+  float softcapping;
+  int64_t q_token_stride;
+  int dtype;
+};
+
+// Workspace layout of the decode kernel (all offsets 256-byte aligned):
+// [counters: kDecodeMaxCounters x u32][partial o][partial (m, l)].
+constexpr size_t kDecodeMaxCounters = 65536;  // num_seqs * num_kv_heads limit
+struct DecodeWorkspace {
+  int pages_per_split;
+  int max_splits;
+  size_t off_o, off_ml, off_counters, total;
+};
+DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_heads,
+                                        int head_dim, int block_size, int max_context_len);
+
+int launch_append(const AppendArgs &a, cudaStream_t s);
+int launch_decode(const DecodeArgs &a, cudaStream_t s);
+int launch_gather(const GatherArgs &a, cudaStream_t s);
+int launch_prefill(const PrefillArgs &a, cudaStream_t s);
+int launch_copy_blocks(void *const *k, void *const *v, int layers, const int64_t *mapping,
+                       int64_t pairs, int64_t num_blocks, int64_t block_bytes, cudaStream_t s);
+int launch_swap_blocks(void *dst, const void *src, const int64_t *mapping, int64_t pairs,
+                       int64_t src_blocks, int64_t dst_blocks, int64_t block_bytes,
+                       cudaStream_t s);
+
+int read_error_kv_ops(uint32_t *bits, bool clear, cudaStream_t s);
+int read_error_decode(uint32_t *bits, bool clear, cudaStream_t s);
+int read_error_prefill(uint32_t *bits, bool clear, cudaStream_t s);
+
+// Raise a kernel's dynamic shared-memory limit once per device. The
+// attribute is not a stream operation, so this is legal during capture.
+template <typename F>
+inline bool ensure_smem_attr(F *func, int bytes, std::atomic<uint64_t> &done_mask) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done_mask.load(std::memory_order_acquire) & bit) return true;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void *>(func),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  done_mask.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
+}
+
+}  // namespace vasr
