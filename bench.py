@@ -57,6 +57,12 @@ def parse_args():
                    help="target CPU time of the bounded cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--kernel", default=None,
+                   choices=["decode", "append", "prefill", "copy", "swap", "config1"],
+                   help="microbenchmark one kernel on its BASELINE config instead of the decode step")
+    p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
+    p.add_argument("--layers", type=int, default=28,
+                   help="distinct per-layer caches cycled through by --kernel decode/copy")
     return p.parse_args()
 
 
@@ -440,9 +446,186 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# -------------------------------------------------- kernel microbenchmarks
+def _events_time(fn, iters):
+    """Mean ms per call of fn(i) with CUDA events on the current stream (after 3 warm-ups)."""
+    import torch
+
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    evs = []
+    for i in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn(i)
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+
+def run_kernel_bench(args):
+    """One JSON line per kernel: device time per launch and the roofline fraction."""
+    import numpy as np
+    import torch
+
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = load_peaks()
+    rng = np.random.default_rng(args.seed)
+    hq, hkv, d, bs = 16, 8, 128, BLOCK_SIZE
+    lines = []
+
+    def pool(nb, layers, dtype=torch.bfloat16):
+        x = 16 // torch.empty((), dtype=dtype).element_size()
+        out = []
+        for _ in range(layers):
+            kc = torch.randn(nb, hkv, d // x, bs, x, device=dev).to(dtype)
+            vc = torch.randn(nb, hkv, d, bs, device=dev).to(dtype)
+            out.append((kc, vc))
+        return out
+
+    def tables_for(lens, nb, cols=None):
+        blocks = [-(-int(n) // bs) for n in lens]
+        perm = rng.permutation(np.arange(1, nb))
+        t = np.zeros((len(lens), cols or max(blocks)), np.int32)
+        off = 0
+        for i, n in enumerate(blocks):
+            t[i, :n] = perm[off:off + n]
+            off += n
+        return t
+
+    k = args.kernel
+    if k in ("decode", "config1"):
+        dtype = torch.float32 if k == "config1" else torch.bfloat16
+        if k == "config1":
+            lens = np.array([138, 513, 1024, 2049])
+            nb, layers = 512, 1
+        else:
+            lens = context_lens(args.seed, 0)
+            nb = sum(-(-int(n) // bs) for n in lens) + 1
+            layers = args.layers
+        caches = pool(nb, layers, dtype)
+        t = torch.from_numpy(tables_for(lens, nb)).to(dev)
+        ctx = torch.from_numpy(lens.astype(np.int32)).to(dev)
+        q = torch.randn(len(lens), hq, d, device=dev).to(dtype)
+        mcl = int(lens.max())
+        out = torch.empty_like(q)
+        es = q.element_size()
+
+        def launch(i):
+            kc, vc = caches[i % layers]
+            pa.paged_attention(q, None, None, kc, vc, t, ctx, None, mcl, d ** -0.5, 1.0, None, out=out)
+
+        ms = _events_time(launch, args.iters)
+        alg = int(lens.sum()) * hkv * d * 2 * es + q.numel() * es * 2
+        lines.append({"kernel": "paged_decode", "config": "config1" if k == "config1" else "config2",
+                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
+                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "layers_cycled": layers})
+        if k == "config1":
+            kn = torch.randn(4, hkv, d, device=dev)
+            sl = torch.from_numpy((t[:, 0].cpu().numpy().astype(np.int64) * bs)).to(dev)
+            ms = _events_time(lambda i: pa.reshape_and_cache(kn, kn, None, None, caches[0][0], caches[0][1], sl),
+                              args.iters)
+            alg = 4 * hkv * d * 4 * 2 * 2
+            lines.append({"kernel": "kv_append", "config": "config1", "us": ms * 1e3, "bytes": alg,
+                          "GB/s": alg / ms / 1e6})
+    elif k == "append":
+        for name, ntok, per_seq in (("config2_decode", 64, 1), ("config3_chunk", 32 * 256, 256)):
+            nb = ntok // per_seq * (-(-per_seq // bs)) + 16 + 1
+            kc, vc = pool(nb, 1)[0]
+            kv = torch.randn(ntok, hkv, d, device=dev).to(torch.bfloat16)
+            nseq = ntok // per_seq
+            t = tables_for([per_seq] * nseq, nb)
+            pos = np.arange(per_seq)
+            slots = np.concatenate([t[i, pos // bs].astype(np.int64) * bs + pos % bs for i in range(nseq)])
+            sl = torch.from_numpy(slots).to(dev)
+            ms = _events_time(lambda i: pa.reshape_and_cache(kv, kv, None, None, kc, vc, sl), args.iters)
+            alg = ntok * hkv * d * 2 * 2 * 2
+            lines.append({"kernel": "kv_append", "config": name, "tokens": ntok, "us": ms * 1e3,
+                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
+    elif k == "prefill":
+        sys.path.insert(0, str(REPO / "tests"))
+        sys.path.insert(0, str(REPO / "oracle"))
+        from cases import config3_rounds
+
+        lens, rounds = config3_rounds(args.seed)
+        nb = sum(-(-int(n) // bs) for n in lens) + 1
+        kc, vc = pool(nb, 1)[0]
+        t_all = tables_for(lens, nb)
+        total_flops, total_ms = 0.0, 0.0
+        for r in rounds:
+            idx = [i for (i, _, _) in r]
+            chunk = np.array([n for (_, _, n) in r])
+            ctx = np.array([s + n for (_, s, n) in r])
+            cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+            q = torch.randn(int(chunk.sum()), hq, d, device=dev).to(torch.bfloat16)
+            bt = torch.from_numpy(t_all[idx]).to(dev)
+            dctx = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+            dcu = torch.from_numpy(cu).to(dev)
+            mq = int(chunk.max())
+            ms = _events_time(lambda i: pa.paged_attention_varlen_prefill(q, kc, vc, bt, dctx, dcu, None, None,
+                                                                          d ** -0.5, 1.0, mq), args.iters)
+            vis = sum(sum(int(s) + j + 1 for j in range(int(n))) for (_, s, n) in r)
+            total_flops += 4.0 * d * hq * vis
+            total_ms += ms
+        tflops = total_flops / (total_ms / 1e3) / 1e12
+        mp = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
+        tpeak = float(mp.get("bf16_tflops", 1590.0))
+        lines.append({"kernel": "paged_prefill_varlen", "config": "config3 (one layer, all chunk rounds)",
+                      "rounds": len(rounds), "us_per_layer": total_ms * 1e3, "flops_per_layer": total_flops,
+                      "TFLOP/s": tflops, "frac_of_bf16_peak": tflops / tpeak,
+                      "tflops_28_layers": total_flops * 28 / 1e12})
+    elif k == "copy":
+        free, _ = torch.cuda.mem_get_info()
+        per_layer = 200_000 * hkv * d * bs * 2 * 2
+        layers = max(1, min(args.layers, int(free * 0.8 // per_layer)))
+        nb = 200_000
+        caches = []
+        for _ in range(layers):
+            caches.append((torch.empty(nb, hkv, d // 8, bs, 8, dtype=torch.bfloat16, device=dev),
+                           torch.empty(nb, hkv, d, bs, dtype=torch.bfloat16, device=dev)))
+        perm = rng.permutation(nb)
+        pairs = torch.from_numpy(np.stack([perm[:4096], perm[4096:8192]], 1).astype(np.int64)).to(dev)
+        ms = _events_time(lambda i: pa.copy_blocks([c[0] for c in caches], [c[1] for c in caches], pairs),
+                          args.iters)
+        alg = 4096 * layers * 2 * (hkv * d * bs * 2) * 2
+        lines.append({"kernel": "copy_blocks", "config": "config4", "layers_allocated": layers,
+                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
+                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak,
+                      "ms_28_layers_extrapolated": ms * 28 / layers})
+    elif k == "swap":
+        nb_dev, nb_host = 8192, 2048
+        dcache = torch.randn(nb_dev, hkv, d, bs, device=dev).to(torch.bfloat16)
+        hcache = torch.empty(nb_host, hkv, d, bs, dtype=torch.bfloat16).pin_memory()
+        src = rng.permutation(nb_dev)[:1024]
+        dst = rng.permutation(nb_host)[:1024]
+        out_map = torch.from_numpy(np.stack([src, dst], 1).astype(np.int64)).to(dev)
+        in_map = torch.from_numpy(np.stack([dst, src], 1).astype(np.int64)).to(dev)
+        blk = hkv * d * bs * 2
+        ms_out = _events_time(lambda i: pa.swap_blocks(dcache, hcache, out_map), args.iters)
+        ms_in = _events_time(lambda i: pa.swap_blocks(hcache, dcache, in_map), args.iters)
+        big = torch.empty(1024 * blk // 2, dtype=torch.bfloat16, device=dev)
+        hbig = torch.empty_like(big, device="cpu").pin_memory()
+        ms_d2h = _events_time(lambda i: hbig.copy_(big, non_blocking=True), args.iters)
+        ms_h2d = _events_time(lambda i: big.copy_(hbig, non_blocking=True), args.iters)
+        n = 1024 * blk
+        lines.append({"kernel": "swap_blocks", "config": "config4 (1024 blocks of one layer cache)",
+                      "d2h_GB/s": n / ms_out / 1e6, "h2d_GB/s": n / ms_in / 1e6,
+                      "pinned_copy_d2h_GB/s": n / ms_d2h / 1e6, "pinned_copy_h2d_GB/s": n / ms_h2d / 1e6,
+                      "bytes": n})
+    for ln in lines:
+        print(json.dumps(ln), flush=True)
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.kernel is not None:
+        run_kernel_bench(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

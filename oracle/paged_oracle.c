@@ -20,6 +20,8 @@
  *  - the cached causal mask of make_causal_mask_cached (attention.rs:86-149)
  *    for chunked prefill: query at absolute position p sees keys j <= p.
  *  - copy/swap blocks as plain sequential block copies.
+ * The attention entry points take f32 values laid out like a cache of any
+ * element size (x = 16 / element size is passed in).
  * Arithmetic is f32 like Candle's CPU path, or f64 accumulation when
  * `use_double` is set (a tighter second check). OpenMP parallelises over
  * (sequence, head) for the timed CPU baseline.
@@ -118,9 +120,9 @@ void oracle_swap_blocks(void *dst, const void *src, const int64_t *pairs, int64_
 /* One query row against keys [0, n_keys) of one sequence / kv head.
  * Restates attention.rs:243-286 for a single (batch, head, query) row. */
 static void attend_row(float *o, const float *q, const float *kc, const float *vc,
-                       const uint32_t *table, int64_t n_keys, int kvh, int H, int D, int BS,
+                       const uint32_t *table, int64_t n_keys, int kvh, int H, int D, int BS, int x,
                        float scale, float softcap, int use_double, float *w) {
-  const int x = 4; /* f32 cache */
+  /* x = key pack of the cache layout the values came from (16 / element size). */
   for (int64_t j = 0; j < n_keys; ++j) {
     const int64_t blk = table[j / BS];
     const int off = (int)(j % BS);
@@ -171,8 +173,8 @@ static void attend_row(float *o, const float *q, const float *kc, const float *v
 /* paged decode attention, f32 cache and q/out [B, Hq, D] contiguous. */
 void oracle_paged_attention_f32(float *out, const float *q, const float *kc, const float *vc,
                                 const uint32_t *block_tables, const uint32_t *ctx, int B, int Hq,
-                                int Hkv, int D, int BS, int cols, float scale, float softcap,
-                                int use_double, int threads) {
+                                int Hkv, int D, int BS, int x, int cols, float scale,
+                                float softcap, int use_double, int threads) {
   const int G = Hq / Hkv;
   if (threads > 0) omp_set_num_threads(threads);
 #pragma omp parallel for collapse(2) schedule(dynamic)
@@ -185,7 +187,7 @@ void oracle_paged_attention_f32(float *out, const float *q, const float *kc, con
         for (int d = 0; d < D; ++d) o[d] = 0.f;
       } else {
         attend_row(o, q + ((int64_t)b * Hq + h) * D, kc, vc, block_tables + (int64_t)b * cols, n,
-                   h / G, Hkv, D, BS, scale, softcap, use_double, w);
+                   h / G, Hkv, D, BS, x, scale, softcap, use_double, w);
       }
       free(w);
     }
@@ -195,7 +197,7 @@ void oracle_paged_attention_f32(float *out, const float *q, const float *kc, con
  * cu_q[b]..cu_q[b+1] at absolute positions ctx[b]-qlen+i. */
 void oracle_prefill_varlen_f32(float *out, const float *q, const float *kc, const float *vc,
                                const uint32_t *block_tables, const uint32_t *ctx,
-                               const uint32_t *cu_q, int B, int Hq, int Hkv, int D, int BS,
+                               const uint32_t *cu_q, int B, int Hq, int Hkv, int D, int BS, int x,
                                int cols, float scale, float softcap, int use_double, int threads) {
   const int G = Hq / Hkv;
   if (threads > 0) omp_set_num_threads(threads);
@@ -214,7 +216,7 @@ void oracle_prefill_varlen_f32(float *out, const float *q, const float *kc, cons
         for (int d = 0; d < D; ++d) o[d] = 0.f;
       } else {
         attend_row(o, q + (t * Hq + h) * D, kc, vc, block_tables + (int64_t)b * cols, n, h / G, Hkv,
-                   D, BS, scale, softcap, use_double, w);
+                   D, BS, x, scale, softcap, use_double, w);
       }
       free(w);
     }

@@ -578,9 +578,9 @@ def c_oracle() -> ctypes.CDLL:
         so.oracle_copy_blocks.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(vp), i32, vp, i64, i64]
         so.oracle_swap_blocks.argtypes = [vp, vp, vp, i64, i64]
         so.oracle_paged_attention_f32.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32,
-                                                  i32, f32, f32, i32, i32]
+                                                  i32, i32, f32, f32, i32, i32]
         so.oracle_prefill_varlen_f32.argtypes = [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32,
-                                                 i32, f32, f32, i32, i32]
+                                                 i32, i32, f32, f32, i32, i32]
         so.oracle_max_threads.restype = i32
         _SO = so
     return _SO
@@ -624,13 +624,14 @@ def swap_blocks(dst, src, pairs):
 
 def paged_attention(q, key_cache, value_cache, block_tables, context_lens, scale, softcap=1.0,
                     use_double=True, threads=0):
-    """f32 decode attention over an f32 paged cache (numpy arrays)."""
+    """f32 decode attention over f32 values in a paged layout (key pack = key_cache.shape[4])."""
     b, hq, d = q.shape
     hkv, bs = value_cache.shape[1], value_cache.shape[3]
     out = np.empty((b, hq, d), dtype=np.float32)
     c_oracle().oracle_paged_attention_f32(_ptr(out), _ptr(q), _ptr(key_cache), _ptr(value_cache),
                                           _ptr(block_tables), _ptr(context_lens), b, hq, hkv, d, bs,
-                                          block_tables.shape[1], scale, softcap, int(use_double), threads)
+                                          key_cache.shape[4], block_tables.shape[1], scale, softcap,
+                                          int(use_double), threads)
     return out
 
 
@@ -641,8 +642,8 @@ def prefill_varlen(q, key_cache, value_cache, block_tables, context_lens, cu_q, 
     out = np.empty((t, hq, d), dtype=np.float32)
     c_oracle().oracle_prefill_varlen_f32(_ptr(out), _ptr(q), _ptr(key_cache), _ptr(value_cache),
                                          _ptr(block_tables), _ptr(context_lens), _ptr(cu_q),
-                                         block_tables.shape[0], hq, hkv, d, bs, block_tables.shape[1],
-                                         scale, softcap, int(use_double), threads)
+                                         block_tables.shape[0], hq, hkv, d, bs, key_cache.shape[4],
+                                         block_tables.shape[1], scale, softcap, int(use_double), threads)
     return out
 
 

@@ -97,6 +97,15 @@ def make_decode_case(seed: int, cached_lens, dtype="f32", num_heads=16, num_kv_h
                      ctx.astype(np.uint32), tables, kc, vc, q, k_new, v_new, slots)
 
 
+def appended(case: PagedCase) -> PagedCase:
+    """The same case with its new token already in the pool (for decode-only checks)."""
+    kc, vc = case.key_cache.copy(), case.value_cache.copy()
+    ref.reshape_and_cache(case.k_new, case.v_new, kc, vc, case.slots, case.block_size)
+    return PagedCase(case.dtype, case.num_heads, case.num_kv_heads, case.head_dim, case.block_size,
+                     case.num_blocks, case.context_lens, case.block_tables, kc, vc, case.q,
+                     case.k_new, case.v_new, case.slots)
+
+
 def oracle_decode(case: PagedCase, scale=None, softcap=1.0, after_append=True, use_double=True):
     """Oracle output (f32) of append(new token) + paged decode for a case."""
     kc, vc = case.key_cache.copy(), case.value_cache.copy()
@@ -126,3 +135,76 @@ def uniform_lens(seed, n, lo, hi):
 def loguniform_lens(seed, n, lo, hi):
     r = np.random.default_rng(seed)
     return np.exp(r.uniform(np.log(lo), np.log(hi), size=n)).astype(np.int64)
+
+
+@dataclass
+class PrefillCase:
+    dtype: str
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int
+    block_size: int
+    context_lens: np.ndarray      # u32 [B] = cached + chunk
+    cu_q: np.ndarray              # u32 [B + 1]
+    block_tables: np.ndarray      # u32 [B, cols]
+    key_cache: np.ndarray         # raw bits, every token < context_lens[b] present
+    value_cache: np.ndarray
+    q: np.ndarray                 # raw bits [sum chunk, Hq, D]
+
+    def as_f32(self, bits):
+        return bits.view(np.float32) if self.dtype == "f32" else ref.bf16_bits_to_f32(bits)
+
+
+def make_prefill_case(seed, cached, chunk, dtype="bf16", num_heads=16, num_kv_heads=8, head_dim=128,
+                      block_size=16, num_blocks=None, cols=None) -> PrefillCase:
+    """Sequences with ``cached[b]`` tokens in the pool whose next ``chunk[b]`` tokens (also already
+    appended, as the engine does before attention) are the packed queries."""
+    rng = np.random.default_rng(seed)
+    cached = np.asarray(cached, np.int64)
+    chunk = np.asarray(chunk, np.int64)
+    ctx = cached + chunk
+    lens_blocks = [int(-(-c // block_size)) for c in ctx]
+    if num_blocks is None:
+        num_blocks = sum(lens_blocks) + 8
+    tables = disjoint_block_tables(rng, lens_blocks, num_blocks, cols)
+    x = 16 // (4 if dtype == "f32" else 2)
+    sentinel = F32_SENTINEL if dtype == "f32" else BF16_SENTINEL
+    kc = np.full((num_blocks, num_kv_heads, head_dim // x, block_size, x), sentinel)
+    vc = np.full((num_blocks, num_kv_heads, head_dim, block_size), sentinel)
+    for i, n in enumerate(ctx):
+        n = int(n)
+        k = _to_bits(rng.standard_normal((n, num_kv_heads, head_dim), dtype=np.float32), dtype)
+        v = _to_bits(rng.standard_normal((n, num_kv_heads, head_dim), dtype=np.float32), dtype)
+        pos = np.arange(n)
+        slots = tables[i, pos // block_size].astype(np.int64) * block_size + pos % block_size
+        ref.reshape_and_cache(k, v, kc, vc, slots, block_size)
+    total = int(chunk.sum())
+    q = _to_bits(rng.standard_normal((total, num_heads, head_dim), dtype=np.float32), dtype)
+    cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.uint32)
+    return PrefillCase(dtype, num_heads, num_kv_heads, head_dim, block_size, ctx.astype(np.uint32), cu,
+                       tables, kc, vc, q)
+
+
+def oracle_prefill(case: PrefillCase, scale=None, softcap=1.0, use_double=True):
+    kf = np.ascontiguousarray(case.as_f32(case.key_cache))
+    vf = np.ascontiguousarray(case.as_f32(case.value_cache))
+    qf = np.ascontiguousarray(case.as_f32(case.q))
+    scale = scale if scale is not None else case.head_dim ** -0.5
+    return ref.prefill_varlen(qf, kf, vf, np.ascontiguousarray(case.block_tables),
+                              np.ascontiguousarray(case.context_lens), case.cu_q, scale, softcap,
+                              use_double=use_double)
+
+
+def config3_rounds(seed=0, n=32, lo=100, hi=800, chunk=256):
+    """Config 3: prompt lengths ~U[lo, hi]; round r prefills tokens [256 r, 256 r + 256) of each."""
+    lens = uniform_lens(seed, n, lo, hi)
+    rounds = []
+    r = 0
+    while True:
+        start = r * chunk
+        active = [i for i in range(n) if lens[i] > start]
+        if not active:
+            break
+        rounds.append([(i, start, int(min(chunk, lens[i] - start))) for i in active])
+        r += 1
+    return lens, rounds

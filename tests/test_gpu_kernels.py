@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import paged_ref as ref
-from cases import (CONFIG1_CACHED, config1_case, loguniform_lens, make_decode_case, oracle_decode,
+from cases import (CONFIG1_CACHED, appended, config1_case, loguniform_lens, make_decode_case, oracle_decode,
                    uniform_lens)
 from vasr_paged_attn import _lib
 from vasr_paged_attn import mistralrs_paged_attn as pa
@@ -170,8 +170,8 @@ def test_decode_ragged_contexts(cuda_device, dtype, block_size):
 
 @pytest.mark.parametrize("gqa", [1, 2, 4])
 def test_decode_gqa_groups(cuda_device, gqa):
-    case = make_decode_case(5, [33, 300, 999], dtype="bf16", num_heads=8 * gqa, num_kv_heads=8,
-                            num_blocks=128)
+    case = appended(make_decode_case(5, [33, 300, 999], dtype="bf16", num_heads=8 * gqa, num_kv_heads=8,
+                            num_blocks=128))
     t = upload(case, cuda_device)
     out = run_decode(case, t)
     exp, _, _ = oracle_decode(case, after_append=False)
@@ -192,7 +192,7 @@ def test_decode_config2_shapes_bf16(cuda_device):
 
 def test_decode_graph_bucket_upper_bound_and_padded_tables(cuda_device):
     """max_context_len is only a bound (cuda_graph.rs:141); tables padded by repeating the last block."""
-    case = make_decode_case(6, [150, 20, 900], dtype="bf16", num_blocks=128, cols=128)
+    case = appended(make_decode_case(6, [150, 20, 900], dtype="bf16", num_blocks=128, cols=128))
     for i, n in enumerate(case.context_lens):
         nblk = -(-int(n) // 16)
         case.block_tables[i, nblk:] = case.block_tables[i, nblk - 1]
@@ -223,7 +223,7 @@ def test_decode_dummy_rows_use_null_block(cuda_device):
 
 
 def test_decode_softcap(cuda_device):
-    case = make_decode_case(12, [77, 513], dtype="f32", num_blocks=64)
+    case = appended(make_decode_case(12, [77, 513], dtype="f32", num_blocks=64))
     t = upload(case, cuda_device)
     out = run_decode(case, t, softcap=5.0)
     exp, _, _ = oracle_decode(case, softcap=5.0, after_append=False)
@@ -231,7 +231,7 @@ def test_decode_softcap(cuda_device):
 
 
 def test_decode_zero_context_rows_are_zero(cuda_device):
-    case = make_decode_case(13, [10, 20], dtype="f32", num_blocks=16)
+    case = appended(make_decode_case(13, [10, 20], dtype="f32", num_blocks=16))
     t = upload(case, cuda_device)
     t["ctx"][1] = 0
     out = to_f32(run_decode(case, t, max_context_len=64))
@@ -242,7 +242,7 @@ def test_decode_zero_context_rows_are_zero(cuda_device):
 def test_decode_repeatable_and_workspace_reuse(cuda_device):
     """Split-K counters reset themselves: repeated calls are bit-identical."""
     lens = loguniform_lens(1, 48, 64, 4096) - 1
-    case = make_decode_case(1, lens, dtype="bf16", num_blocks=int(sum(lens) // 16 + 64))
+    case = appended(make_decode_case(1, lens, dtype="bf16", num_blocks=int(sum(lens) // 16 + 64)))
     t = upload(case, cuda_device)
     outs = [to_bits(run_decode(case, t)) for _ in range(3)]
     assert all(np.array_equal(outs[0], o) for o in outs[1:])
@@ -342,7 +342,7 @@ def test_swap_blocks_device_host_roundtrip(cuda_device):
     pa.swap_blocks(host_cache, back, in_map)  # restore: pinned host -> device
     torch.cuda.synchronize()
     for s_ in src:
-        assert torch.equal(back[int(s_)], dev_cache[int(s_)])
+        assert np.array_equal(to_bits(back[int(s_)]), to_bits(dev_cache[int(s_)]))
 
 
 def test_swap_rejects_pageable_host_memory(cuda_device):
