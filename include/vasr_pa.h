@@ -56,7 +56,8 @@ typedef enum vasr_pa_status {
   VASR_PA_ENOT_SUPPORTED = -6,   /* head_dim / GQA group not instantiated  */
   VASR_PA_ELAUNCH = -7,          /* cudaLaunchKernel reported an error     */
   VASR_PA_EDEVICE = -8,          /* no usable sm_100 device current        */
-  VASR_PA_EINVAL_POINTER = -9    /* NULL or host-only pointer              */
+  VASR_PA_EINVAL_POINTER = -9,   /* NULL or host-only pointer              */
+  VASR_PA_ESCRATCH_LIMIT = -10   /* sizes exceed the fixed no-alloc scratch */
 } vasr_pa_status;
 
 /* Device error word bits (set by kernels, read with vasr_pa_get_device_error). */
@@ -140,6 +141,38 @@ int32_t vasr_pa_paged_attention(void *out, const void *query,
                                 int32_t dtype, void *workspace,
                                 size_t workspace_bytes,
                                 vasr_pa_stream_t stream);
+
+/*
+ * Decode attention for callers that cannot allocate device memory.
+ * No counterpart in the reference: it is an addition of this library.
+ *
+ * Same arguments and results as vasr_pa_paged_attention minus the workspace.
+ * The split-K scratch is a fixed buffer inside the library (a file-scope
+ * device array of vasr_pa_noalloc_scratch_bytes() = 16 MiB that every GPU
+ * loading the library keeps until exit), so a caller whose device memory is
+ * owned by someone else — a plugin enqueue path that must not allocate, a
+ * fixed-budget host framework, a real-time thread that must not block in the
+ * allocator — passes only inputs and outputs. Sizes whose workspace
+ * (vasr_pa_paged_attention_workspace_size) exceeds the buffer return
+ * VASR_PA_ESCRATCH_LIMIT. The first call on a device looks up the buffer's
+ * device address; make that first call before any stream capture. All calls
+ * on a device share the buffer: calls that overlap on the GPU race.
+ */
+int32_t vasr_pa_paged_attention_noalloc(void *out, const void *query,
+                                        const void *key_cache,
+                                        const void *value_cache,
+                                        const uint32_t *block_tables,
+                                        const uint32_t *context_lens,
+                                        int32_t num_seqs, int32_t num_heads,
+                                        int32_t num_kv_heads, int32_t head_dim,
+                                        int32_t block_size, int64_t num_blocks,
+                                        int32_t max_num_blocks_per_seq,
+                                        int32_t max_context_len, float scale,
+                                        float softcapping, int64_t q_seq_stride,
+                                        int32_t dtype, vasr_pa_stream_t stream);
+
+/* Size in bytes of the fixed scratch used by vasr_pa_paged_attention_noalloc. */
+size_t vasr_pa_noalloc_scratch_bytes(void);
 
 /*
  * Gather the first kv_len tokens of each sequence out of the pages into

@@ -60,6 +60,8 @@ const char *vasr_pa_status_string(int32_t status) {
     case VASR_PA_ELAUNCH: return "CUDA launch failed";
     case VASR_PA_EDEVICE: return "no usable CUDA device";
     case VASR_PA_EINVAL_POINTER: return "null or inaccessible pointer";
+    case VASR_PA_ESCRATCH_LIMIT:
+      return "sizes need more split-K scratch than the fixed 16 MiB no-alloc buffer holds";
     default: return "unknown status";
   }
 }

@@ -26,6 +26,7 @@ ENOT_SUPPORTED = -6
 ELAUNCH = -7
 EDEVICE = -8
 EINVAL_POINTER = -9
+ESCRATCH_LIMIT = -10
 # device error bits
 DERR_SLOT_RANGE = 0x1
 DERR_BLOCK_RANGE = 0x2
@@ -73,6 +74,12 @@ SIGNATURES: dict[str, tuple] = {
         _i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p]
     ),
     "vasr_pa_get_device_error": (_i32, [ctypes.POINTER(_i32), _i32, _c_void_p]),
+    "vasr_pa_paged_attention_noalloc": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32,
+         _i32, _i32, _i64, _i32, _i32, _f32, _f32, _i64, _i32, _c_void_p],
+    ),
+    "vasr_pa_noalloc_scratch_bytes": (_size, []),
 }
 
 
