@@ -246,6 +246,29 @@ int32_t vasr_pa_swap_blocks(void *dst, const void *src,
                             int64_t block_bytes, vasr_pa_stream_t stream);
 
 /*
+ * Fused pre-attention step of one decoder layer: per-head q/k RMSNorm, rotary
+ * embedding of q and k, and the KV append. Replaces the chain at
+ * vasr-models/src/model/thinker_text.rs:1041-1109 (q_norm, k_norm,
+ * apply_multimodal_rotary_pos_emb — 1-D RoPE when the three mRoPE position
+ * streams are equal, as for text and audio tokens — then reshape_and_cache).
+ * qkv is the fused projection output [num_tokens, (Hq + 2 Hkv) * D] with
+ * token stride qkv_token_stride (elements): q heads, then k heads, then v
+ * heads. Writes q_out [num_tokens, Hq, D] (normed + rotated) and appends the
+ * normed + rotated k and the raw v at slot_mapping[t] (negative = skip).
+ * cos_table / sin_table are f32 [max_position, D / 2]; positions i64 [T].
+ * RMSNorm: x * rsqrt(mean(x^2) + eps) * w in f32, rounded to the element
+ * type; RoPE in f32 on the rounded values, rounded again. bf16/f16, D = 128.
+ */
+int32_t vasr_pa_fused_qk_norm_rope_append(
+    void *q_out, const void *qkv, int64_t qkv_token_stride,
+    const void *q_norm_weight, const void *k_norm_weight, float eps,
+    const float *cos_table, const float *sin_table, int64_t max_position,
+    const int64_t *positions, void *key_cache, void *value_cache,
+    const int64_t *slot_mapping, int64_t num_tokens, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int64_t num_blocks, int32_t dtype, vasr_pa_stream_t stream);
+
+/*
  * Read (and optionally clear) the device error word of the current device.
  * Synchronises `stream` because it copies the word to the host; call it
  * outside stream capture.

@@ -651,6 +651,29 @@ def max_threads() -> int:
     return int(c_oracle().oracle_max_threads())
 
 
+# ============================== fused q/k RMSNorm + RoPE (thinker_text.rs:1041-1068)
+def qk_norm_rope_ref(qkv_bits, q_w_bits, k_w_bits, eps, cos, sin, positions, num_heads, num_kv_heads,
+                     head_dim=128):
+    """bf16 restatement of per-head RMSNorm (x * rsqrt(mean(x^2) + eps) * w in f32, rounded)
+    followed by rotate-half RoPE in f32 on the rounded values (rounded again).
+    Returns (q_bits [T, Hq, D], k_bits [T, Hkv, D], v_bits [T, Hkv, D])."""
+    t = qkv_bits.shape[0]
+    x = bf16_bits_to_f32(qkv_bits).reshape(t, num_heads + 2 * num_kv_heads, head_dim)
+    qk = x[:, :num_heads + num_kv_heads].astype(np.float64)
+    w = np.concatenate([np.broadcast_to(bf16_bits_to_f32(q_w_bits), (num_heads, head_dim)),
+                        np.broadcast_to(bf16_bits_to_f32(k_w_bits), (num_kv_heads, head_dim))])
+    inv = 1.0 / np.sqrt((qk ** 2).mean(-1, keepdims=True) + eps)
+    n = bf16_bits_to_f32(f32_to_bf16_bits((qk * inv * w).astype(np.float32))).astype(np.float64)
+    half = head_dim // 2
+    c = cos[positions][:, None, :].astype(np.float64)
+    s = sin[positions][:, None, :].astype(np.float64)
+    x1, x2 = n[..., :half], n[..., half:]
+    r = np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1).astype(np.float32)
+    rb = f32_to_bf16_bits(r)
+    v_bits = qkv_bits.reshape(t, num_heads + 2 * num_kv_heads, head_dim)[:, num_heads + num_kv_heads:]
+    return rb[:, :num_heads], rb[:, num_heads:], np.ascontiguousarray(v_bits)
+
+
 # ------------------------------------------------------------ bf16 helpers
 def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
     return (bits.astype(np.uint32) << 16).view(np.float32)

@@ -234,14 +234,44 @@ int32_t vasr_pa_swap_blocks(void *dst, const void *src, const int64_t *block_map
                                   dst_num_blocks, block_bytes, to_stream(stream));
 }
 
+int32_t vasr_pa_fused_qk_norm_rope_append(
+    void *q_out, const void *qkv, int64_t qkv_token_stride, const void *q_norm_weight,
+    const void *k_norm_weight, float eps, const float *cos_table, const float *sin_table,
+    int64_t max_position, const int64_t *positions, void *key_cache, void *value_cache,
+    const int64_t *slot_mapping, int64_t num_tokens, int32_t num_heads, int32_t num_kv_heads,
+    int32_t head_dim, int32_t block_size, int64_t num_blocks, int32_t dtype,
+    vasr_pa_stream_t stream) {
+  const int g = check_geometry(dtype, num_kv_heads, head_dim, block_size, num_blocks);
+  if (g != VASR_PA_OK) return g;
+  if (dtype == VASR_PA_F32 || head_dim != 128) return VASR_PA_ENOT_SUPPORTED;
+  if (num_tokens < 0 || num_heads <= 0 || max_position <= 0) return VASR_PA_EINVAL_SHAPE;
+  if (num_tokens == 0) return VASR_PA_OK;
+  if (qkv_token_stride < (int64_t)(num_heads + 2 * num_kv_heads) * head_dim)
+    return VASR_PA_EINVAL_SHAPE;
+  if (!q_out || !qkv || !q_norm_weight || !k_norm_weight || !cos_table || !sin_table ||
+      !positions || !key_cache || !value_cache || !slot_mapping)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned(qkv, 4) || (qkv_token_stride % 2) != 0 || !aligned(q_out, 4) ||
+      !aligned(q_norm_weight, 4) || !aligned(k_norm_weight, 4) || !aligned(cos_table, 8) ||
+      !aligned(sin_table, 8) || !aligned(positions, 8) || !aligned(slot_mapping, 8) ||
+      !aligned16(key_cache) || !aligned16(value_cache))
+    return VASR_PA_EINVAL_ALIGN;
+  vasr::FusedRopeArgs a{q_out, qkv, qkv_token_stride, q_norm_weight, k_norm_weight, eps,
+                        cos_table, sin_table, max_position, positions, key_cache, value_cache,
+                        slot_mapping, num_tokens, num_heads, num_kv_heads, head_dim, block_size,
+                        num_blocks, dtype};
+  return vasr::launch_fused_rope(a, to_stream(stream));
+}
+
 int32_t vasr_pa_get_device_error(int32_t *out_bits, int32_t clear, vasr_pa_stream_t stream) {
   if (!out_bits) return VASR_PA_EINVAL_POINTER;
-  uint32_t a = 0, b = 0, c = 0;
+  uint32_t a = 0, b = 0, c = 0, d = 0;
   int r;
   if ((r = vasr::read_error_kv_ops(&a, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
   if ((r = vasr::read_error_decode(&b, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
   if ((r = vasr::read_error_prefill(&c, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
-  *out_bits = (int32_t)(a | b | c);
+  if ((r = vasr::read_error_fused(&d, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
+  *out_bits = (int32_t)(a | b | c | d);
   return VASR_PA_OK;
 }
 

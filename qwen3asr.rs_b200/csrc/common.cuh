@@ -1,7 +1,7 @@
 // common.cuh — shared device helpers for the sm_100a paged KV-cache kernels.
 //
 // Element types, 16-byte vector access, bf16 <-> f32 unpacking, the device
-// error word, and the mbarrier + cp.async.bulk (non-multicast, CTA-local)
+// error word, and the mbarrier + cp.async.bulk (CTA-local destination)
 // primitives used to stage whole cache pages in shared memory.
 #pragma once
 
@@ -136,7 +136,8 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
-// Non-multicast; src and dst 16-byte aligned, bytes a multiple of 16.
+// Destination is this CTA only; src and dst 16-byte aligned, bytes a
+// multiple of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void *src, uint32_t bytes,
                                          uint32_t bar) {
   asm volatile(

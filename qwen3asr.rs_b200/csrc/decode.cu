@@ -1,5 +1,5 @@
 // decode.cu — launchers and instantiations of the paged decode kernel.
-#include "decode.cuh"
+#include "decode_g2.cuh"
 #include "launch.h"
 
 namespace vasr {
@@ -65,8 +65,57 @@ int launch_decode_t(const DecodeArgs &a, cudaStream_t stream) {
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
+// GQA group 2 (Qwen3-ASR) runs the specialised kernel of decode_g2.cuh.
+template <typename T, int BS, int D>
+int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
+  constexpr int kStageBytes = 2 * ((16 > BS) ? 16 / BS : 1) * D * BS * (int)sizeof(T);
+  constexpr int kNST = kStageBytes <= 8192 ? 8 : 4;
+  constexpr int kMinBlocks = 3;
+  using C = DecodeG2Cfg<T, BS, D, kNST>;
+  const DecodeWorkspace w = decode_workspace_layout(a.num_seqs, a.num_heads, a.num_kv_heads,
+                                                    a.head_dim, a.block_size, a.max_context_len);
+  if ((size_t)a.num_seqs * a.num_kv_heads > kDecodeMaxCounters) return VASR_PA_ENOT_SUPPORTED;
+  if (a.workspace == nullptr || a.workspace_bytes < w.total) return VASR_PA_EINVAL_WORKSPACE;
+  if (w.pages_per_split > C::kMaxPagesPerSplit) return VASR_PA_ENOT_SUPPORTED;
+  DecodeParams p;
+  p.out = a.out;
+  p.q = a.query;
+  p.k_cache = a.key_cache;
+  p.v_cache = a.value_cache;
+  p.block_tables = a.block_tables;
+  p.context_lens = a.context_lens;
+  unsigned char *ws = static_cast<unsigned char *>(a.workspace);
+  p.ws_o = reinterpret_cast<float *>(ws + w.off_o);
+  p.ws_ml = reinterpret_cast<float2 *>(ws + w.off_ml);
+  p.counters = reinterpret_cast<uint32_t *>(ws + w.off_counters);
+  p.q_seq_stride = a.q_seq_stride;
+  p.num_blocks = a.num_blocks;
+  p.num_seqs = a.num_seqs;
+  p.num_heads = a.num_heads;
+  p.num_kv_heads = a.num_kv_heads;
+  p.cols = a.max_num_blocks_per_seq;
+  p.pages_per_split = w.pages_per_split;
+  p.max_splits = w.max_splits;
+  p.scale = a.scale;
+  p.softcap = a.softcapping;
+  auto kern = paged_decode_g2_kernel<T, BS, D, kNST, kMinBlocks>;
+  static std::atomic<uint64_t> attr_done{0};
+  if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
+  dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
 template <typename T, int D, int G>
 int dispatch_bs(const DecodeArgs &a, cudaStream_t s) {
+  if constexpr (G == 2) {
+    switch (a.block_size) {
+      case 8: return launch_decode_g2<T, 8, D>(a, s);
+      case 16: return launch_decode_g2<T, 16, D>(a, s);
+      case 32: return launch_decode_g2<T, 32, D>(a, s);
+      default: return VASR_PA_EINVAL_BLOCKSIZE;
+    }
+  }
   switch (a.block_size) {
     case 8: return launch_decode_t<T, 8, D, G>(a, s);
     case 16: return launch_decode_t<T, 16, D, G>(a, s);

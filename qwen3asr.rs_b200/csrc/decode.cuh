@@ -11,7 +11,7 @@
 //   A CTA owns one (sequence, kv head, split of P tokens). It computes all
 //   G = num_heads / num_kv_heads query heads of the group, so every K/V byte
 //   leaves HBM exactly once. Pages of the split are staged in shared memory
-//   by 1-D bulk copies (cp.async.bulk, CTA-local, no multicast) into NST
+//   by 1-D bulk copies (cp.async.bulk, CTA-local destination) into NST
 //   stages; stage s belongs to warp s % 4, which waits on the stage's
 //   mbarrier, consumes it and immediately refills it with the page NST
 //   stages ahead. Each warp keeps an online-softmax state; the 4 warp states
@@ -394,17 +394,20 @@ __global__ void __launch_bounds__(128, 2) paged_decode_kernel(const DecodeParams
   }
   if (single) return;
 
-  // ---- split-K: the last CTA of this (sequence, kv head) merges partials
-  __threadfence();
+  // ---- split-K: the last CTA of this (sequence, kv head) merges partials.
+  // The barrier orders every thread's partial stores before thread 0's
+  // device-scope fence and arrival; the last arriver fences again before the
+  // CTA reads the other splits' partials through L2.
   __syncthreads();
   uint32_t *flag = reinterpret_cast<uint32_t *>(smem + C::kOffFlag);
   if (tid == 0) {
+    __threadfence();
     const uint32_t prev = atomicAdd(p.counters + bk, 1u);
+    __threadfence();
     flag[0] = (prev == (uint32_t)(n_splits - 1)) ? 1u : 0u;
   }
   __syncthreads();
   if (flag[0] == 0u) return;
-  __threadfence();
 #pragma unroll
   for (int e0 = 0; e0 < G * D; e0 += C::kThreads) {
     const int e = e0 + tid;

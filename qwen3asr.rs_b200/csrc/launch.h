@@ -90,6 +90,31 @@ struct PrefillArgs {
   int dtype;
 };
 
+struct FusedRopeArgs {
+  void *q_out;
+  const void *qkv;
+  int64_t qkv_token_stride;
+  const void *q_norm_weight;
+  const void *k_norm_weight;
+  float eps;
+  const float *cos_table;
+  const float *sin_table;
+  int64_t max_position;
+  const int64_t *positions;
+  void *key_cache;
+  void *value_cache;
+  const int64_t *slot_mapping;
+  int64_t num_tokens;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  int64_t num_blocks;
+  int dtype;
+};
+int launch_fused_rope(const FusedRopeArgs &a, cudaStream_t s);
+int read_error_fused(uint32_t *bits, bool clear, cudaStream_t s);
+
 // Workspace layout of the decode kernel (all offsets 256-byte aligned):
 // [counters: kDecodeMaxCounters x u32][partial o][partial (m, l)].
 constexpr size_t kDecodeMaxCounters = 65536;  // num_seqs * num_kv_heads limit

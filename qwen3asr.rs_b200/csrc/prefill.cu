@@ -12,7 +12,7 @@
 // FlashAttention-2 style. A CTA owns 64 rows = (64 / G) query positions x
 // the G query heads of one kv head, so each K/V tile staged in shared memory
 // serves the whole GQA group. K pages [D/8][bs][8] and V pages [D][bs] are
-// copied verbatim by 1-D bulk copies (no multicast) and both feed ldmatrix
+// copied verbatim by 1-D CTA-local bulk copies and both feed ldmatrix
 // directly: a K page row (8 dims of one token) and a V page row (8 tokens
 // of one dim) are each one 16-byte ldmatrix row.
 // f32: CUDA-core kernel, one CTA per (query row, kv head), online softmax.

@@ -80,6 +80,12 @@ SIGNATURES: dict[str, tuple] = {
          _i32, _i32, _i64, _i32, _i32, _f32, _f32, _i64, _i32, _c_void_p],
     ),
     "vasr_pa_noalloc_scratch_bytes": (_size, []),
+    "vasr_pa_fused_qk_norm_rope_append": (
+        _i32,
+        [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _f32, _c_void_p, _c_void_p, _i64,
+         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _i64, _i32,
+         _c_void_p],
+    ),
 }
 
 

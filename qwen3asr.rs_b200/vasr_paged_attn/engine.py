@@ -29,6 +29,7 @@ from typing import Optional
 import torch
 import torch.nn.functional as F
 
+from . import fused as fused_ops
 from . import mistralrs_paged_attn as pa
 
 
@@ -114,26 +115,37 @@ class RandomQwen3Decoder:
     def decode_step(self, input_ids: torch.Tensor, positions: torch.Tensor, kv_caches,
                     slot_mapping: torch.Tensor, block_tables: torch.Tensor,
                     context_lens: torch.Tensor, max_context_len: int,
-                    next_ids_out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """One token per sequence through all layers; returns greedy next ids [B] (int64)."""
+                    next_ids_out: Optional[torch.Tensor] = None, fused: bool = True) -> torch.Tensor:
+        """One token per sequence through all layers; returns greedy next ids [B] (int64).
+
+        ``fused`` runs q/k RMSNorm + RoPE + KV append as one kernel
+        (vasr_pa_fused_qk_norm_rope_append); ``fused=False`` runs the same math
+        as separate torch ops followed by reshape_and_cache.
+        """
         cfg = self.cfg
         b = input_ids.shape[0]
         hq, hkv, d = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
         x = F.embedding(input_ids, self.embed)
-        cos = self.rope_cos.index_select(0, positions)
-        sin = self.rope_sin.index_select(0, positions)
+        if not fused:
+            cos = self.rope_cos.index_select(0, positions)
+            sin = self.rope_sin.index_select(0, positions)
         scale = d ** -0.5
         for l, (kc, vc) in zip(self.layers, kv_caches):
             h = F.rms_norm(x, (cfg.hidden_size,), l["in_norm"], cfg.rms_norm_eps)
             qkv = h @ l["w_qkv"].t()
-            q = qkv[:, : hq * d].view(b, hq, d)
-            k = qkv[:, hq * d:(hq + hkv) * d].view(b, hkv, d)
-            v = qkv[:, (hq + hkv) * d:].view(b, hkv, d)
-            q = F.rms_norm(q, (d,), l["q_norm"], cfg.rms_norm_eps)
-            k = F.rms_norm(k, (d,), l["k_norm"], cfg.rms_norm_eps)
-            q = self._rope(q, cos, sin)
-            k = self._rope(k, cos, sin)
-            pa.reshape_and_cache(k, v, None, None, kc, vc, slot_mapping)
+            if fused:
+                q = fused_ops.qk_norm_rope_append(qkv, l["q_norm"], l["k_norm"], cfg.rms_norm_eps,
+                                                  self.rope_cos, self.rope_sin, positions, kc, vc,
+                                                  slot_mapping, hq)
+            else:
+                q = qkv[:, : hq * d].view(b, hq, d)
+                k = qkv[:, hq * d:(hq + hkv) * d].view(b, hkv, d)
+                v = qkv[:, (hq + hkv) * d:].view(b, hkv, d)
+                q = F.rms_norm(q, (d,), l["q_norm"], cfg.rms_norm_eps)
+                k = F.rms_norm(k, (d,), l["k_norm"], cfg.rms_norm_eps)
+                q = self._rope(q, cos, sin)
+                k = self._rope(k, cos, sin)
+                pa.reshape_and_cache(k, v, None, None, kc, vc, slot_mapping)
             attn = pa.paged_attention(q, None, None, kc, vc, block_tables, context_lens, None,
                                       max_context_len, scale, 1.0, None)
             x = x + attn.view(b, hq * d) @ l["w_o"].t()
