@@ -1,6 +1,19 @@
-// decode.cu — launchers and instantiations of the paged decode kernel.
+// decode.cu — launchers and instantiations of the paged decode kernels.
+//
+// GQA group 2 (Qwen3-ASR: 16 query / 8 kv heads) runs paged_decode_g2_kernel
+// (decode_g2.cuh); groups 1 and 4 run the generic paged_decode_kernel
+// (decode.cuh). Both use the same split-K workspace layout.
 #include "decode_g2.cuh"
 #include "launch.h"
+
+// Launch-shape constants of the GQA-2 kernel (stages per CTA and resident
+// CTAs per SM); chosen by measurement on B200, see the design notes.
+#ifndef VASR_G2_NST
+#define VASR_G2_NST 8
+#endif
+#ifndef VASR_G2_MINB
+#define VASR_G2_MINB 3
+#endif
 
 namespace vasr {
 
@@ -28,14 +41,7 @@ DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_
 
 namespace {
 
-template <typename T, int BS, int D, int G>
-int launch_decode_t(const DecodeArgs &a, cudaStream_t stream) {
-  using C = DecodeCfg<T, BS, D, G>;
-  const DecodeWorkspace w = decode_workspace_layout(a.num_seqs, a.num_heads, a.num_kv_heads,
-                                                    a.head_dim, a.block_size, a.max_context_len);
-  if ((size_t)a.num_seqs * a.num_kv_heads > kDecodeMaxCounters) return VASR_PA_ENOT_SUPPORTED;
-  if (a.workspace == nullptr || a.workspace_bytes < w.total) return VASR_PA_EINVAL_WORKSPACE;
-  if (w.pages_per_split > C::kMaxPagesPerSplit) return VASR_PA_ENOT_SUPPORTED;
+DecodeParams make_decode_params(const DecodeArgs &a, const DecodeWorkspace &w) {
   DecodeParams p;
   p.out = a.out;
   p.q = a.query;
@@ -57,6 +63,28 @@ int launch_decode_t(const DecodeArgs &a, cudaStream_t stream) {
   p.max_splits = w.max_splits;
   p.scale = a.scale;
   p.softcap = a.softcapping;
+  return p;
+}
+
+// Host-side checks shared by both kernels; returns the workspace layout.
+int check_workspace(const DecodeArgs &a, int max_pages_per_split, DecodeWorkspace *w) {
+  *w = decode_workspace_layout(a.num_seqs, a.num_heads, a.num_kv_heads, a.head_dim,
+                               a.block_size, a.max_context_len);
+  if ((size_t)a.num_seqs * a.num_kv_heads > kDecodeMaxCounters) return VASR_PA_ENOT_SUPPORTED;
+  if (a.workspace == nullptr || a.workspace_bytes < w->total) return VASR_PA_EINVAL_WORKSPACE;
+  if (w->pages_per_split > max_pages_per_split) return VASR_PA_ENOT_SUPPORTED;
+  return VASR_PA_OK;
+}
+
+// grid = (split, kv head, sequence): the splits of one (sequence, kv head)
+// are adjacent, so its partials are merged soon after they are written.
+template <typename T, int BS, int D, int G>
+int launch_decode_generic(const DecodeArgs &a, cudaStream_t stream) {
+  using C = DecodeCfg<T, BS, D, G>;
+  DecodeWorkspace w;
+  const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
+  if (st != VASR_PA_OK) return st;
+  const DecodeParams p = make_decode_params(a, w);
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(paged_decode_kernel<T, BS, D, G>, C::kSmemBytes, attr_done))
     return VASR_PA_ELAUNCH;
@@ -65,40 +93,16 @@ int launch_decode_t(const DecodeArgs &a, cudaStream_t stream) {
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
-// GQA group 2 (Qwen3-ASR) runs the specialised kernel of decode_g2.cuh.
 template <typename T, int BS, int D>
 int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
   constexpr int kStageBytes = 2 * ((16 > BS) ? 16 / BS : 1) * D * BS * (int)sizeof(T);
-  constexpr int kNST = kStageBytes <= 8192 ? 8 : 4;
-  constexpr int kMinBlocks = 3;
+  constexpr int kNST = kStageBytes <= 8192 ? VASR_G2_NST : 4;
   using C = DecodeG2Cfg<T, BS, D, kNST>;
-  const DecodeWorkspace w = decode_workspace_layout(a.num_seqs, a.num_heads, a.num_kv_heads,
-                                                    a.head_dim, a.block_size, a.max_context_len);
-  if ((size_t)a.num_seqs * a.num_kv_heads > kDecodeMaxCounters) return VASR_PA_ENOT_SUPPORTED;
-  if (a.workspace == nullptr || a.workspace_bytes < w.total) return VASR_PA_EINVAL_WORKSPACE;
-  if (w.pages_per_split > C::kMaxPagesPerSplit) return VASR_PA_ENOT_SUPPORTED;
-  DecodeParams p;
-  p.out = a.out;
-  p.q = a.query;
-  p.k_cache = a.key_cache;
-  p.v_cache = a.value_cache;
-  p.block_tables = a.block_tables;
-  p.context_lens = a.context_lens;
-  unsigned char *ws = static_cast<unsigned char *>(a.workspace);
-  p.ws_o = reinterpret_cast<float *>(ws + w.off_o);
-  p.ws_ml = reinterpret_cast<float2 *>(ws + w.off_ml);
-  p.counters = reinterpret_cast<uint32_t *>(ws + w.off_counters);
-  p.q_seq_stride = a.q_seq_stride;
-  p.num_blocks = a.num_blocks;
-  p.num_seqs = a.num_seqs;
-  p.num_heads = a.num_heads;
-  p.num_kv_heads = a.num_kv_heads;
-  p.cols = a.max_num_blocks_per_seq;
-  p.pages_per_split = w.pages_per_split;
-  p.max_splits = w.max_splits;
-  p.scale = a.scale;
-  p.softcap = a.softcapping;
-  auto kern = paged_decode_g2_kernel<T, BS, D, kNST, kMinBlocks>;
+  DecodeWorkspace w;
+  const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
+  if (st != VASR_PA_OK) return st;
+  const DecodeParams p = make_decode_params(a, w);
+  auto kern = paged_decode_g2_kernel<T, BS, D, kNST, VASR_G2_MINB>;
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
   dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
@@ -117,9 +121,9 @@ int dispatch_bs(const DecodeArgs &a, cudaStream_t s) {
     }
   }
   switch (a.block_size) {
-    case 8: return launch_decode_t<T, 8, D, G>(a, s);
-    case 16: return launch_decode_t<T, 16, D, G>(a, s);
-    case 32: return launch_decode_t<T, 32, D, G>(a, s);
+    case 8: return launch_decode_generic<T, 8, D, G>(a, s);
+    case 16: return launch_decode_generic<T, 16, D, G>(a, s);
+    case 32: return launch_decode_generic<T, 32, D, G>(a, s);
     default: return VASR_PA_EINVAL_BLOCKSIZE;
   }
 }

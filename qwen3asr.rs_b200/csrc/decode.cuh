@@ -431,12 +431,17 @@ __global__ void __launch_bounds__(128, 2) paged_decode_kernel(const DecodeParams
 }
 
 // Split size chosen from host-visible arguments only, so that the workspace
-// size and the launch always agree: 256 tokens per split, halved (down to 64)
-// while fewer than 2 CTAs per B200 SM would be launched.
+// size and the launch always agree: VASR_DECODE_SPLIT_TOKENS tokens per split,
+// halved (down to 64) while fewer than 2 CTAs per B200 SM would be launched.
+// 512 measured best on B200 for config 2 (46.8 us vs 50.7 us at 256, 47.6 at
+// 768, 49.8 at 1024): fewer CTA start-ups per byte, still ~2 waves of CTAs.
+#ifndef VASR_DECODE_SPLIT_TOKENS
+#define VASR_DECODE_SPLIT_TOKENS 512
+#endif
 inline int decode_pages_per_split(int num_seqs, int num_kv_heads, int block_size,
                                   int max_context_len) {
   const int kTargetCtas = 2 * 148;
-  int tokens = 256;
+  int tokens = VASR_DECODE_SPLIT_TOKENS;
   auto ctas = [&](int t) {
     return (int64_t)num_seqs * num_kv_heads * ((max_context_len + t - 1) / t);
   };

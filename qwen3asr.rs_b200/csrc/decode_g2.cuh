@@ -65,6 +65,13 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
   const int lane = tid & 31;
   const int P = p.pages_per_split * BS;
 
+  // The block ids of this split are loaded speculatively, in parallel with
+  // the context length (only in-row entries; those past the length are
+  // discarded below).
+  uint32_t spec_id = 0;
+  const int spec_col = split * p.pages_per_split + tid;
+  if (tid < p.pages_per_split && spec_col < p.cols)
+    spec_id = __ldg(p.block_tables + (int64_t)b * p.cols + spec_col);
   int ctx = (int)p.context_lens[b];
   const int cap_tables = p.cols * BS;
   const int cap_splits = p.max_splits * P;
@@ -82,7 +89,6 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
   if (split >= n_splits) return;
   const int tok_begin = split * P;
   const int tok_end = min(ctx, tok_begin + P);
-  const int page_begin = tok_begin / BS;
   const int n_pages = (tok_end - tok_begin + BS - 1) / BS;
   const int n_units = (n_pages + C::kSP - 1) / C::kSP;
 
@@ -91,7 +97,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
   float *p_s = reinterpret_cast<float *>(smem + C::kOffP);
 
   if (tid < n_pages) {
-    uint32_t id = p.block_tables[(int64_t)b * p.cols + page_begin + tid];
+    uint32_t id = spec_id;  // == block_tables[b * cols + tok_begin / BS + tid]
     if ((int64_t)id >= p.num_blocks) {
       raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
       id = 0;

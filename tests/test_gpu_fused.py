@@ -20,12 +20,14 @@ def bits(t):
 
 
 def ulp_close(a_bits, b_bits, min_exact=0.999):
-    """At least ``min_exact`` of the elements bit-identical, the rest within 4 bf16 ulps
-    (2^-5 relative) + 1e-5: rsqrtf can round a normalised value across a bf16 boundary, and
-    the rotation then spreads that one-ulp step over a few ulps of the output."""
+    """At least ``min_exact`` of the elements bit-identical; the rest within one bf16 ulp of
+    the output (2^-7 relative) plus 4e-3 absolute. rsqrtf can round a normalised value
+    (magnitude ~1, bf16 ulp ~4e-3) across a bf16 boundary; the rotation carries that step
+    into outputs that may be near-cancelled and small, so the bound is absolute at the
+    scale of the normalised inputs."""
     a = ref.bf16_bits_to_f32(a_bits)
     b = ref.bf16_bits_to_f32(b_bits)
-    ok = np.abs(a - b) <= np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -5 + 1e-5
+    ok = np.abs(a - b) <= np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -7 + 4e-3
     return bool(ok.all()) and (a_bits == b_bits).mean() >= min_exact
 
 

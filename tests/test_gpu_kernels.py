@@ -190,6 +190,29 @@ def test_decode_config2_shapes_bf16(cuda_device):
     assert err <= BF16_TOL, err
 
 
+def test_decode_more_than_1024_sequences(cuda_device):
+    """Above 1024 sequences the grid kernel (one CTA per split) runs instead of the persistent one."""
+    lens = uniform_lens(3, 1100, 1, 60) - 1
+    case = make_decode_case(3, lens, dtype="bf16", num_blocks=1100 * 4 + 8)
+    t = upload(case, cuda_device)
+    pa.reshape_and_cache(t["k"], t["v"], None, None, t["kc"], t["vc"], t["slots"])
+    out = run_decode(case, t, max_context_len=512)
+    exp, _, _ = oracle_decode(case)
+    assert np.abs(to_f32(out) - exp).max() <= BF16_TOL
+
+
+def test_decode_persistent_many_items_per_cta(cuda_device):
+    """Long bound with short true contexts: many (sequence, head, split) items per CTA."""
+    lens = loguniform_lens(4, 300, 1, 3000) - 1
+    case = make_decode_case(4, np.maximum(lens, 0), dtype="bf16",
+                            num_blocks=int(np.maximum(lens, 0).sum() // 16 + 320))
+    t = upload(case, cuda_device)
+    pa.reshape_and_cache(t["k"], t["v"], None, None, t["kc"], t["vc"], t["slots"])
+    out = run_decode(case, t, max_context_len=4096)
+    exp, _, _ = oracle_decode(case)
+    assert np.abs(to_f32(out) - exp).max() <= BF16_TOL
+
+
 def test_decode_graph_bucket_upper_bound_and_padded_tables(cuda_device):
     """max_context_len is only a bound (cuda_graph.rs:141); tables padded by repeating the last block."""
     case = appended(make_decode_case(6, [150, 20, 900], dtype="bf16", num_blocks=128, cols=128))
