@@ -9,12 +9,16 @@
 // (thinker_text.rs:1344-1365).
 //
 // bf16 / f16: tensor-core kernel (mma.sync m16n8k16, f32 accumulate),
-// FlashAttention-2 style. A CTA owns 64 rows = (64 / G) query positions x
-// the G query heads of one kv head, so each K/V tile staged in shared memory
-// serves the whole GQA group. K pages [D/8][bs][8] and V pages [D][bs] are
-// copied verbatim by 1-D CTA-local bulk copies and both feed ldmatrix
-// directly: a K page row (8 dims of one token) and a V page row (8 tokens
-// of one dim) are each one 16-byte ldmatrix row.
+// FlashAttention-2 style. A CTA of 8 warps owns 128 rows = (128 / G) query
+// positions x the G query heads of one kv head, so each K/V tile staged in
+// shared memory serves the whole GQA group and 128 rows. K pages
+// [D/8][bs][8] and V pages [D][bs] are copied verbatim by 1-D CTA-local bulk
+// copies into a 2-stage ring and both feed ldmatrix directly: a K page row
+// (8 dims of one token) and a V page row (8 tokens of one dim) are each one
+// 16-byte ldmatrix row. 64-key tiles are computed in two 32-key halves and
+// the query fragments are re-read from shared memory per k-step, which keeps
+// the kernel under 128 registers (2 CTAs = 16 warps per SM). Warps whose
+// rows the causal mask hides from a whole half-tile skip it.
 // f32: CUDA-core kernel, one CTA per (query row, kv head), online softmax.
 #include "common.cuh"
 #include "launch.h"
@@ -96,15 +100,16 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
 
 template <typename T, int BS, int D, int G>
 struct TcCfg {
-  static constexpr int kWarps = 4;
-  static constexpr int kThreads = 128;
+  static constexpr int kWarps = 8;
+  static constexpr int kThreads = 32 * kWarps;
   static constexpr int kRows = 16 * kWarps;       // rows (position x head) per CTA
   static constexpr int kPos = kRows / G;          // query positions per CTA
-  static constexpr int kBK = 64;                  // keys per tile
+  static constexpr int kBK = 64;                  // keys per staged tile
+  static constexpr int kHK = 32;                  // keys per compute half
   static constexpr int kPagesPerTile = (kBK + BS - 1) / BS;
   static constexpr int kPB = D * BS * 2;          // bytes of one page (2-byte elements)
   static constexpr int kTileBytes = kPagesPerTile * kPB;
-  static constexpr int kNST = 3;
+  static constexpr int kNST = 2;
   static constexpr int kQPitch = D * 2 + 16;      // padded Q row (conflict-free ldmatrix)
   static constexpr int kMaxIds = 512;             // block ids cached in shared memory
   static constexpr int kOffK = 0;
@@ -113,13 +118,13 @@ struct TcCfg {
   static constexpr int kOffIds = kOffQ + kRows * kQPitch;
   static constexpr int kOffBar = kOffIds + kMaxIds * 4;
   static constexpr int kSmemBytes = kOffBar + kNST * 8;
-  static_assert(kBK % BS == 0 || BS % kBK == 0, "tile/page mismatch");
-  static_assert(kBK >= BS, "a key tile holds at least one page");
+  static_assert(kBK % BS == 0, "tile/page mismatch");
+  static_assert(kHK % 16 == 0 && kBK % kHK == 0, "halves");
   static_assert(D % 16 == 0, "head_dim multiple of 16");
 };
 
 template <typename T, int BS, int D, int G>
-__global__ void __launch_bounds__(128) prefill_tc_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(256, 2) prefill_tc_kernel(const PrefillParams p) {
   using C = TcCfg<T, BS, D, G>;
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -168,7 +173,7 @@ __global__ void __launch_bounds__(128) prefill_tc_kernel(const PrefillParams p) 
   const uint32_t s_base = smem_addr(smem);
   uint32_t *ids = reinterpret_cast<uint32_t *>(smem + C::kOffIds);
   for (int i = tid; i < min(n_pages, C::kMaxIds); i += C::kThreads) {
-    uint32_t id = p.block_tables[(int64_t)b * p.cols + i];
+    uint32_t id = __ldg(p.block_tables + (int64_t)b * p.cols + i);
     if ((int64_t)id >= p.num_blocks) {
       raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
       id = 0;
@@ -215,140 +220,137 @@ __global__ void __launch_bounds__(128) prefill_tc_kernel(const PrefillParams p) 
   if (tid == 0)
     for (int kt = 0; kt < min(C::kNST, n_kt); ++kt) issue_tile(kt);
 
-  // ---- Q fragments (A operand) for this warp's 16 rows, all D/16 k-steps
   const int grp = lane >> 2, tig = lane & 3;
-  uint32_t qf[D / 16][4];
-  {
-    const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-    const int cofs = (lane >> 4) * 8;
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks)
-      ldmatrix_x4(s_base + C::kOffQ + r * C::kQPitch + (ks * 16 + cofs) * 2, qf[ks][0], qf[ks][1],
-                  qf[ks][2], qf[ks][3]);
-  }
+  // ldmatrix row address of this lane inside the warp's 16 Q rows
+  const uint32_t q_lane = s_base + C::kOffQ +
+                          (warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * C::kQPitch +
+                          (lane >> 4) * 16;
   // rows of this thread: r_lo = warp*16 + grp, r_hi = r_lo + 8
   const int r_lo = warp * 16 + grp, r_hi = r_lo + 8;
   const int pos_lo = base_pos + r_lo / G, pos_hi = base_pos + r_hi / G;
   const bool val_lo = (r_lo / G) < n_pos, val_hi = (r_hi / G) < n_pos;
+  // largest position among this warp's valid rows (-1: the warp has no valid row)
+  const int warp_pos_max =
+      (warp * 16) / G < n_pos ? base_pos + min((warp * 16 + 15) / G, n_pos - 1) : -1;
 
-  constexpr int kNT = C::kBK / 8;  // n-tiles of 8 keys
+  constexpr int kNT = C::kHK / 8;  // n-tiles of 8 keys per half
   constexpr int kDT = D / 8;       // n-tiles of 8 dims
   float o[kDT][4];
 #pragma unroll
   for (int j = 0; j < kDT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
   const bool use_softcap = (p.softcap != 1.0f) && (p.softcap > 0.f);
-  bool aborted = false;
 
   for (int kt = 0; kt < n_kt; ++kt) {
     const int s = kt % C::kNST;
-    if (!mbar_wait_bounded(s_base + C::kOffBar + s * 8, (uint32_t)((kt / C::kNST) & 1))) {
-      aborted = true;
-    }
+    mbar_wait_bounded(s_base + C::kOffBar + s * 8, (uint32_t)((kt / C::kNST) & 1));
     const int key0 = kt * C::kBK;
     const uint32_t sk = s_base + C::kOffK + s * C::kTileBytes;
     const uint32_t sv = s_base + C::kOffV + s * C::kTileBytes;
     // Partial tile: zero V for keys >= kv_end so masked keys (P = 0) cannot
     // bring stale or non-finite values into the P.V product.
     if (key0 + C::kBK > kv_end) {
-      unsigned char *vtile = smem + C::kOffV + s * C::kTileBytes;
+      uint16_t *vtile = reinterpret_cast<uint16_t *>(smem + C::kOffV + s * C::kTileBytes);
       for (int e = tid; e < C::kPagesPerTile * D * BS; e += C::kThreads) {
-        const int pgl = e / (D * BS);
-        const int t = e % BS;
-        const int key = key0 + pgl * BS + t;
-        if (key >= kv_end) reinterpret_cast<uint16_t *>(vtile)[e] = 0;
+        const int key = key0 + (e / (D * BS)) * BS + e % BS;
+        if (key >= kv_end) vtile[e] = 0;
       }
       __syncthreads();
     }
-    // ---- S = Q K^T for 16 rows x 64 keys
-    float sacc[kNT][4];
 #pragma unroll
-    for (int j = 0; j < kNT; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
+    for (int h = 0; h < C::kBK / C::kHK; ++h) {
+      const int hkey0 = key0 + h * C::kHK;
+      if (hkey0 > warp_pos_max || hkey0 >= kv_end) continue;  // hidden from every row of this warp
+      // ---- S = Q K^T for 16 rows x 32 keys
+      float sacc[kNT][4];
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
+      for (int j = 0; j < kNT; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
 #pragma unroll
-      for (int jp = 0; jp < kNT / 2; ++jp) {
-        // matrices: keys [16jp, +8) chunk 2ks | chunk 2ks+1 ; keys [16jp+8, +8) chunk 2ks | 2ks+1
-        const int key = jp * 16 + (lane & 7) + (lane >> 4) * 8;
-        const int chunk = 2 * ks + ((lane >> 3) & 1);
-        const uint32_t addr = sk + (key / BS) * C::kPB + (chunk * BS + key % BS) * 16;
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(addr, b0, b1, b2, b3);
-        mma16816<T>(sacc[2 * jp], qf[ks], b0, b1);
-        mma16816<T>(sacc[2 * jp + 1], qf[ks], b2, b3);
-      }
-    }
-    // ---- scale, softcap, causal mask, online softmax (log2 domain)
-    const bool need_mask = (key0 + C::kBK - 1 > base_pos) || (key0 + C::kBK > kv_end);
-    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t qa[4];
+        ldmatrix_x4(q_lane + ks * 32, qa[0], qa[1], qa[2], qa[3]);
 #pragma unroll
-    for (int j = 0; j < kNT; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float x = sacc[j][e] * p.scale;
-        if (use_softcap) x = p.softcap * tanhf(x / p.softcap);
-        x *= kLog2e;
-        if (need_mask) {
-          const int key = key0 + j * 8 + tig * 2 + (e & 1);
-          const int pos = (e < 2) ? pos_lo : pos_hi;
-          const bool ok = (e < 2 ? val_lo : val_hi) && key <= pos && key < kv_end;
-          x = ok ? x : -INFINITY;
+        for (int jp = 0; jp < kNT / 2; ++jp) {
+          const int key = h * C::kHK + jp * 16 + (lane & 7) + (lane >> 4) * 8;
+          const int chunk = 2 * ks + ((lane >> 3) & 1);
+          const uint32_t addr = sk + (key / BS) * C::kPB + (chunk * BS + key % BS) * 16;
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(addr, b0, b1, b2, b3);
+          mma16816<T>(sacc[2 * jp], qa, b0, b1);
+          mma16816<T>(sacc[2 * jp + 1], qa, b2, b3);
         }
-        sacc[j][e] = x;
       }
-      mx_lo = fmaxf(mx_lo, fmaxf(sacc[j][0], sacc[j][1]));
-      mx_hi = fmaxf(mx_hi, fmaxf(sacc[j][2], sacc[j][3]));
-    }
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-    // rows with nothing visible yet keep m = -inf; use 0 as the exp offset
-    const float off_lo = (mn_lo == -INFINITY) ? 0.f : mn_lo;
-    const float off_hi = (mn_hi == -INFINITY) ? 0.f : mn_hi;
-    const float a_lo = exp2f(m_lo - off_lo), a_hi = exp2f(m_hi - off_hi);
-    m_lo = mn_lo;
-    m_hi = mn_hi;
-    float ps_lo = 0.f, ps_hi = 0.f;
-    uint32_t pa[kNT / 2][4];
+      // ---- scale, softcap, causal mask, online softmax (log2 domain)
+      const bool need_mask = (hkey0 + C::kHK - 1 > base_pos) || (hkey0 + C::kHK > kv_end);
+      float mx_lo = -INFINITY, mx_hi = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kNT; ++j) {
-      const float p0 = exp2f(sacc[j][0] - off_lo), p1 = exp2f(sacc[j][1] - off_lo);
-      const float p2 = exp2f(sacc[j][2] - off_hi), p3 = exp2f(sacc[j][3] - off_hi);
-      ps_lo += p0 + p1;
-      ps_hi += p2 + p3;
-      // C fragment of n-tile j -> A fragment of key k-step j/2
-      if ((j & 1) == 0) {
-        pa[j / 2][0] = pack2<T>(p0, p1);
-        pa[j / 2][1] = pack2<T>(p2, p3);
-      } else {
-        pa[j / 2][2] = pack2<T>(p0, p1);
-        pa[j / 2][3] = pack2<T>(p2, p3);
+      for (int j = 0; j < kNT; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float x = sacc[j][e] * p.scale;
+          if (use_softcap) x = p.softcap * tanhf(x / p.softcap);
+          x *= kLog2e;
+          if (need_mask) {
+            const int key = hkey0 + j * 8 + tig * 2 + (e & 1);
+            const int pos = (e < 2) ? pos_lo : pos_hi;
+            const bool ok = (e < 2 ? val_lo : val_hi) && key <= pos && key < kv_end;
+            x = ok ? x : -INFINITY;
+          }
+          sacc[j][e] = x;
+        }
+        mx_lo = fmaxf(mx_lo, fmaxf(sacc[j][0], sacc[j][1]));
+        mx_hi = fmaxf(mx_hi, fmaxf(sacc[j][2], sacc[j][3]));
       }
-    }
-    l_lo = l_lo * a_lo + ps_lo;
-    l_hi = l_hi * a_hi + ps_hi;
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+      const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+      // rows with nothing visible yet keep m = -inf; use 0 as the exp offset
+      const float off_lo = (mn_lo == -INFINITY) ? 0.f : mn_lo;
+      const float off_hi = (mn_hi == -INFINITY) ? 0.f : mn_hi;
+      const float a_lo = exp2f(m_lo - off_lo), a_hi = exp2f(m_hi - off_hi);
+      m_lo = mn_lo;
+      m_hi = mn_hi;
+      float ps_lo = 0.f, ps_hi = 0.f;
+      uint32_t pa[kNT / 2][4];
 #pragma unroll
-    for (int j = 0; j < kDT; ++j) {
-      o[j][0] *= a_lo;
-      o[j][1] *= a_lo;
-      o[j][2] *= a_hi;
-      o[j][3] *= a_hi;
-    }
-    // ---- O += P V : k-steps of 16 keys, n-tiles of 8 dims
+      for (int j = 0; j < kNT; ++j) {
+        const float p0 = exp2f(sacc[j][0] - off_lo), p1 = exp2f(sacc[j][1] - off_lo);
+        const float p2 = exp2f(sacc[j][2] - off_hi), p3 = exp2f(sacc[j][3] - off_hi);
+        ps_lo += p0 + p1;
+        ps_hi += p2 + p3;
+        // C fragment of n-tile j -> A fragment of key k-step j/2
+        if ((j & 1) == 0) {
+          pa[j / 2][0] = pack2<T>(p0, p1);
+          pa[j / 2][1] = pack2<T>(p2, p3);
+        } else {
+          pa[j / 2][2] = pack2<T>(p0, p1);
+          pa[j / 2][3] = pack2<T>(p2, p3);
+        }
+      }
+      l_lo = l_lo * a_lo + ps_lo;
+      l_hi = l_hi * a_hi + ps_hi;
 #pragma unroll
-    for (int kk = 0; kk < C::kBK / 16; ++kk) {
+      for (int j = 0; j < kDT; ++j) {
+        o[j][0] *= a_lo;
+        o[j][1] *= a_lo;
+        o[j][2] *= a_hi;
+        o[j][3] *= a_hi;
+      }
+      // ---- O += P V : k-steps of 16 keys, n-tiles of 8 dims
 #pragma unroll
-      for (int dp = 0; dp < kDT / 2; ++dp) {
-        // matrices: dims [16dp, +8) keys [16kk, +8) | keys +8 ; dims +8 keys [16kk,+8) | keys +8
-        const int d = dp * 16 + (lane & 7) + (lane >> 4) * 8;
-        const int key = kk * 16 + ((lane >> 3) & 1) * 8;
-        const uint32_t addr = sv + (key / BS) * C::kPB + (d * BS + key % BS) * 2;
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(addr, b0, b1, b2, b3);
-        mma16816<T>(o[2 * dp], pa[kk], b0, b1);
-        mma16816<T>(o[2 * dp + 1], pa[kk], b2, b3);
+      for (int kk = 0; kk < C::kHK / 16; ++kk) {
+#pragma unroll
+        for (int dp = 0; dp < kDT / 2; ++dp) {
+          const int d = dp * 16 + (lane & 7) + (lane >> 4) * 8;
+          const int key = h * C::kHK + kk * 16 + ((lane >> 3) & 1) * 8;
+          const uint32_t addr = sv + (key / BS) * C::kPB + (d * BS + key % BS) * 2;
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(addr, b0, b1, b2, b3);
+          mma16816<T>(o[2 * dp], pa[kk], b0, b1);
+          mma16816<T>(o[2 * dp + 1], pa[kk], b2, b3);
+        }
       }
     }
     __syncthreads();  // every warp is done with stage s
@@ -357,7 +359,6 @@ __global__ void __launch_bounds__(128) prefill_tc_kernel(const PrefillParams p) 
       issue_tile(kt + C::kNST);
     }
   }
-  (void)aborted;
 
   // ---- normalise and store
   l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
