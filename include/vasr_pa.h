@@ -66,6 +66,7 @@ typedef enum vasr_pa_status {
 #define VASR_PA_DERR_CTX_RANGE 0x4     /* context_len > max_context_len bound */
 #define VASR_PA_DERR_WAIT_TIMEOUT 0x8  /* a bounded mbarrier wait gave up     */
 #define VASR_PA_DERR_MAPPING_RANGE 0x10 /* copy/swap pair out of range        */
+#define VASR_PA_DERR_QLEN_RANGE 0x20   /* prefill q_len > max_query_len       */
 
 int32_t vasr_pa_abi_version(void);
 const char *vasr_pa_status_string(int32_t status);
@@ -204,6 +205,10 @@ int32_t vasr_pa_gather_kv_cache(void *key_out, void *value_out,
  * vasr-models/src/model/attention.rs:86-149 with cache_len = context - q_len.
  * This replaces gather_kv_cache + flash_attn_varlen
  * (thinker_text.rs:1344-1365, attention.rs:580-657) in one kernel.
+ * max_query_len bounds every q_len (flash_attn_varlen's max_seqlen_q); the
+ * kernel schedules num_seqs x ceil(max_query_len / rows per CTA) CTAs, so a
+ * sequence longer than it is cut short and sets VASR_PA_DERR_QLEN_RANGE.
+ * 0 means "unknown" and schedules for the worst case (total_q_tokens).
  */
 int32_t vasr_pa_paged_attention_varlen_prefill(
     void *out, const void *query, const void *key_cache,

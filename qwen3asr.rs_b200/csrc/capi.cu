@@ -265,13 +265,15 @@ int32_t vasr_pa_fused_qk_norm_rope_append(
 
 int32_t vasr_pa_get_device_error(int32_t *out_bits, int32_t clear, vasr_pa_stream_t stream) {
   if (!out_bits) return VASR_PA_EINVAL_POINTER;
-  uint32_t a = 0, b = 0, c = 0, d = 0;
+  uint32_t a = 0, b = 0, c = 0, d = 0, e = 0;
   int r;
   if ((r = vasr::read_error_kv_ops(&a, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
   if ((r = vasr::read_error_decode(&b, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
   if ((r = vasr::read_error_prefill(&c, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
   if ((r = vasr::read_error_fused(&d, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
-  *out_bits = (int32_t)(a | b | c | d);
+  if ((r = vasr::read_error_prefill_umma(&e, clear != 0, to_stream(stream))) != VASR_PA_OK)
+    return r;
+  *out_bits = (int32_t)(a | b | c | d | e);
   return VASR_PA_OK;
 }
 

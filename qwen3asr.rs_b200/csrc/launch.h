@@ -130,6 +130,16 @@ int launch_append(const AppendArgs &a, cudaStream_t s);
 int launch_decode(const DecodeArgs &a, cudaStream_t s);
 int launch_gather(const GatherArgs &a, cudaStream_t s);
 int launch_prefill(const PrefillArgs &a, cudaStream_t s);
+// Position tiles per sequence for CTAs of `positions` query positions:
+// ceil(max_query_len / positions); max_query_len 0 (unknown) counts as
+// total_q_tokens, the largest length a single sequence can have.
+inline int64_t prefill_tiles_per_seq(const PrefillArgs &a, int positions) {
+  const int64_t mq = a.max_query_len > 0 ? a.max_query_len : a.total_q_tokens;
+  return (mq + positions - 1) / positions;
+}
+// tcgen05 kernel (bf16/f16, 16-token pages, head_dim 128, G in {1,2,4});
+// VASR_PA_ENOT_SUPPORTED for any other shape.
+int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s);
 int launch_copy_blocks(void *const *k, void *const *v, int layers, const int64_t *mapping,
                        int64_t pairs, int64_t num_blocks, int64_t block_bytes, cudaStream_t s);
 int launch_swap_blocks(void *dst, const void *src, const int64_t *mapping, int64_t pairs,
@@ -139,6 +149,7 @@ int launch_swap_blocks(void *dst, const void *src, const int64_t *mapping, int64
 int read_error_kv_ops(uint32_t *bits, bool clear, cudaStream_t s);
 int read_error_decode(uint32_t *bits, bool clear, cudaStream_t s);
 int read_error_prefill(uint32_t *bits, bool clear, cudaStream_t s);
+int read_error_prefill_umma(uint32_t *bits, bool clear, cudaStream_t s);
 
 // Raise a kernel's dynamic shared-memory limit once per device. The
 // attribute is not a stream operation, so this is legal during capture.

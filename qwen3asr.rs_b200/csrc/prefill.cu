@@ -20,6 +20,9 @@
 // the kernel under 128 registers (2 CTAs = 16 warps per SM). Warps whose
 // rows the causal mask hides from a whole half-tile skip it.
 // f32: CUDA-core kernel, one CTA per (query row, kv head), online softmax.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -40,6 +43,7 @@ struct PrefillParams {
   int num_heads;
   int num_kv_heads;
   int cols;
+  int tiles;  // position tiles per sequence (ceil(max_query_len / positions per CTA))
   float scale;
   float softcap;
 };
@@ -130,24 +134,13 @@ __global__ void __launch_bounds__(256, 2) prefill_tc_kernel(const PrefillParams 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kvh = blockIdx.y;
 
-  // ---- which (sequence, position tile) this CTA owns: walk the tiles per sequence
-  int b = -1, tile = 0;
-  {
-    int acc = 0;
-    for (int s = 0; s < p.num_seqs; ++s) {
-      const int ql = (int)(p.cu_q[s + 1] - p.cu_q[s]);
-      const int nt = (ql + C::kPos - 1) / C::kPos;
-      if ((int)blockIdx.x < acc + nt) {
-        b = s;
-        tile = (int)blockIdx.x - acc;
-        break;
-      }
-      acc += nt;
-    }
-  }
-  if (b < 0) return;
+  // ---- (sequence, position tile) of this CTA: blockIdx.x = b * tiles + tile
+  const int b = (int)blockIdx.x / p.tiles, tile = (int)blockIdx.x % p.tiles;
   const int64_t q0 = p.cu_q[b];
-  const int qlen = (int)(p.cu_q[b + 1] - p.cu_q[b]);
+  const int qlen = (int)(p.cu_q[b + 1] - q0);
+  if (tile == p.tiles - 1 && qlen > p.tiles * C::kPos && tid == 0)
+    raise_device_error(VASR_PA_DERR_QLEN_RANGE);
+  if (tile * C::kPos >= qlen) return;
   int ctx = (int)p.context_lens[b];
   if (ctx > p.cols * BS) {
     if (tid == 0) raise_device_error(VASR_PA_DERR_CTX_RANGE);
@@ -472,11 +465,12 @@ int launch_tc(const PrefillArgs &a, const PrefillParams &p, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(prefill_tc_kernel<T, BS, D, G>, C::kSmemBytes, attr_done))
     return VASR_PA_ELAUNCH;
-  // upper bound on position tiles: sum_b ceil(qlen_b / kPos) <= T / kPos + B
-  const int64_t tiles = a.total_q_tokens / C::kPos + a.num_seqs;
-  if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
-  dim3 grid((unsigned)tiles, (unsigned)a.num_kv_heads);
-  prefill_tc_kernel<T, BS, D, G><<<grid, C::kThreads, C::kSmemBytes, s>>>(p);
+  const int64_t tiles = prefill_tiles_per_seq(a, C::kPos);
+  if (tiles <= 0 || tiles * a.num_seqs > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+  PrefillParams pt = p;
+  pt.tiles = (int)tiles;
+  dim3 grid((unsigned)(tiles * a.num_seqs), (unsigned)a.num_kv_heads);
+  prefill_tc_kernel<T, BS, D, G><<<grid, C::kThreads, C::kSmemBytes, s>>>(pt);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
@@ -499,6 +493,16 @@ int tc_dispatch(const PrefillArgs &a, const PrefillParams &p, cudaStream_t s) {
     case 4: return tc_bs<T, 128, 4>(a, p, s);
     default: return VASR_PA_ENOT_SUPPORTED;
   }
+}
+
+// The tcgen05 kernel (prefill_umma.cu) serves the shapes it supports unless
+// VASR_PREFILL_KERNEL=mma selects this file's mma.sync kernel (A/B timing).
+bool umma_enabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("VASR_PREFILL_KERNEL");
+    return !(e && std::strcmp(e, "mma") == 0);
+  }();
+  return on;
 }
 
 template <int BS>
@@ -531,8 +535,13 @@ int launch_prefill(const PrefillArgs &a, cudaStream_t s) {
   p.num_heads = a.num_heads;
   p.num_kv_heads = a.num_kv_heads;
   p.cols = a.max_num_blocks_per_seq;
+  p.tiles = 1;
   p.scale = a.scale;
   p.softcap = a.softcapping;
+  if ((a.dtype == VASR_PA_BF16 || a.dtype == VASR_PA_F16) && umma_enabled()) {
+    const int r = launch_prefill_umma(a, s);
+    if (r != VASR_PA_ENOT_SUPPORTED) return r;
+  }
   switch (a.dtype) {
     case VASR_PA_BF16: return tc_dispatch<__nv_bfloat16>(a, p, s);
     case VASR_PA_F16: return tc_dispatch<__half>(a, p, s);

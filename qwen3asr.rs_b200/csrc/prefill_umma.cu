@@ -1,0 +1,676 @@
+// prefill_umma.cu — causal varlen (chunked) prefill attention on the
+// 5th-generation tensor cores (tcgen05.mma, accumulators in tensor memory).
+//
+// Same contract as the mma.sync kernel of prefill.cu (row i of sequence b
+// sits at position ctx[b] - qlen_b + i and attends keys j <= position, the
+// cached causal mask of vasr-models/src/model/attention.rs:86-149 applied
+// to run_single_sequence_attention :243-286), for bf16 / f16 pages of 16
+// tokens and head_dim 128.
+//
+// One CTA owns M = 128 rows = (128 / G) query positions x the G query heads
+// of one kv head and walks the keys in 64-key tiles:
+//   S  = Q K^T   one tcgen05.mma M128 N64 K16 per 16 head dims -> TMEM
+//   P  = exp2(S * scale * log2e - m)   one thread per row, P -> smem
+//   O += P V     one tcgen05.mma M128 N128 K16 per 16-token page -> TMEM
+// Warp roles (192 threads): warps 0-3 own TMEM lanes 0-127 (one row per
+// thread: softmax, O rescale, epilogue); warp 4 stages K/V tiles; warp 5
+// issues the MMAs. S is double-buffered in TMEM, so Q K^T of tile j+1 runs
+// on the tensor core while the softmax warps work on tile j.
+//
+// Shared-memory operand layouts (all "K-major", the reduction dim inside a
+// 16-byte chunk):
+//   Q  [16 dim chunks][128 rows][16 B]        no swizzle, LBO 2048, SBO 128
+//   K  [16 dim chunks][64 keys][16 B]         no swizzle, LBO 1024, SBO 128
+//      assembled from 256-byte bulk copies (one dim chunk of one page);
+//   P  [8 key chunks][128 rows][16 B]         no swizzle, LBO 2048, SBO 128
+//   V  one page = [128 dims][16 tokens] rows of 32 B, copied by a 2-D TMA
+//      load with the 32-byte swizzle, i.e. the canonical SW32 K-major layout
+//      (SBO 256) that the page's 16 tokens feed as one K = 16 step.
+// Softmax keeps a per-row running max that only moves when a tile's max
+// exceeds it by more than 2^8, so O in TMEM is rescaled rarely (exact in
+// real arithmetic: numerator and denominator use the same offset).
+// Every mbarrier wait is bounded (VASR_PA_DERR_WAIT_TIMEOUT) and the kernel
+// always frees its tensor memory before returning.
+#include <cuda.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace vasr {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kM = 128;                      // rows per CTA (UMMA M)
+constexpr int kNT = 64;                      // keys per tile (UMMA N of S)
+constexpr int kBS = 16;                      // tokens per page
+constexpr int kPagesPerTile = kNT / kBS;     // 4
+constexpr int kPageBytes = kD * kBS * 2;     // one head's K or V page
+constexpr int kStages = 2;
+constexpr int kQBytes = kM * kD * 2;         // 32 KB
+constexpr int kKVTile = kNT * kD * 2;        // 16 KB
+constexpr int kPBytes = kM * kNT * 2;        // 16 KB
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kQBytes;
+constexpr int kOffV = kOffK + kStages * kKVTile;
+constexpr int kOffP = kOffV + kStages * kKVTile;
+constexpr int kOffBar = kOffP + kPBytes;
+constexpr int kBarFullK = 0, kBarFullV = 2, kBarEmptyK = 4, kBarEmptyV = 6, kBarSFull = 8,
+              kBarPvDone = 10, kBarQ = 11;
+constexpr int kNumBars = 12;
+constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+constexpr int kSmemUsed = kOffTmemSlot + 16;
+constexpr int kSmemAlign = 256;              // SW32 pages need 256-byte alignment
+constexpr int kSmemBytes = kSmemUsed + kSmemAlign;
+constexpr int kTmemCols = 256;               // S ring 2 x 64 columns + O 128 columns
+constexpr int kTmemS = 0, kTmemO = 128;
+constexpr int kThreads = 160;              // warps 0-3 rows, warp 4 loads
+constexpr int kLoadWarp = 4;
+constexpr int kIdRegs = 4;                 // block ids of pages 0..127 held in registers
+constexpr float kRescaleLog2 = 8.f;          // rescale O only when the max grows > 2^8
+constexpr uint64_t kWaitNs = 200000000ull;   // 200 ms per wait before giving up
+
+static_assert(kSmemBytes + 1024 <= 233472 / 2, "two CTAs per SM must fit");
+
+// ------------------------------------------------------------ tcgen05 helpers
+// Shared-memory matrix descriptor: start, leading / stride byte offsets
+// (16-byte units), descriptor version 1, layout type (0 none, 6 SW32).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                          uint32_t layout) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+// Instruction descriptor of kind::f16: f32 accumulate, A and B of the same
+// 16-bit type, both K-major, M = 128, N = n.
+template <typename T>
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(kM >> 4) << 24);
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive (count 1) on `bar` once every tcgen05 op issued so far by this thread completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   slot_smem),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// 2-D tiled TMA load into this CTA's shared memory (no cluster fan-out).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
+      "[%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Single-thread bounded wait (same rules as wait_phase, no warp vote).
+__device__ __forceinline__ void wait_one(uint32_t bar, uint32_t parity, bool &dead) {
+  if (dead || mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return;
+    if (globaltimer_ns() - t0 > kWaitNs) break;
+  }
+  raise_device_error(VASR_PA_DERR_WAIT_TIMEOUT);
+  dead = true;
+}
+__device__ __forceinline__ float ex2_approx(float x) {  // PTX ex2.approx.ftz.f32
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+// Warp-uniform bounded wait for the phase `parity` of `bar` (every lane of
+// the warp calls it). After kWaitNs it raises VASR_PA_DERR_WAIT_TIMEOUT and
+// sets `dead`; a dead warp skips all later waits, so the CTA runs straight
+// to its end, drains its own copies and MMAs with bounded waits and frees
+// its tensor memory.
+__device__ __forceinline__ void wait_phase(uint32_t bar, uint32_t parity, bool &dead) {
+  if (!dead && !mbar_try_wait(bar, parity)) {
+    const uint64_t t0 = globaltimer_ns();
+    bool ok = false;
+    while (!ok) {
+      for (int i = 0; i < 64 && !ok; ++i) ok = mbar_try_wait(bar, parity);
+      if (!ok && globaltimer_ns() - t0 > kWaitNs) break;
+    }
+    if (!ok) {
+      raise_device_error(VASR_PA_DERR_WAIT_TIMEOUT);
+      dead = true;
+    }
+  }
+  dead = __any_sync(0xffffffffu, dead);
+}
+
+// 2-D TMA gather of four rows (box one row high) into four consecutive
+// shared-memory rows.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int x, int r0,
+                                            int r1, int r2, int r3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
+      : "memory");
+}
+// 4-D tiled TMA load (the Q tile: 16-byte chunks x heads x tokens x chunk index).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
+      "[%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2f(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2f<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2f<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kThreads, 2)
+    prefill_umma_kernel(const PrefillArgs p, const int tiles,
+                        const __grid_constant__ CUtensorMap q_map,
+                        const __grid_constant__ CUtensorMap k_map,
+                        const __grid_constant__ CUtensorMap v_map) {
+  constexpr int kPos = kM / G;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  const uint32_t sbase = (raw + kSmemAlign - 1) & ~(uint32_t)(kSmemAlign - 1);
+  unsigned char *smem = smem_raw + (sbase - raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kvh = blockIdx.y;
+  if (warp == kLoadWarp && lane == 0) {
+    prefetch_tensormap(&q_map);
+    prefetch_tensormap(&k_map);
+    prefetch_tensormap(&v_map);
+  }
+
+  // ---- (sequence, position tile) of this CTA: blockIdx.x = b * tiles + tile
+  const int b = (int)blockIdx.x / tiles, tile = (int)blockIdx.x % tiles;
+  const int cols = p.max_num_blocks_per_seq;
+  const int64_t q0 = p.cu_seqlens_q[b];
+  const int qlen = (int)(p.cu_seqlens_q[b + 1] - q0);
+  if (tile == tiles - 1 && qlen > tiles * kPos && tid == 0)
+    raise_device_error(VASR_PA_DERR_QLEN_RANGE);
+  if (tile * kPos >= qlen) return;
+  int ctx = (int)p.context_lens[b];
+  if (ctx > cols * kBS) {
+    if (tid == 0) raise_device_error(VASR_PA_DERR_CTX_RANGE);
+    ctx = cols * kBS;
+  }
+  const int i0 = tile * kPos;
+  const int n_pos = min(kPos, qlen - i0);
+  const int base_pos = ctx - qlen + i0;
+  const int kv_end = min(ctx, base_pos + n_pos);
+  T *out = reinterpret_cast<T *>(p.out);
+  const int64_t row_stride = (int64_t)p.num_heads * kD;
+  if (kv_end <= 0) {
+    for (int e = tid; e < n_pos * G * kD; e += kThreads) {
+      const int r = e / kD, d = e % kD;
+      out[(q0 + i0 + r / G) * row_stride + (int64_t)(kvh * G + r % G) * kD + d] =
+          Elem<T>::from_f32(0.f);
+    }
+    return;
+  }
+  const int n_pages = (kv_end + kBS - 1) / kBS;
+  const int n_kt = (kv_end + kNT - 1) / kNT;
+  const uint32_t bar = sbase + kOffBar;
+  auto B = [&](int i) { return bar + 8u * (uint32_t)i; };
+
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ loads
+    // K tile j -> K stage j & 1 as 64 bulk copies (one 256-byte dim chunk of
+    // one page each); V tile j -> V stage j & 1 as one swizzled 2-D TMA load
+    // per page. K j + 2 waits for Q K^T j, V j + 2 for P V j. Lane l keeps
+    // the block ids of pages l, l + 32, l + 64, l + 96 in registers.
+    const uint32_t *table = p.block_tables + (int64_t)b * cols;
+    uint32_t ids[kIdRegs];
+#pragma unroll
+    for (int i = 0; i < kIdRegs; ++i) {
+      const int pg = lane + 32 * i;
+      ids[i] = pg < n_pages ? __ldg(table + pg) : 0u;
+    }
+    if (lane == 0) {
+      for (int i = 0; i < kNumBars; ++i) mbar_init(B(i), 1);
+      mbar_fence_init();
+      mbar_arrive_expect_tx(B(kBarQ), (uint32_t)kQBytes);
+      tma_load_4d(sbase + kOffQ, &q_map, 0, kvh * G, (int)(q0 + i0), 0, B(kBarQ));
+    }
+    __syncwarp();
+    auto tile_page = [&](int j, int &np) -> uint32_t {  // page id of tile j held by this lane
+      const int pg0 = j * kPagesPerTile;
+      np = min(kPagesPerTile, n_pages - pg0);
+      const int grp = pg0 >> 5;  // warp-uniform: a tile's pages share one group of 32
+      uint32_t v = ids[0];
+#pragma unroll
+      for (int i = 1; i < kIdRegs; ++i) v = grp == i ? ids[i] : v;
+      uint32_t id = __shfl_sync(0xffffffffu, v, (pg0 & 31) + (lane & (kPagesPerTile - 1)));
+      if (grp >= kIdRegs && lane < np) id = __ldg(table + pg0 + lane);
+      if (lane < np && (int64_t)id >= p.num_blocks) {
+        raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
+        id = 0;
+      }
+      return id;
+    };
+    auto load_k = [&](int j) {
+      // one gather of the four pages' 256-byte rows of dim chunk c per lane c
+      int np;
+      uint32_t id = tile_page(j, np);
+      const uint32_t id0 = __shfl_sync(0xffffffffu, id, 0);
+      if (lane >= np) id = id0;  // pages past the context: any valid row (masked)
+      int row[kPagesPerTile];
+#pragma unroll
+      for (int pg = 0; pg < kPagesPerTile; ++pg)
+        row[pg] = (int)(((int64_t)__shfl_sync(0xffffffffu, id, pg) * p.num_kv_heads + kvh) * 16);
+      const uint32_t fb = B(kBarFullK + (j & 1));
+      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)kKVTile);
+      __syncwarp();
+      if (lane < kD / 8)
+        tma_gather4(sbase + kOffK + (j & 1) * kKVTile + lane * (kNT * 16), &k_map, 0,
+                    row[0] + lane, row[1] + lane, row[2] + lane, row[3] + lane, fb);
+    };
+    auto load_v = [&](int j) {
+      int np;
+      const uint32_t id = tile_page(j, np);
+      const uint32_t fb = B(kBarFullV + (j & 1));
+      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(np * kPageBytes));
+      __syncwarp();
+      if (lane < np)
+        tma_load_2d(sbase + kOffV + (j & 1) * kKVTile + lane * kPageBytes, &v_map, 0,
+                    (int)(((int64_t)id * p.num_kv_heads + kvh) * kD), fb);
+    };
+    // the first two K and V tiles start before the CTA-wide sync
+    load_k(0);
+    if (n_kt > 1) load_k(1);
+    load_v(0);
+    if (n_kt > 1) load_v(1);
+    __syncthreads();
+    // The tensor core completes Q K^T 0, Q K^T 1, P V 0, Q K^T 2, P V 1, ...
+    // in this order; the loads wait for those events in the same order.
+    bool dead = false;
+    for (int j = 2; j < min(n_kt, 4); ++j) {
+      wait_phase(B(kBarEmptyK + (j & 1)), ((j >> 1) - 1) & 1, dead);
+      load_k(j);
+    }
+    for (int j = 2; j < n_kt; ++j) {
+      wait_phase(B(kBarEmptyV + (j & 1)), ((j >> 1) - 1) & 1, dead);
+      load_v(j);
+      if (j + 2 < n_kt) {
+        wait_phase(B(kBarEmptyK + (j & 1)), (((j + 2) >> 1) - 1) & 1, dead);
+        load_k(j + 2);
+      }
+    }
+    // copies still in flight must land before the CTA's shared memory goes
+    // away (in a healthy run every one of them was already waited for)
+    dead = false;
+    for (int j = max(0, n_kt - kStages); j < n_kt; ++j) {
+      wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
+      wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
+    }
+    __syncthreads();
+    return;
+  }
+
+  // ---------------------------------------------------------------- warps 0-3
+  // One row per thread (TMEM lane = row): softmax, O rescale, epilogue.
+  // Thread 0 also issues every MMA of the CTA.
+  if (warp == 0) tmem_alloc(sbase + kOffTmemSlot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffTmemSlot);
+  bool dead = false;     // this warp gave up on a wait
+  bool dead_mma = false; // thread 0 gave up on a wait
+  const uint32_t idesc_s = idesc_f16<T>(kNT), idesc_o = idesc_f16<T>(kD);
+  auto issue_s = [&](int j) {  // thread 0: S(j & 1) = Q K_j^T
+    wait_one(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead_mma);
+    tc_fence_after();
+    const uint32_t sk = sbase + kOffK + (j & 1) * kKVTile;
+#pragma unroll
+    for (int ks = 0; ks < kD / 16; ++ks)
+      umma_f16(tmem + kTmemS + (j & 1) * kNT,
+               sdesc(sbase + kOffQ + ks * 2 * (kM * 16), kM * 16, 128, 0),
+               sdesc(sk + ks * 2 * (kNT * 16), kNT * 16, 128, 0), idesc_s, ks > 0);
+    umma_commit(B(kBarSFull + (j & 1)));
+    umma_commit(B(kBarEmptyK + (j & 1)));
+  };
+  if (tid == 0) {
+    wait_one(B(kBarQ), 0, dead_mma);
+    issue_s(0);
+    if (n_kt > 1) issue_s(1);
+  }
+  __syncwarp();
+
+  const int r = tid;
+  const bool row_ok = (r / G) < n_pos;
+  const int lim = row_ok ? min(base_pos + r / G, kv_end - 1) : -1;  // last visible key
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const bool use_softcap = (p.softcapping != 1.0f) && (p.softcapping > 0.f);
+  const float c = p.scale * kLog2e;
+  float m = -INFINITY, l = 0.f;
+  for (int j = 0; j < n_kt; ++j) {
+    wait_phase(B(kBarSFull + (j & 1)), (j >> 1) & 1, dead);
+    tc_fence_after();
+    uint32_t u[kNT];
+    const uint32_t ts = tmem + lane_base + kTmemS + (j & 1) * kNT;
+    tmem_ld32(ts, u);
+    tmem_ld32(ts + 32, u + 32);
+    tmem_wait_ld();
+    const int kmax = lim - j * kNT;  // elements k <= kmax are visible to this row
+    float x[kNT];
+    if (!use_softcap) {
+#pragma unroll
+      for (int k = 0; k < kNT; ++k) x[k] = (k <= kmax) ? __uint_as_float(u[k]) * c : -INFINITY;
+    } else {
+#pragma unroll
+      for (int k = 0; k < kNT; ++k) {
+        const float v = p.softcapping * tanhf(__uint_as_float(u[k]) * p.scale / p.softcapping);
+        x[k] = (k <= kmax) ? v * kLog2e : -INFINITY;
+      }
+    }
+    float m4[4] = {x[0], x[1], x[2], x[3]};
+#pragma unroll
+    for (int k = 4; k < kNT; ++k) m4[k & 3] = fmaxf(m4[k & 3], x[k]);
+    const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    const float m_new = (mx > m + kRescaleLog2) ? mx : m;
+    const float alpha = (m_new == m) ? 1.f : ex2_approx(m - m_new);
+    const float off = (m_new == -INFINITY) ? 0.f : m_new;
+    m = m_new;
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t pk[kNT / 2];
+#pragma unroll
+    for (int k = 0; k < kNT / 2; ++k) {
+      const float p0 = ex2_approx(x[2 * k] - off), p1 = ex2_approx(x[2 * k + 1] - off);
+      s4[k & 3] += p0 + p1;
+      pk[k] = pack2f<T>(p0, p1);
+    }
+    l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+    if (j > 0) {
+      // the P buffer and O are free once P V of the previous tile completed
+      wait_phase(B(kBarPvDone), (j - 1) & 1, dead);
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int cc = 0; cc < kD; cc += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + kTmemO + cc, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem + lane_base + kTmemO + cc, o);
+        }
+        tmem_wait_st();
+      }
+    }
+#pragma unroll
+    for (int kc = 0; kc < kNT / 8; ++kc)
+      *reinterpret_cast<uint4 *>(smem + kOffP + kc * (kM * 16) + r * 16) =
+          make_uint4(pk[4 * kc], pk[4 * kc + 1], pk[4 * kc + 2], pk[4 * kc + 3]);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    named_bar_sync(1, 4 * 32);  // P_j complete, S_j consumed by all four warps
+    if (warp == 0) {
+      tc_fence_after();
+      wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
+      if (j == n_kt - 1 && (kv_end % kBS) != 0) {
+        // V of tokens >= kv_end in the last page holds other data (possibly
+        // non-finite); zero it so that P = 0 there contributes exactly 0.
+        const int pl = (kv_end - 1) / kBS - j * kPagesPerTile;
+        const int valid = kv_end - (j * kPagesPerTile + pl) * kBS;
+        unsigned char *vp = smem + kOffV + (j & 1) * kKVTile + pl * kPageBytes;
+        for (int e = lane; e < kD * kBS; e += 32) {
+          const int d = e >> 4, key = e & 15;
+          if (key >= valid) {
+            const int chunk = (key >> 3) ^ ((d >> 2) & 1);  // 32-byte swizzle
+            *reinterpret_cast<uint16_t *>(vp + d * 32 + chunk * 16 + (key & 7) * 2) = 0;
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      if (lane == 0) {
+        const int np = min(kPagesPerTile, n_pages - j * kPagesPerTile);
+        const uint32_t sv = sbase + kOffV + (j & 1) * kKVTile;
+        for (int pg = 0; pg < np; ++pg)
+          umma_f16(tmem + kTmemO, sdesc(sbase + kOffP + pg * 2 * (kM * 16), kM * 16, 128, 0),
+                   sdesc(sv + pg * kPageBytes, 16, 256, 6), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
+        umma_commit(B(kBarEmptyV + (j & 1)));
+        umma_commit(B(kBarPvDone));
+        if (j + 2 < n_kt) issue_s(j + 2);
+      }
+      __syncwarp();
+    }
+  }
+
+  // ---- epilogue: O / l -> out (the last P V commit covers every MMA)
+  wait_phase(B(kBarPvDone), (n_kt - 1) & 1, dead);
+  tc_fence_after();
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  T *dst = out + (q0 + i0 + r / G) * row_stride + (int64_t)(kvh * G + r % G) * kD;
+#pragma unroll 1
+  for (int cc = 0; cc < kD; cc += 64) {
+    uint32_t o[64];
+    tmem_ld32(tmem + lane_base + kTmemO + cc, o);
+    tmem_ld32(tmem + lane_base + kTmemO + cc + 32, o + 32);
+    tmem_wait_ld();
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      w[i] = pack2f<T>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+    if (row_ok) {
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst + cc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------- host
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn tensor_map_encoder() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// V cache viewed as rows of one token page line: [nb * Hkv * 128 dims][16 tokens].
+bool make_v_map(CUtensorMap *map, const void *v_cache, int64_t num_blocks, int num_kv_heads) {
+  EncodeTiledFn enc = tensor_map_encoder();
+  if (!enc) return false;
+  const int64_t rows = num_blocks * num_kv_heads * kD;
+  if (rows <= 0 || rows >= (int64_t(1) << 31)) return false;  // int32 TMA row coordinates
+  const cuuint64_t dims[2] = {(cuuint64_t)kBS, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kBS * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBS, (cuuint32_t)kD};
+  const cuuint32_t estr[2] = {1, 1};
+  std::memset(map, 0, sizeof(*map));
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(v_cache), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// K cache viewed as rows of one dim chunk of one page: [nb * Hkv * 16][16 tokens x 8].
+bool make_k_map(CUtensorMap *map, const void *k_cache, int64_t num_blocks, int num_kv_heads) {
+  EncodeTiledFn enc = tensor_map_encoder();
+  if (!enc) return false;
+  const int64_t rows = num_blocks * num_kv_heads * (kD / 8);
+  const cuuint64_t dims[2] = {(cuuint64_t)kBS * 8, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kBS * 8 * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBS * 8, 1};
+  const cuuint32_t estr[2] = {1, 1};
+  std::memset(map, 0, sizeof(*map));
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(k_cache), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Q viewed as [16 dim chunks][tokens][heads][8 elements]: a box of
+// (8, G, 128 / G, 16) lands as [chunk][position][head][16 B], the canonical
+// no-swizzle K-major layout of the CTA's 128 rows (row = position * G + head).
+// Rows past the last token read zeros.
+bool make_q_map(CUtensorMap *map, const PrefillArgs &a, int g) {
+  EncodeTiledFn enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {8, (cuuint64_t)a.num_heads, (cuuint64_t)a.total_q_tokens, kD / 8};
+  const cuuint64_t strides[3] = {(cuuint64_t)kD * 2, (cuuint64_t)a.q_token_stride * 2, 16};
+  const cuuint32_t box[4] = {8, (cuuint32_t)g, (cuuint32_t)(kM / g), kD / 8};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  std::memset(map, 0, sizeof(*map));
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void *>(a.query), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, int G>
+int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, const CUtensorMap &kmap,
+             const CUtensorMap &map, cudaStream_t s) {
+  static std::atomic<uint64_t> attr_done{0};
+  if (!ensure_smem_attr(prefill_umma_kernel<T, G>, kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
+  constexpr int kPos = kM / G;
+  const int64_t tiles = prefill_tiles_per_seq(a, kPos);
+  if (tiles <= 0 || tiles * a.num_seqs > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+  dim3 grid((unsigned)(tiles * a.num_seqs), (unsigned)a.num_kv_heads);
+  prefill_umma_kernel<T, G><<<grid, kThreads, kSmemBytes, s>>>(a, (int)tiles, qmap, kmap, map);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
+}  // namespace
+
+int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s) {
+  if (a.head_dim != kD || a.block_size != kBS) return VASR_PA_ENOT_SUPPORTED;
+  if (a.dtype != VASR_PA_BF16 && a.dtype != VASR_PA_F16) return VASR_PA_ENOT_SUPPORTED;
+  if (a.num_kv_heads > 65535) return VASR_PA_EINVAL_SHAPE;
+  const int g = a.num_heads / a.num_kv_heads;
+  if (g != 1 && g != 2 && g != 4) return VASR_PA_ENOT_SUPPORTED;
+  if ((int64_t)a.num_blocks * a.num_kv_heads * kD >= (int64_t(1) << 31))
+    return VASR_PA_ENOT_SUPPORTED;  // int32 TMA row coordinates
+  if (a.total_q_tokens >= (int64_t(1) << 31)) return VASR_PA_ENOT_SUPPORTED;
+  CUtensorMap qmap, kmap, map;
+  if (!make_v_map(&map, a.value_cache, a.num_blocks, a.num_kv_heads)) return VASR_PA_ELAUNCH;
+  if (!make_k_map(&kmap, a.key_cache, a.num_blocks, a.num_kv_heads)) return VASR_PA_ELAUNCH;
+  if (!make_q_map(&qmap, a, g)) return VASR_PA_ELAUNCH;
+  const bool bf = a.dtype == VASR_PA_BF16;
+  switch (g) {
+    case 1:
+      return bf ? launch_g<__nv_bfloat16, 1>(a, qmap, kmap, map, s) : launch_g<__half, 1>(a, qmap, kmap, map, s);
+    case 2:
+      return bf ? launch_g<__nv_bfloat16, 2>(a, qmap, kmap, map, s) : launch_g<__half, 2>(a, qmap, kmap, map, s);
+    default:
+      return bf ? launch_g<__nv_bfloat16, 4>(a, qmap, kmap, map, s) : launch_g<__half, 4>(a, qmap, kmap, map, s);
+  }
+}
+
+int read_error_prefill_umma(uint32_t *bits, bool clear, cudaStream_t s) {
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_device_error, sizeof(v), 0, cudaMemcpyDeviceToHost, s) !=
+      cudaSuccess)
+    return VASR_PA_ELAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return VASR_PA_ELAUNCH;
+  if (clear) {
+    const uint32_t z = 0;
+    if (cudaMemcpyToSymbolAsync(g_device_error, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s) !=
+        cudaSuccess)
+      return VASR_PA_ELAUNCH;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return VASR_PA_ELAUNCH;
+  }
+  *bits = v;
+  return VASR_PA_OK;
+}
+
+}  // namespace vasr

@@ -33,6 +33,7 @@ DERR_BLOCK_RANGE = 0x2
 DERR_CTX_RANGE = 0x4
 DERR_WAIT_TIMEOUT = 0x8
 DERR_MAPPING_RANGE = 0x10
+DERR_QLEN_RANGE = 0x20
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32

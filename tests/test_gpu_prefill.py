@@ -87,3 +87,19 @@ def test_prefill_config3_first_rounds(cuda_device):
         chunk = [n for (_, _, n) in r]
         case = make_prefill_case(10 + len(r), cached, chunk, dtype="bf16")
         assert np.abs(run_prefill(case, cuda_device) - oracle_prefill(case)).max() <= TOL["bf16"]
+
+
+def test_prefill_max_query_len_bound(cuda_device):
+    """max_query_len 0 means unknown (worst-case schedule); too small a bound is flagged."""
+    case = make_prefill_case(7, [0, 40, 7], [150, 3, 64], dtype="bf16")
+    exp = oracle_prefill(case)
+    args = (to_dev(case.q, "bf16", cuda_device), to_dev(case.key_cache, "bf16", cuda_device),
+            to_dev(case.value_cache, "bf16", cuda_device),
+            torch.from_numpy(case.block_tables.astype(np.int32)).to(cuda_device),
+            torch.from_numpy(case.context_lens.astype(np.int32)).to(cuda_device),
+            torch.from_numpy(case.cu_q.astype(np.int32)).to(cuda_device), None, None, 128 ** -0.5, 1.0)
+    got = pa.paged_attention_varlen_prefill(*args, 0).float().cpu().numpy()
+    assert np.abs(got - exp).max() <= TOL["bf16"]
+    assert pa.device_error() == 0
+    pa.paged_attention_varlen_prefill(*args, 20)
+    assert pa.device_error(clear=True) & 0x20  # VASR_PA_DERR_QLEN_RANGE
