@@ -10,22 +10,24 @@
 // One CTA owns M = 128 rows = (128 / G) query positions x the G query heads
 // of one kv head and walks the keys in 64-key tiles:
 //   S  = Q K^T   one tcgen05.mma M128 N64 K16 per 16 head dims -> TMEM
-//   P  = exp2(S * scale * log2e - m)   one thread per row, P -> smem
-//   O += P V     one tcgen05.mma M128 N128 K16 per 16-token page -> TMEM
+//   P  = exp2(S * scale * log2e - m)   one thread per row; P (16-bit) is
+//        stored back over the first half of its S buffer in TMEM
+//   O += P V     one tcgen05.mma M128 N128 K16 per 16-token page, A = P read
+//        from TMEM, accumulator O in TMEM
 // Warp roles (192 threads): warps 0-3 own TMEM lanes 0-127 (one row per
-// thread: softmax, O rescale, epilogue); warp 4 stages K/V tiles; warp 5
-// issues the MMAs. S is double-buffered in TMEM, so Q K^T of tile j+1 runs
-// on the tensor core while the softmax warps work on tile j.
+// thread: softmax, O rescale, epilogue); warp 4 issues the MMAs; warp 5
+// stages Q, K and V with TMA. S is double-buffered in TMEM, so Q K^T of
+// tile j + 1 is ready while the softmax warps work on tile j.
 //
 // Shared-memory operand layouts (all "K-major", the reduction dim inside a
 // 16-byte chunk):
-//   Q  [16 dim chunks][128 rows][16 B]        no swizzle, LBO 2048, SBO 128
-//   K  [16 dim chunks][64 keys][16 B]         no swizzle, LBO 1024, SBO 128
-//      assembled from 256-byte bulk copies (one dim chunk of one page);
-//   P  [8 key chunks][128 rows][16 B]         no swizzle, LBO 2048, SBO 128
-//   V  one page = [128 dims][16 tokens] rows of 32 B, copied by a 2-D TMA
-//      load with the 32-byte swizzle, i.e. the canonical SW32 K-major layout
-//      (SBO 256) that the page's 16 tokens feed as one K = 16 step.
+//   Q  [16 dim chunks][128 rows][16 B]   no swizzle, LBO 2048, SBO 128; one
+//      4-D TMA load (chunk x token x head x 8 elements)
+//   K  [16 dim chunks][64 keys][16 B]    no swizzle, LBO 1024, SBO 128; per
+//      dim chunk one TMA gather4 of that chunk's 256-byte row in 4 pages
+//   V  one page = [128 dims][16 tokens] rows of 32 B, one 2-D TMA load with
+//      the 32-byte swizzle = the canonical SW32 K-major layout (SBO 256) that
+//      the page's 16 tokens feed as one K = 16 step
 // Softmax keeps a per-row running max that only moves when a tile's max
 // exceeds it by more than 2^8, so O in TMEM is rescaled rarely (exact in
 // real arithmetic: numerator and denominator use the same offset).
@@ -53,23 +55,22 @@ constexpr int kPageBytes = kD * kBS * 2;     // one head's K or V page
 constexpr int kStages = 2;
 constexpr int kQBytes = kM * kD * 2;         // 32 KB
 constexpr int kKVTile = kNT * kD * 2;        // 16 KB
-constexpr int kPBytes = kM * kNT * 2;        // 16 KB
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVTile;
-constexpr int kOffP = kOffV + kStages * kKVTile;
-constexpr int kOffBar = kOffP + kPBytes;
+constexpr int kOffBar = kOffV + kStages * kKVTile;
 constexpr int kBarFullK = 0, kBarFullV = 2, kBarEmptyK = 4, kBarEmptyV = 6, kBarSFull = 8,
-              kBarPvDone = 10, kBarQ = 11;
-constexpr int kNumBars = 12;
+              kBarPFull = 10, kBarPvDone = 12, kBarQ = 13;
+constexpr int kNumBars = 14;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemUsed = kOffTmemSlot + 16;
 constexpr int kSmemAlign = 256;              // SW32 pages need 256-byte alignment
 constexpr int kSmemBytes = kSmemUsed + kSmemAlign;
 constexpr int kTmemCols = 256;               // S ring 2 x 64 columns + O 128 columns
 constexpr int kTmemS = 0, kTmemO = 128;
-constexpr int kThreads = 160;              // warps 0-3 rows, warp 4 loads
-constexpr int kLoadWarp = 4;
+constexpr int kThreads = 192;              // warps 0-3 rows, warp 4 MMA, warp 5 loads
+constexpr int kMmaWarp = 4;
+constexpr int kLoadWarp = 5;
 constexpr int kIdRegs = 4;                 // block ids of pages 0..127 held in registers
 constexpr float kRescaleLog2 = 8.f;          // rescale O only when the max grows > 2^8
 constexpr uint64_t kWaitNs = 200000000ull;   // 200 ms per wait before giving up
@@ -91,6 +92,15 @@ __device__ __forceinline__ uint32_t idesc_f16(int n) {
   constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
   return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(kM >> 4) << 24);
+}
+// A from tensor memory: row i in lane i, 16-bit K pairs packed per 32-bit column.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
 }
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                          uint32_t accumulate) {
@@ -167,25 +177,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Single-thread bounded wait (same rules as wait_phase, no warp vote).
-__device__ __forceinline__ void wait_one(uint32_t bar, uint32_t parity, bool &dead) {
-  if (dead || mbar_try_wait(bar, parity)) return;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return;
-    if (globaltimer_ns() - t0 > kWaitNs) break;
-  }
-  raise_device_error(VASR_PA_DERR_WAIT_TIMEOUT);
-  dead = true;
-}
 __device__ __forceinline__ float ex2_approx(float x) {  // PTX ex2.approx.ftz.f32
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -264,8 +262,20 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---- (sequence, position tile) of this CTA: blockIdx.x = b * tiles + tile
-  const int b = (int)blockIdx.x / tiles, tile = (int)blockIdx.x % tiles;
+  // (the last position tile of a sequence, the one with the most keys, first)
+  const int b = (int)blockIdx.x / tiles, tile = tiles - 1 - (int)blockIdx.x % tiles;
   const int cols = p.max_num_blocks_per_seq;
+  // The load warp fetches the sequence's first block ids (pages lane + 32 i)
+  // together with its lengths, before it knows how many it needs.
+  const uint32_t *table = p.block_tables + (int64_t)b * cols;
+  uint32_t ids[kIdRegs];
+#pragma unroll
+  for (int i = 0; i < kIdRegs; ++i) ids[i] = 0u;
+  if (warp == kLoadWarp) {
+#pragma unroll
+    for (int i = 0; i < kIdRegs; ++i)
+      if (lane + 32 * i < cols) ids[i] = __ldg(table + lane + 32 * i);
+  }
   const int64_t q0 = p.cu_seqlens_q[b];
   const int qlen = (int)(p.cu_seqlens_q[b + 1] - q0);
   if (tile == tiles - 1 && qlen > tiles * kPos && tid == 0)
@@ -301,15 +311,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     // one page each); V tile j -> V stage j & 1 as one swizzled 2-D TMA load
     // per page. K j + 2 waits for Q K^T j, V j + 2 for P V j. Lane l keeps
     // the block ids of pages l, l + 32, l + 64, l + 96 in registers.
-    const uint32_t *table = p.block_tables + (int64_t)b * cols;
-    uint32_t ids[kIdRegs];
-#pragma unroll
-    for (int i = 0; i < kIdRegs; ++i) {
-      const int pg = lane + 32 * i;
-      ids[i] = pg < n_pages ? __ldg(table + pg) : 0u;
-    }
     if (lane == 0) {
-      for (int i = 0; i < kNumBars; ++i) mbar_init(B(i), 1);
+      for (int i = 0; i < kNumBars; ++i) mbar_init(B(i), (i == kBarPFull || i == kBarPFull + 1) ? 4 * 32 : 1);
       mbar_fence_init();
       mbar_arrive_expect_tx(B(kBarQ), (uint32_t)kQBytes);
       tma_load_4d(sbase + kOffQ, &q_map, 0, kvh * G, (int)(q0 + i0), 0, B(kBarQ));
@@ -389,106 +392,38 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
 
-  // ---------------------------------------------------------------- warps 0-3
-  // One row per thread (TMEM lane = row): softmax, O rescale, epilogue.
-  // Thread 0 also issues every MMA of the CTA.
+  // ------------------------------------------------------ warps 0-3 and 5
   if (warp == 0) tmem_alloc(sbase + kOffTmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffTmemSlot);
-  bool dead = false;     // this warp gave up on a wait
-  bool dead_mma = false; // thread 0 gave up on a wait
-  const uint32_t idesc_s = idesc_f16<T>(kNT), idesc_o = idesc_f16<T>(kD);
-  auto issue_s = [&](int j) {  // thread 0: S(j & 1) = Q K_j^T
-    wait_one(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead_mma);
-    tc_fence_after();
-    const uint32_t sk = sbase + kOffK + (j & 1) * kKVTile;
+  bool dead = false;  // this warp gave up on a wait
+
+  if (warp == kMmaWarp) {
+    // ---------------------------------------------------------- MMA issuer
+    // Order on the tensor core: Q K^T 0, Q K^T 1, then per tile j: P V j,
+    // Q K^T j + 2. Backpressure from the tensor core stalls only this warp.
+    const uint32_t idesc_s = idesc_f16<T>(kNT), idesc_o = idesc_f16<T>(kD);
+    auto issue_s = [&](int j) {  // S(j & 1) = Q K_j^T
+      wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t sk = sbase + kOffK + (j & 1) * kKVTile;
 #pragma unroll
-    for (int ks = 0; ks < kD / 16; ++ks)
-      umma_f16(tmem + kTmemS + (j & 1) * kNT,
-               sdesc(sbase + kOffQ + ks * 2 * (kM * 16), kM * 16, 128, 0),
-               sdesc(sk + ks * 2 * (kNT * 16), kNT * 16, 128, 0), idesc_s, ks > 0);
-    umma_commit(B(kBarSFull + (j & 1)));
-    umma_commit(B(kBarEmptyK + (j & 1)));
-  };
-  if (tid == 0) {
-    wait_one(B(kBarQ), 0, dead_mma);
+        for (int ks = 0; ks < kD / 16; ++ks)
+          umma_f16(tmem + kTmemS + (j & 1) * kNT,
+                   sdesc(sbase + kOffQ + ks * 2 * (kM * 16), kM * 16, 128, 0),
+                   sdesc(sk + ks * 2 * (kNT * 16), kNT * 16, 128, 0), idesc_s, ks > 0);
+        umma_commit(B(kBarSFull + (j & 1)));
+        umma_commit(B(kBarEmptyK + (j & 1)));
+      }
+      __syncwarp();
+    };
+    wait_phase(B(kBarQ), 0, dead);
     issue_s(0);
     if (n_kt > 1) issue_s(1);
-  }
-  __syncwarp();
-
-  const int r = tid;
-  const bool row_ok = (r / G) < n_pos;
-  const int lim = row_ok ? min(base_pos + r / G, kv_end - 1) : -1;  // last visible key
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  const bool use_softcap = (p.softcapping != 1.0f) && (p.softcapping > 0.f);
-  const float c = p.scale * kLog2e;
-  float m = -INFINITY, l = 0.f;
-  for (int j = 0; j < n_kt; ++j) {
-    wait_phase(B(kBarSFull + (j & 1)), (j >> 1) & 1, dead);
-    tc_fence_after();
-    uint32_t u[kNT];
-    const uint32_t ts = tmem + lane_base + kTmemS + (j & 1) * kNT;
-    tmem_ld32(ts, u);
-    tmem_ld32(ts + 32, u + 32);
-    tmem_wait_ld();
-    const int kmax = lim - j * kNT;  // elements k <= kmax are visible to this row
-    float x[kNT];
-    if (!use_softcap) {
-#pragma unroll
-      for (int k = 0; k < kNT; ++k) x[k] = (k <= kmax) ? __uint_as_float(u[k]) * c : -INFINITY;
-    } else {
-#pragma unroll
-      for (int k = 0; k < kNT; ++k) {
-        const float v = p.softcapping * tanhf(__uint_as_float(u[k]) * p.scale / p.softcapping);
-        x[k] = (k <= kmax) ? v * kLog2e : -INFINITY;
-      }
-    }
-    float m4[4] = {x[0], x[1], x[2], x[3]};
-#pragma unroll
-    for (int k = 4; k < kNT; ++k) m4[k & 3] = fmaxf(m4[k & 3], x[k]);
-    const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-    const float m_new = (mx > m + kRescaleLog2) ? mx : m;
-    const float alpha = (m_new == m) ? 1.f : ex2_approx(m - m_new);
-    const float off = (m_new == -INFINITY) ? 0.f : m_new;
-    m = m_new;
-    float s4[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t pk[kNT / 2];
-#pragma unroll
-    for (int k = 0; k < kNT / 2; ++k) {
-      const float p0 = ex2_approx(x[2 * k] - off), p1 = ex2_approx(x[2 * k + 1] - off);
-      s4[k & 3] += p0 + p1;
-      pk[k] = pack2f<T>(p0, p1);
-    }
-    l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
-    if (j > 0) {
-      // the P buffer and O are free once P V of the previous tile completed
-      wait_phase(B(kBarPvDone), (j - 1) & 1, dead);
-      tc_fence_after();
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-        for (int cc = 0; cc < kD; cc += 32) {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_base + kTmemO + cc, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tmem + lane_base + kTmemO + cc, o);
-        }
-        tmem_wait_st();
-      }
-    }
-#pragma unroll
-    for (int kc = 0; kc < kNT / 8; ++kc)
-      *reinterpret_cast<uint4 *>(smem + kOffP + kc * (kM * 16) + r * 16) =
-          make_uint4(pk[4 * kc], pk[4 * kc + 1], pk[4 * kc + 2], pk[4 * kc + 3]);
-    fence_proxy_async_smem();
-    tc_fence_before();
-    named_bar_sync(1, 4 * 32);  // P_j complete, S_j consumed by all four warps
-    if (warp == 0) {
-      tc_fence_after();
+    for (int j = 0; j < n_kt; ++j) {
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
       if (j == n_kt - 1 && (kv_end % kBS) != 0) {
         // V of tokens >= kv_end in the last page holds other data (possibly
@@ -506,18 +441,108 @@ __global__ void __launch_bounds__(kThreads, 2)
         fence_proxy_async_smem();
         __syncwarp();
       }
+      // P of tile j (a ring of two: the softmax warps may run one tile ahead)
+      wait_phase(B(kBarPFull + (j & 1)), (j >> 1) & 1, dead);
+      tc_fence_after();
       if (lane == 0) {
         const int np = min(kPagesPerTile, n_pages - j * kPagesPerTile);
         const uint32_t sv = sbase + kOffV + (j & 1) * kKVTile;
         for (int pg = 0; pg < np; ++pg)
-          umma_f16(tmem + kTmemO, sdesc(sbase + kOffP + pg * 2 * (kM * 16), kM * 16, 128, 0),
-                   sdesc(sv + pg * kPageBytes, 16, 256, 6), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * kNT + pg * (kBS / 2),
+                      sdesc(sv + pg * kPageBytes, 16, 256, 6), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
         umma_commit(B(kBarEmptyV + (j & 1)));
         umma_commit(B(kBarPvDone));
-        if (j + 2 < n_kt) issue_s(j + 2);
       }
       __syncwarp();
+      if (j + 2 < n_kt) {
+        // Q K^T j + 2 overwrites the S buffer that holds P j: the tensor core
+        // does not order a later MMA's D writes after an earlier MMA's TMEM A
+        // reads, so P V j must have completed first.
+        wait_phase(B(kBarPvDone), j & 1, dead);
+        tc_fence_after();
+        issue_s(j + 2);
+      }
     }
+    // the last P V commit (waited for by the epilogue) covers every MMA issued here
+    tc_fence_before();
+    __syncthreads();
+    return;
+  }
+
+  // ------------------------------------------------- softmax, one row per thread
+  const int r = tid;
+  const bool row_ok = (r / G) < n_pos;
+  const int lim = row_ok ? min(base_pos + r / G, kv_end - 1) : -1;  // last visible key
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const bool use_softcap = (p.softcapping != 1.0f) && (p.softcapping > 0.f);
+  const float cx = use_softcap ? 1.f : p.scale * kLog2e;
+  float m = -INFINITY, l = 0.f;
+  for (int j = 0; j < n_kt; ++j) {
+    wait_phase(B(kBarSFull + (j & 1)), (j >> 1) & 1, dead);
+    tc_fence_after();
+    uint32_t u[kNT];
+    const uint32_t ts = tmem + lane_base + kTmemS + (j & 1) * kNT;
+    tmem_ld32(ts, u);
+    tmem_ld32(ts + 32, u + 32);
+    tmem_wait_ld();
+    const int kmax = lim - j * kNT;  // elements k <= kmax are visible to this row
+    // x holds raw scores (exponent x * c - m) or, with softcapping, log2-domain
+    // capped logits (c = 1); m is kept in log2 units either way.
+    float x[kNT];
+#pragma unroll
+    for (int k = 0; k < kNT; ++k) x[k] = __uint_as_float(u[k]);
+    if (use_softcap) {
+#pragma unroll
+      for (int k = 0; k < kNT; ++k)
+        x[k] = p.softcapping * tanhf(x[k] * p.scale / p.softcapping) * kLog2e;
+    }
+    if (!__all_sync(0xffffffffu, kmax >= kNT - 1)) {  // diagonal / last tile: mask
+#pragma unroll
+      for (int k = 0; k < kNT; ++k) x[k] = (k <= kmax) ? x[k] : -INFINITY;
+    }
+    float m4[4] = {x[0], x[1], x[2], x[3]};
+#pragma unroll
+    for (int k = 4; k < kNT; ++k) m4[k & 3] = fmaxf(m4[k & 3], x[k]);
+    const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * cx;
+    const float m_new = (mx > m + kRescaleLog2) ? mx : m;
+    const float alpha = (m_new == m) ? 1.f : ex2_approx(m - m_new);
+    const float off = (m_new == -INFINITY) ? 0.f : m_new;
+    m = m_new;
+    float s4[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t pk[kNT / 2];
+#pragma unroll
+    for (int k = 0; k < kNT / 2; ++k) {
+      const float p0 = ex2_approx(fmaf(x[2 * k], cx, -off));
+      const float p1 = ex2_approx(fmaf(x[2 * k + 1], cx, -off));
+      s4[k & 3] += p0 + p1;
+      pk[k] = pack2f<T>(p0, p1);
+    }
+    l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+    if (j > 0) {
+      // Wait for P V of the previous tile every tile, also when O needs no
+      // rescale: a parity wait is only exact while the barrier is at most one
+      // phase away, and the epilogue relies on it.
+      wait_phase(B(kBarPvDone), (j - 1) & 1, dead);
+      tc_fence_after();
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int cc = 0; cc < kD; cc += 32) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + kTmemO + cc, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem + lane_base + kTmemO + cc, o);
+        }
+        tmem_wait_st();
+      }
+    }
+    // P (16-bit pairs) replaces the first 32 columns of its S buffer; P V of
+    // the tile two back, which read them last, completed before this S did.
+    tmem_st32(ts, pk);
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(B(kBarPFull + (j & 1)));
   }
 
   // ---- epilogue: O / l -> out (the last P V commit covers every MMA)
