@@ -274,6 +274,58 @@ int32_t vasr_pa_fused_qk_norm_rope_append(
     int64_t num_blocks, int32_t dtype, vasr_pa_stream_t stream);
 
 /*
+ * Device-side decode step bookkeeping (no counterpart call in the reference,
+ * which does this on the host every step; it replaces the host work of
+ * paged_batch_decode_step, vasr-models/src/model/paged_batch_engine.rs:634-712,
+ * with decode_metadata_for_batch_step, vasr-paged-attn/src/paged_kv_cache.rs:
+ * 924-1059, so a captured decode step replays without a host round trip).
+ * For each row b, with step = *step (a device u32):
+ *   - a row not yet finished takes tok = next_ids[b]; tok in eos_ids marks it
+ *     finished (finished[b] = 1); otherwise tok is recorded
+ *     (history[b * history_cols + generated[b]] when there is room, then
+ *     generated[b] += 1; generated/history may be NULL) and the row gets
+ *     input_ids = tok, positions = prompt_lens[b] + step, slot_mapping =
+ *     block_tables[b][pos / block_size] * block_size + pos % block_size and
+ *     context_lens = pos + 1 (slot_for_block_table_position,
+ *     paged_kv_cache.rs:74-103);
+ *   - a finished row becomes a padding row of pad_decode_batch_to_max
+ *     (cuda_graph.rs:373-486): input 0, position 0, slot 0, context 1.
+ * block_table_lens[b] (may be NULL = all columns valid) is the number of
+ * valid table entries; a position past it gets slot -1 and sets
+ * VASR_PA_DERR_SLOT_RANGE (the host must allocate blocks ahead of the steps
+ * it replays without syncing). Capture-safe.
+ */
+int32_t vasr_pa_decode_step_prepare(
+    const uint32_t *next_ids, const uint32_t *eos_ids, int32_t num_eos,
+    const uint32_t *prompt_lens, const uint32_t *step,
+    const uint32_t *block_tables, const uint32_t *block_table_lens,
+    int32_t max_num_blocks_per_seq, int32_t block_size, int64_t num_blocks,
+    int32_t num_seqs, uint8_t *finished, uint32_t *generated,
+    uint32_t *history, int32_t history_cols, int64_t *input_ids,
+    int64_t *positions, int64_t *slot_mapping, uint32_t *context_lens,
+    vasr_pa_stream_t stream);
+
+/*
+ * Greedy next tokens on the device: next_ids[b] = argmax over v < vocab of
+ * logits[b * row_stride + v] (argmax_token_ids_from_logits,
+ * vasr-models/src/model/generation.rs:443-460; the lowest index among equal
+ * maxima, NaN never wins, a row without a value above -inf gives 0). Rows
+ * with finished[b] != 0 are skipped (finished may be NULL). If step is not
+ * NULL, *step is incremented once (the decode step counter read by
+ * vasr_pa_decode_step_prepare). workspace: at least
+ * vasr_pa_greedy_argmax_workspace_size(num_seqs, vocab) bytes, zeroed once
+ * before first use and left zeroed by every call; one call at a time per
+ * workspace. dtype f32/bf16/f16. Capture-safe.
+ */
+size_t vasr_pa_greedy_argmax_workspace_size(int32_t num_seqs, int64_t vocab);
+int32_t vasr_pa_greedy_argmax(uint32_t *next_ids, const void *logits,
+                              int32_t num_seqs, int64_t vocab,
+                              int64_t row_stride, int32_t dtype,
+                              const uint8_t *finished, uint32_t *step,
+                              void *workspace, size_t workspace_bytes,
+                              vasr_pa_stream_t stream);
+
+/*
  * Read (and optionally clear) the device error word of the current device.
  * Synchronises `stream` because it copies the word to the host; call it
  * outside stream capture.

@@ -499,6 +499,69 @@ def pad_decode_batch_to_max(max_batch, input_ids, slot_mapping, context_lens, bl
 
 
 # =========================================== attention.rs (numpy restatement)
+# ============================================== device decode loop (host restatement)
+def decode_step_prepare(state, eos_ids, block_tables, block_table_lens, block_size, num_blocks):
+    """One decode step's token feedback + metadata, as the reference host loop does it.
+
+    Restates paged_batch_engine.rs:634-676 (a row whose fed token is an EOS id
+    becomes finished; otherwise the token is recorded), the decode metadata of
+    paged_kv_cache.rs:924-1059 (position = prompt_len + step, context =
+    position + 1, slot by slot_for_block_table_position :74-103) and, for
+    finished rows, the padding rows of cuda_graph.rs:373-486 (token 0,
+    position 0, slot 0, context 1). ``state`` holds numpy arrays prompt_lens,
+    next_ids, finished (bool), generated, history [B, cols] and the int
+    ``step``; it is updated in place. Returns (input_ids, positions,
+    slot_mapping, context_lens, slot_errors) where slot_errors counts rows
+    whose table was too short (slot -1 there).
+    """
+    b = len(state["prompt_lens"])
+    ids = np.zeros(b, np.int64)
+    pos = np.zeros(b, np.int64)
+    slots = np.zeros(b, np.int64)
+    ctx = np.ones(b, np.uint32)
+    errors = 0
+    hist = state["history"]
+    for i in range(b):
+        if not state["finished"][i]:
+            tok = int(state["next_ids"][i])
+            if tok in set(int(e) for e in eos_ids):
+                state["finished"][i] = True
+            else:
+                g = int(state["generated"][i])
+                if hist is not None and g < hist.shape[1]:
+                    hist[i, g] = tok
+                state["generated"][i] = g + 1
+                p = int(state["prompt_lens"][i]) + state["step"]
+                n = int(block_table_lens[i]) if block_table_lens is not None else block_tables.shape[1]
+                table = [int(x) for x in block_tables[i, :n]]
+                try:
+                    slots[i] = slot_for_block_table_position([table], block_size, num_blocks, 0, p)
+                except OracleError:
+                    slots[i] = PAD_SLOT_ID
+                    errors += 1
+                ids[i], pos[i], ctx[i] = tok, p, p + 1
+                continue
+        # finished (now or before): padding row
+    return ids, pos, slots, ctx, errors
+
+
+def greedy_argmax(logits, finished=None):
+    """argmax_token_ids_from_logits (generation.rs:443-460): first index of the row maximum.
+
+    NaN never wins and a row without a value above -inf gives 0; rows with
+    finished set are left out (None in the result).
+    """
+    out = []
+    for i, row in enumerate(np.asarray(logits, np.float64)):
+        if finished is not None and finished[i]:
+            out.append(None)
+            continue
+        r = np.where(np.isnan(row), -np.inf, row)
+        m = r.max()
+        out.append(0 if not m > -np.inf else int(np.argmax(r == m)))
+    return out
+
+
 def repeat_kv(x, n_rep):
     """attention.rs:12-21: (b, kvh, s, d) -> (b, kvh * n_rep, s, d), head h <- kv head h // n_rep."""
     if n_rep == 1:

@@ -33,7 +33,7 @@ NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 CUDA_HOME = Path(NVCC).resolve().parent.parent
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_UNITS = ["kv_ops.cu", "decode.cu", "prefill.cu", "capi.cu", "decode_noalloc.cu",
-              "fused_rope.cu", "prefill_umma.cu"]
+              "fused_rope.cu", "prefill_umma.cu", "decode_loop.cu"]
 NVCC_FLAGS = ARCH + [
     "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
     "--expt-relaxed-constexpr", "-I", str(INCLUDE),

@@ -263,6 +263,66 @@ int32_t vasr_pa_fused_qk_norm_rope_append(
   return vasr::launch_fused_rope(a, to_stream(stream));
 }
 
+int32_t vasr_pa_decode_step_prepare(
+    const uint32_t *next_ids, const uint32_t *eos_ids, int32_t num_eos,
+    const uint32_t *prompt_lens, const uint32_t *step, const uint32_t *block_tables,
+    const uint32_t *block_table_lens, int32_t max_num_blocks_per_seq, int32_t block_size,
+    int64_t num_blocks, int32_t num_seqs, uint8_t *finished, uint32_t *generated,
+    uint32_t *history, int32_t history_cols, int64_t *input_ids, int64_t *positions,
+    int64_t *slot_mapping, uint32_t *context_lens, vasr_pa_stream_t stream) {
+  if (num_seqs < 0 || num_eos < 0 || max_num_blocks_per_seq <= 0 || block_size <= 0 ||
+      num_blocks <= 0 || history_cols < 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0) return VASR_PA_OK;
+  if (!next_ids || (num_eos > 0 && !eos_ids) || !prompt_lens || !step || !block_tables ||
+      !finished || !input_ids || !positions || !slot_mapping || !context_lens ||
+      (history && (!generated || history_cols == 0)))
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned(next_ids, 4) || !aligned(eos_ids, 4) || !aligned(prompt_lens, 4) ||
+      !aligned(step, 4) || !aligned(block_tables, 4) || !aligned(block_table_lens, 4) ||
+      !aligned(generated, 4) || !aligned(history, 4) || !aligned(input_ids, 8) ||
+      !aligned(positions, 8) || !aligned(slot_mapping, 8) || !aligned(context_lens, 4))
+    return VASR_PA_EINVAL_ALIGN;
+  vasr::DecodeStepArgs a{next_ids,  eos_ids,   num_eos,      prompt_lens,  step,
+                         block_tables, block_table_lens, max_num_blocks_per_seq, block_size,
+                         num_blocks, num_seqs,  finished,     generated,    history,
+                         history_cols, input_ids, positions,  slot_mapping, context_lens};
+  return vasr::launch_decode_step_prepare(a, to_stream(stream));
+}
+
+size_t vasr_pa_greedy_argmax_workspace_size(int32_t num_seqs, int64_t vocab) {
+  if (num_seqs <= 0 || vocab <= 0) return 0;
+  return vasr::argmax_workspace_bytes(num_seqs, vocab);
+}
+
+int32_t vasr_pa_greedy_argmax(uint32_t *next_ids, const void *logits, int32_t num_seqs,
+                              int64_t vocab, int64_t row_stride, int32_t dtype,
+                              const uint8_t *finished, uint32_t *step, void *workspace,
+                              size_t workspace_bytes, vasr_pa_stream_t stream) {
+  if (dtype != VASR_PA_F32 && dtype != VASR_PA_BF16 && dtype != VASR_PA_F16)
+    return VASR_PA_EINVAL_DTYPE;
+  if (num_seqs < 0 || num_seqs > 65535 || vocab <= 0 || vocab > 0xfffffffeLL ||
+      row_stride < vocab)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0) return VASR_PA_OK;
+  if (!next_ids || !logits || !workspace) return VASR_PA_EINVAL_POINTER;
+  if (workspace_bytes < vasr::argmax_workspace_bytes(num_seqs, vocab))
+    return VASR_PA_EINVAL_WORKSPACE;
+  if (!aligned(next_ids, 4) || !aligned(logits, elem_size(dtype)) || !aligned(step, 4) ||
+      !aligned(workspace, 256))
+    return VASR_PA_EINVAL_ALIGN;
+  vasr::ArgmaxArgs a{};
+  a.next_ids = next_ids;
+  a.logits = logits;
+  a.num_seqs = num_seqs;
+  a.vocab = vocab;
+  a.row_stride = row_stride;
+  a.dtype = dtype;
+  a.finished = finished;
+  a.step = step;
+  return vasr::launch_greedy_argmax(a, workspace, to_stream(stream));
+}
+
 int32_t vasr_pa_get_device_error(int32_t *out_bits, int32_t clear, vasr_pa_stream_t stream) {
   if (!out_bits) return VASR_PA_EINVAL_POINTER;
   uint32_t a = 0, b = 0, c = 0, d = 0, e = 0;
@@ -273,7 +333,9 @@ int32_t vasr_pa_get_device_error(int32_t *out_bits, int32_t clear, vasr_pa_strea
   if ((r = vasr::read_error_fused(&d, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
   if ((r = vasr::read_error_prefill_umma(&e, clear != 0, to_stream(stream))) != VASR_PA_OK)
     return r;
-  *out_bits = (int32_t)(a | b | c | d | e);
+  uint32_t f = 0;
+  if ((r = vasr::read_error_decode_loop(&f, clear != 0, to_stream(stream))) != VASR_PA_OK) return r;
+  *out_bits = (int32_t)(a | b | c | d | e | f);
   return VASR_PA_OK;
 }
 

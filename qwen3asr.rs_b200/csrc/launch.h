@@ -113,6 +113,49 @@ struct FusedRopeArgs {
   int dtype;
 };
 int launch_fused_rope(const FusedRopeArgs &a, cudaStream_t s);
+
+struct DecodeStepArgs {
+  const uint32_t *next_ids;
+  const uint32_t *eos_ids;
+  int num_eos;
+  const uint32_t *prompt_lens;
+  const uint32_t *step;
+  const uint32_t *block_tables;
+  const uint32_t *block_table_lens;  // may be null: every column valid
+  int max_num_blocks_per_seq;
+  int block_size;
+  int64_t num_blocks;
+  int num_seqs;
+  uint8_t *finished;
+  uint32_t *generated;  // may be null
+  uint32_t *history;    // may be null
+  int history_cols;
+  int64_t *input_ids;
+  int64_t *positions;
+  int64_t *slot_mapping;
+  uint32_t *context_lens;
+};
+int launch_decode_step_prepare(const DecodeStepArgs &a, cudaStream_t s);
+
+struct ArgmaxArgs {
+  uint32_t *next_ids;
+  const void *logits;
+  int num_seqs;
+  int64_t vocab;
+  int64_t row_stride;
+  int dtype;
+  const uint8_t *finished;  // may be null
+  uint32_t *step;           // may be null: incremented once per call
+  // filled by launch_greedy_argmax
+  int num_chunks;
+  int64_t chunk_elems;
+  uint32_t *counters;
+  void *partials;
+};
+void argmax_chunking(int64_t vocab, int *num_chunks, int64_t *chunk_elems);
+size_t argmax_workspace_bytes(int num_seqs, int64_t vocab);
+int launch_greedy_argmax(ArgmaxArgs a, void *workspace, cudaStream_t s);
+int read_error_decode_loop(uint32_t *bits, bool clear, cudaStream_t s);
 int read_error_fused(uint32_t *bits, bool clear, cudaStream_t s);
 
 // Workspace layout of the decode kernel (all offsets 256-byte aligned):

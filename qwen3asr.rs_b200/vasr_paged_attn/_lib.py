@@ -87,6 +87,18 @@ SIGNATURES: dict[str, tuple] = {
          _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _i64, _i32,
          _c_void_p],
     ),
+    "vasr_pa_decode_step_prepare": (
+        _i32,
+        [_c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i64,
+         _i32, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _c_void_p],
+    ),
+    "vasr_pa_greedy_argmax_workspace_size": (_size, [_i32, _i64]),
+    "vasr_pa_greedy_argmax": (
+        _i32,
+        [_c_void_p, _c_void_p, _i32, _i64, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _size,
+         _c_void_p],
+    ),
 }
 
 

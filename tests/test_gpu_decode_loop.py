@@ -1,0 +1,163 @@
+"""Device decode loop: greedy argmax and step prepare against the oracle's host restatement.
+
+Integer outputs (token ids, positions, slots, context lengths, finished
+flags, histories) must match exactly.
+"""
+import numpy as np
+import pytest
+import torch
+
+import paged_ref as ref
+from vasr_paged_attn import _lib
+from vasr_paged_attn import decode_loop as dl
+from vasr_paged_attn import mistralrs_paged_attn as pa
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _clear(cuda_device):
+    pa.device_error(clear=True)
+    yield
+
+
+def _logits(rng, b, vocab, dtype, dev):
+    x = rng.standard_normal((b, vocab)).astype(np.float32)
+    # planted ties: the same maximum twice, the lower index must win
+    for i in range(0, b, 3):
+        j, k = sorted(rng.choice(vocab, 2, replace=False))
+        x[i, j] = x[i, k] = 50.0
+    if b > 4:
+        x[1, :] = np.nan                # all NaN -> 0
+        x[2, :] = -np.inf               # no value above -inf -> 0
+        x[4, rng.integers(0, vocab, 5)] = np.nan
+    t = torch.from_numpy(x).to(dtype)
+    return t.to(dev), t.float().numpy()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("vocab", [151936, 1000, 7])
+def test_greedy_argmax_matches_first_index(cuda_device, dtype, vocab):
+    rng = np.random.default_rng(vocab)
+    b = 37
+    lg, host = _logits(rng, b, vocab, dtype, cuda_device)
+    got = dl.greedy_argmax(lg).cpu().numpy()
+    exp = ref.greedy_argmax(host)
+    assert got.tolist() == exp
+    assert pa.device_error() == 0
+
+
+def test_greedy_argmax_strided_rows_finished_and_step(cuda_device):
+    rng = np.random.default_rng(5)
+    b, vocab, stride = 19, 5003, 5011  # odd stride: the scalar (non-vector) path
+    base = torch.from_numpy(rng.standard_normal((b, stride)).astype(np.float32)).to(torch.bfloat16)
+    lg = base.to(cuda_device)[:, :vocab]
+    fin = np.zeros(b, np.uint8)
+    fin[[0, 7, 18]] = 1
+    out = torch.full((b,), -5, dtype=torch.int32, device=cuda_device)
+    step = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ws = torch.zeros(dl.greedy_argmax_workspace_bytes(b, vocab), dtype=torch.uint8, device=cuda_device)
+    for call in range(3):  # the workspace counters reset themselves
+        dl.greedy_argmax(lg, out=out, finished=torch.from_numpy(fin).to(cuda_device), step=step, workspace=ws)
+        exp = ref.greedy_argmax(base[:, :vocab].float().numpy(), fin)
+        got = out.cpu().numpy()
+        for i, e in enumerate(exp):
+            assert got[i] == (-5 if e is None else e)
+        assert int(step.item()) == call + 1
+    assert int(ws.view(torch.int32)[:b].abs().sum().item()) == 0
+
+
+def test_greedy_argmax_rejects_bad_arguments(cuda_device):
+    lg = torch.zeros(4, 100, device=cuda_device)
+    ws = torch.zeros(16, dtype=torch.uint8, device=cuda_device)
+    with pytest.raises(_lib.VasrPaError):
+        dl.greedy_argmax(lg, workspace=ws)  # workspace too small
+    with pytest.raises(_lib.VasrPaError):
+        dl.greedy_argmax(lg.to(torch.int32))  # dtype
+
+
+def _loop_case(rng, b, bs, cols, short_row=None):
+    prompt = rng.integers(1, 40, b)
+    need = (prompt + 30 + bs - 1) // bs
+    nb = int(need.sum()) + 2
+    perm = rng.permutation(np.arange(1, nb))
+    tables = np.zeros((b, cols), np.int32)
+    lens = need.copy()
+    o = 0
+    for i in range(b):
+        n = int(need[i])
+        tables[i, :n] = perm[o:o + n]
+        o += n
+    if short_row is not None:
+        lens[short_row] = (prompt[short_row] + 2) // bs + 1  # runs out after a few steps
+    return prompt, tables, lens, nb
+
+
+@pytest.mark.parametrize("bs", [16, 8])
+def test_decode_step_prepare_matches_host_loop(cuda_device, bs):
+    rng = np.random.default_rng(bs)
+    b, cols, steps, vocab = 9, 12, 24, 50
+    eos = [3, 17]
+    prompt, tables, lens, nb = _loop_case(rng, b, bs, cols)
+    first = rng.integers(20, vocab, b)
+    st = dl.DecodeLoopState(prompt.tolist(), first.tolist(), eos, torch.from_numpy(tables).to(cuda_device),
+                            lens.tolist(), bs, nb, vocab, history_cols=16, device=cuda_device)
+    host = {"prompt_lens": prompt, "next_ids": first.copy(), "finished": np.zeros(b, bool),
+            "generated": np.zeros(b, np.int64), "history": np.zeros((b, 16), np.int64), "step": 0}
+    for step in range(steps):
+        st.prepare()
+        ids, pos, slots, ctx, errs = ref.decode_step_prepare(host, eos, tables, lens, bs, nb)
+        assert errs == 0
+        assert st.input_ids.cpu().numpy().tolist() == ids.tolist()
+        assert st.positions.cpu().numpy().tolist() == pos.tolist()
+        assert st.slot_mapping.cpu().numpy().tolist() == slots.tolist()
+        assert st.context_lens.cpu().numpy().astype(np.uint32).tolist() == ctx.tolist()
+        assert st.finished.cpu().numpy().astype(bool).tolist() == host["finished"].tolist()
+        # next tokens: random, with EOS now and then
+        nxt = rng.integers(20, vocab, b)
+        nxt[rng.random(b) < 0.08] = eos[step % 2]
+        st.next_ids.copy_(torch.from_numpy(nxt.astype(np.int32)))
+        host["next_ids"] = nxt
+        st.step += 1
+        host["step"] += 1
+    fin, gen, hist = st.read_back()
+    assert fin.numpy().tolist() == host["finished"].tolist()
+    assert gen.numpy().tolist() == host["generated"].tolist()
+    assert hist.numpy().tolist() == host["history"].tolist()
+    assert pa.device_error() == 0
+
+
+def test_decode_step_prepare_slots_match_reference_metadata(cuda_device):
+    """Without EOS the prepared metadata equals decode_metadata_for_batch_step of the host mirror."""
+    from vasr_paged_attn import host as vh
+    g_tables, g_prompt = [[3, 4], [6, 7]], [4, 5]  # paged_kv_cache.rs:1316-1376 golden case
+    cache = vh.golden_api().new_pool(1, 2, 8, 4, 16, "f32")
+    t = torch.tensor([r + [0] * 2 for r in g_tables], dtype=torch.int32)
+    st = dl.DecodeLoopState(g_prompt, [100, 101], [0], t.to(cuda_device), [2, 2], 4, 16, 200,
+                            device=cuda_device)
+    for step in range(3):
+        st.prepare()
+        m = cache.decode_metadata_for_batch_step(g_tables, g_prompt, step, False)
+        assert st.slot_mapping.cpu().tolist() == list(m.slot_mapping)
+        assert st.context_lens.cpu().tolist() == list(m.context_lens)
+        st.step += 1
+
+
+def test_decode_step_prepare_flags_short_tables(cuda_device):
+    rng = np.random.default_rng(2)
+    b, bs, cols = 5, 16, 8
+    prompt, tables, lens, nb = _loop_case(rng, b, bs, cols, short_row=2)
+    st = dl.DecodeLoopState(prompt.tolist(), [40] * b, [1], torch.from_numpy(tables).to(cuda_device),
+                            lens.tolist(), bs, nb, 64, device=cuda_device)
+    host = {"prompt_lens": prompt, "next_ids": np.full(b, 40), "finished": np.zeros(b, bool),
+            "generated": np.zeros(b, np.int64), "history": None, "step": 0}
+    total_errs = 0
+    for step in range(40):
+        st.prepare()
+        _, _, slots, _, errs = ref.decode_step_prepare(host, [1], tables, lens, bs, nb)
+        total_errs += errs
+        assert st.slot_mapping.cpu().numpy().tolist() == slots.tolist()
+        st.step += 1
+        host["step"] += 1
+    assert total_errs > 0
+    assert pa.device_error(clear=True) & _lib.DERR_SLOT_RANGE

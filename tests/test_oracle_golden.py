@@ -388,3 +388,38 @@ def test_c_oracle_reshape_and_cache_layout():
                 assert kc[s // bs, hh, dd // 4, s % bs, dd % 4] == key[t, hh, dd]
                 assert vc[s // bs, hh, dd, s % bs] == val[t, hh, dd]
     assert np.count_nonzero(kc) == 4 * h * d
+
+
+def test_decode_step_prepare_oracle_matches_batch_step_metadata(api):
+    """The device loop's host restatement reproduces decode_metadata_for_batch_step
+    (paged_kv_cache.rs:1316-1376 golden case) while no row has finished."""
+    g = GOLD["decode_batch_steps"]
+    c = api.new_pool(*g["new_pool"])
+    tables = np.array([t + [0] * 2 for t in g["block_tables"]], np.int64)
+    state = {"prompt_lens": np.array(g["prompt_lens"]), "next_ids": np.array([7, 8]),
+             "finished": np.zeros(2, bool), "generated": np.zeros(2, np.int64),
+             "history": np.zeros((2, 4), np.int64), "step": 0}
+    for step in range(g["steps"]):
+        ids, pos, slots, ctx, errs = ref.decode_step_prepare(state, [0], tables, [2, 2], c.block_size,
+                                                             g["new_pool"][4])
+        m = c.decode_metadata_for_batch_step(g["block_tables"], g["prompt_lens"], step, False)
+        assert errs == 0
+        assert slots.tolist() == list(m.slot_mapping)
+        assert ctx.tolist() == list(m.context_lens)
+        assert pos.tolist() == [p + step for p in g["prompt_lens"]]
+        state["step"] += 1
+    assert state["history"][:, :3].tolist() == [[7, 7, 7], [8, 8, 8]]
+
+
+def test_decode_step_prepare_oracle_finished_rows_are_graph_padding():
+    """A row fed an EOS id turns into the padding row of pad_decode_batch_to_max
+    (cuda_graph.rs:690-763 golden case: id 0, slot 0, context 1)."""
+    g = GOLD["pad_decode_batch"]
+    state = {"prompt_lens": np.array([5, 6, 7]), "next_ids": np.array([11, 2, 33]),
+             "finished": np.zeros(3, bool), "generated": np.zeros(3, np.int64), "history": None, "step": 0}
+    tables = np.array(g["block_tables"], np.int64)
+    ids, pos, slots, ctx, _ = ref.decode_step_prepare(state, [2], tables, None, 16, 64)
+    assert state["finished"].tolist() == [False, True, False]
+    pad_ids = g["ids_out"][len(g["input_ids"]):]
+    assert (ids[1], slots[1], ctx[1]) == (pad_ids[0], g["slots_out"][-1], g["context_lens_out"][-1])
+    assert pos[1] == 0
