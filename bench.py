@@ -16,6 +16,9 @@ the reference (vasr-paged-attn/src/cuda_graph.rs).
              replays, and reads the next token ids back (synchronising).
   roofline   the paged decode kernel alone: algorithmic KV bytes per launch
              / CUDA-event launch time vs the measured HBM copy bandwidth.
+  device_loop  tokens/s of the device-side decode loop: step prepare (token
+             feedback, EOS state, metadata) + the 28 layers + greedy argmax
+             captured as one graph and replayed back to back.
 
 Multi-GPU (torchrun): request-level data parallelism, each rank holds its own
 decoder replica and page pool and decodes its own 64 sequences (weak
@@ -256,7 +259,7 @@ def run_ours(args):
     cfg = eng.DecoderConfig.qwen3_asr_0_6b()
     model = eng.RandomQwen3Decoder(cfg, dev, torch.bfloat16, seed=args.seed)
     k_steps, w_steps = args.steps, max(3, args.warmup)
-    total_steps = 2 * (w_steps + k_steps) + 2  # device loop + e2e loop
+    total_steps = 3 * (w_steps + k_steps) + 2  # device-resident, e2e and device-loop runs
     lens0 = context_lens(args.seed, rank)
     need_tok = lens0 + total_steps
     blocks = np.array([-(-int(n) // BLOCK_SIZE) for n in need_tok])
@@ -381,6 +384,31 @@ def run_ours(args):
            h_tables.numel() * 4)
     d2h = h_next.numel() * 8
 
+    # ---- device decode loop: prepare -> forward -> argmax replayed with no host round trip
+    from vasr_paged_attn import decode_loop as dloop
+    loop_state = dloop.DecodeLoopState(
+        [int(x) + s_idx for x in lens0], [0] * BATCH, [cfg.vocab_size],  # EOS id outside the vocab:
+        torch.from_numpy(tables).to(dev), blocks.tolist(), BLOCK_SIZE, nb,  # every row stays active
+        cfg.vocab_size, device=dev)
+    loop = eng.DecodeLoopGraph(model, caches, loop_state, BLOCK_SIZE)
+    loop.capture()
+    for _ in range(w_steps):
+        loop.replay()
+    torch.cuda.synchronize()
+    barrier()
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0.record()
+    for _ in range(k_steps):
+        loop.replay()
+    l1.record()
+    torch.cuda.synchronize()
+    loop_ms = max_over_ranks(l0.elapsed_time(l1))
+    barrier()
+    fin, gen_counts, _ = loop_state.read_back()
+    loop_value = world * BATCH * k_steps / (loop_ms / 1e3)
+    s_idx += w_steps + k_steps
+    loop.release()
+
     # ---- roofline of the paged decode kernel: one launch per layer, events on its stream
     last = s_idx - 1
     ctx_last = torch.from_numpy(ctx[min(last, total_steps - 1)]).to(dev)
@@ -435,6 +463,11 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": 2 * cfg.num_layers * k_steps,
+            "device_loop": {"value": loop_value, "unit": "tok/s", "ms_per_step": loop_ms / k_steps,
+                            "note": "decode_step_prepare + 28 layers + greedy_argmax captured as one "
+                                    "graph and replayed back to back: next ids, EOS state and metadata "
+                                    "stay on the device (no per-step host round trip)",
+                            "rows_active_at_end": int((~fin).sum()), "tokens_generated": int(gen_counts.sum())},
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

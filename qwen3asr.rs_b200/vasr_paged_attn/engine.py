@@ -115,8 +115,10 @@ class RandomQwen3Decoder:
     def decode_step(self, input_ids: torch.Tensor, positions: torch.Tensor, kv_caches,
                     slot_mapping: torch.Tensor, block_tables: torch.Tensor,
                     context_lens: torch.Tensor, max_context_len: int,
-                    next_ids_out: Optional[torch.Tensor] = None, fused: bool = True) -> torch.Tensor:
-        """One token per sequence through all layers; returns greedy next ids [B] (int64).
+                    next_ids_out: Optional[torch.Tensor] = None, fused: bool = True,
+                    return_logits: bool = False) -> torch.Tensor:
+        """One token per sequence through all layers; returns greedy next ids [B] (int64),
+        or the logits [B, vocab] with ``return_logits`` (for the device-side argmax).
 
         ``fused`` runs q/k RMSNorm + RoPE + KV append as one kernel
         (vasr_pa_fused_qk_norm_rope_append); ``fused=False`` runs the same math
@@ -155,6 +157,8 @@ class RandomQwen3Decoder:
             x = x + (F.silu(gate) * up) @ l["w_down"].t()
         x = F.rms_norm(x, (cfg.hidden_size,), self.final_norm, cfg.rms_norm_eps)
         logits = x @ self.embed.t()
+        if return_logits:
+            return logits
         nxt = torch.argmax(logits, dim=-1)
         if next_ids_out is not None:
             next_ids_out.copy_(nxt)
@@ -226,6 +230,61 @@ class DecodeGraph:
         assert self.graph is not None, "capture() first"
         self.graph.replay()
         return self.next_ids
+
+    def release(self) -> None:
+        self.graph = None
+
+
+class DecodeLoopGraph:
+    """A captured decode step whose inputs come from the previous step on the device.
+
+    prepare (token feedback, EOS state, decode metadata) → 28 layers →
+    greedy argmax, all in one CUDA graph over a ``DecodeLoopState``: replaying
+    it K times decodes K tokens per sequence with no host round trip — the
+    device-side version of paged_batch_decode_step's host loop
+    (vasr-models/src/model/paged_batch_engine.rs:609-730) and of the per-step
+    argmax sync it documents as the dominant decode cost.
+    """
+
+    def __init__(self, model: RandomQwen3Decoder, kv_caches, state, block_size: int):
+        self.model, self.kv_caches, self.state = model, kv_caches, state
+        self.block_size = block_size
+        self.max_context_len = int(state.block_tables.shape[1]) * block_size
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.stream = torch.cuda.Stream(device=model.device)
+
+    def _forward(self):
+        st = self.state
+        st.prepare()
+        logits = self.model.decode_step(st.input_ids, st.positions, self.kv_caches, st.slot_mapping,
+                                        st.block_tables, st.context_lens, self.max_context_len,
+                                        return_logits=True)
+        st.argmax(logits)
+
+    def capture(self) -> None:
+        cfg = self.model.cfg
+        st = self.state
+        need = pa.paged_attention_workspace_bytes(st.num_seqs, cfg.num_heads, cfg.num_kv_heads,
+                                                  cfg.head_dim, self.block_size, self.max_context_len,
+                                                  self.model.dtype)
+        saved = {k: getattr(st, k).clone() for k in ("next_ids", "step", "finished", "generated", "history")}
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):
+            pa.reserve_paged_attention_workspace(self.model.device, need, self.stream)
+            self._forward()  # eager warm-up; its state changes are undone below
+            self.stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self._forward()
+            for k, v in saved.items():
+                getattr(st, k).copy_(v)
+            self.stream.synchronize()
+        torch.cuda.current_stream().wait_stream(self.stream)
+        self.graph = g
+
+    def replay(self) -> None:
+        assert self.graph is not None, "capture() first"
+        self.graph.replay()
 
     def release(self) -> None:
         self.graph = None

@@ -161,3 +161,67 @@ def test_decode_step_prepare_flags_short_tables(cuda_device):
         host["step"] += 1
     assert total_errs > 0
     assert pa.device_error(clear=True) & _lib.DERR_SLOT_RANGE
+
+
+def test_device_loop_graph_matches_host_driven_decode(cuda_device):
+    """K replays of the captured prepare → forward → argmax graph generate the same tokens,
+    EOS handling included, as the host-driven loop (host metadata + torch.argmax per step)."""
+    from vasr_paged_attn import engine as eng
+    cfg = eng.DecoderConfig(num_layers=2, vocab_size=4096)
+    model = eng.RandomQwen3Decoder(cfg, cuda_device, torch.bfloat16, seed=3)
+    rng = np.random.default_rng(11)
+    b, bs, steps = 6, 16, 12
+    prompt = rng.integers(5, 60, b)
+    blocks = (prompt + steps + bs) // bs
+    nb = int(blocks.sum()) + 1
+    cols = int(blocks.max())
+    perm = rng.permutation(np.arange(1, nb))
+    tables = np.zeros((b, cols), np.int32)
+    o = 0
+    for i, n in enumerate(blocks):
+        tables[i, :n] = perm[o:o + n]
+        o += n
+    first = rng.integers(0, cfg.vocab_size, b)
+
+    def fresh_caches():
+        caches = eng.allocate_paged_cache(cfg, nb, bs, cuda_device)
+        g = torch.Generator(device=cuda_device).manual_seed(5)
+        for kc, vc in caches:
+            kc.normal_(generator=g)
+            vc.normal_(generator=g)
+        return caches
+
+    # host-driven reference run; its step-3 token of row 1 becomes an EOS id
+    caches = fresh_caches()
+    dt = torch.from_numpy(tables).to(cuda_device)
+    ids = torch.from_numpy(first).to(cuda_device)
+    host_tokens = []
+    for s in range(steps):
+        pos = torch.from_numpy(prompt + s).to(cuda_device)
+        slots = torch.from_numpy((tables[np.arange(b), (prompt + s) // bs].astype(np.int64) * bs
+                                  + (prompt + s) % bs)).to(cuda_device)
+        ctx = torch.from_numpy((prompt + s + 1).astype(np.int32)).to(cuda_device)
+        ids = model.decode_step(ids, pos, caches, slots, dt, ctx, cols * bs)
+        host_tokens.append(ids.cpu().numpy().copy())
+    host_tokens = np.stack(host_tokens, 1)  # [B, steps]
+    eos = int(host_tokens[1, 3])
+
+    caches = fresh_caches()
+    st = dl.DecodeLoopState(prompt.tolist(), first.tolist(), [eos], dt, blocks.tolist(), bs, nb,
+                            cfg.vocab_size, history_cols=steps + 1, device=cuda_device)
+    loop = eng.DecodeLoopGraph(model, caches, st, bs)
+    loop.capture()
+    for _ in range(steps):
+        loop.replay()
+    fin, gen, hist = st.read_back()
+    loop.release()
+    # history[:, 0] is the first fed token; history[:, s + 1] is the token generated at step s
+    for i in range(b):
+        fed = [int(first[i])] + [int(t) for t in host_tokens[i]]
+        if eos in fed[:steps]:
+            cut = fed.index(eos)
+            assert bool(fin[i]) and int(gen[i]) == cut
+            assert hist[i, :cut].tolist() == fed[:cut]
+        else:
+            assert not bool(fin[i]) and int(gen[i]) == steps
+            assert hist[i, :steps].tolist() == fed[:steps]
