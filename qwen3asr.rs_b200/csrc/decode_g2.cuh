@@ -14,6 +14,10 @@
 
 #include "decode.cuh"
 
+#ifndef VASR_DECODE_BALANCED
+#define VASR_DECODE_BALANCED 1  // share a sequence's pages evenly among its splits
+#endif
+
 namespace vasr {
 
 template <typename T, int BS, int D, int NST>
@@ -51,15 +55,15 @@ struct DecodeG2Cfg {
   static_assert(D % (4 * kRPP) == 0, "head_dim not covered by PV lanes");
 };
 
-template <typename T, int BS, int D, int NST, int MINB>
-__global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const DecodeParams p) {
+// One work item: (split, kv head, sequence). `ubase` = stage-ring units this
+// CTA consumed before (the ring's barriers keep counting across items);
+// returns the units consumed here. The barriers are initialised by the caller.
+template <typename T, int BS, int D, int NST>
+__device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsigned char *smem,
+                                                   const int split, const int kvh, const int b,
+                                                   const uint32_t ubase) {
   using C = DecodeG2Cfg<T, BS, D, NST>;
   constexpr int G = 2;
-  extern __shared__ __align__(128) unsigned char smem[];
-
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y;
-  const int b = blockIdx.z;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -83,12 +87,23 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
   if (ctx <= 0) {
     if (split == 0)
       for (int e = tid; e < G * D; e += C::kThreads) out[e] = Elem<T>::from_f32(0.f);
-    return;
+    return 0;
   }
   const int n_splits = (ctx + P - 1) / P;
-  if (split >= n_splits) return;
-  const int tok_begin = split * P;
-  const int tok_end = min(ctx, tok_begin + P);
+  if (split >= n_splits) return 0;
+#if VASR_DECODE_BALANCED
+  // Balanced splits: the sequence's pages are shared evenly by its splits
+  // (every CTA of a sequence gets the same work), instead of full splits plus
+  // a short last one; CTA durations vary less, which shortens the tail.
+  const int seq_pages = (ctx + BS - 1) / BS;
+  const int per = (seq_pages + n_splits - 1) / n_splits;
+  const int page_begin = split * per;
+#else
+  const int per = p.pages_per_split;
+  const int page_begin = split * p.pages_per_split;
+#endif
+  const int tok_begin = page_begin * BS;
+  const int tok_end = min(ctx, tok_begin + per * BS);
   const int n_pages = (tok_end - tok_begin + BS - 1) / BS;
   const int n_units = (n_pages + C::kSP - 1) / C::kSP;
 
@@ -97,22 +112,22 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
   float *p_s = reinterpret_cast<float *>(smem + C::kOffP);
 
   if (tid < n_pages) {
-    uint32_t id = spec_id;  // == block_tables[b * cols + tok_begin / BS + tid]
+    uint32_t id = spec_id;  // == block_tables[b * cols + tok_begin / BS + tid] when the starts agree
+    if (page_begin != split * p.pages_per_split)
+      id = __ldg(p.block_tables + (int64_t)b * p.cols + page_begin + tid);
     if ((int64_t)id >= p.num_blocks) {
       raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
       id = 0;
     }
     blk[tid] = id;
   }
-  if (tid < C::kNST) mbar_init(s_base + C::kOffBar + tid * 8, 1);
-  if (tid == 0) mbar_fence_init();
   __syncthreads();
 
   const T *kc = reinterpret_cast<const T *>(p.k_cache);
   const T *vc = reinterpret_cast<const T *>(p.v_cache);
   const int64_t page_elems = (int64_t)D * BS;
   auto issue_unit = [&](int u) {
-    const int s = u % C::kNST;
+    const int s = (ubase + u) % C::kNST;
     const int pg0 = u * C::kSP;
     const int np = min(C::kSP, n_pages - pg0);
     const uint32_t bar = s_base + C::kOffBar + s * 8;
@@ -123,8 +138,10 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
       bulk_g2s(s_base + C::kOffV + (s * C::kSP + i) * C::kPB, vc + off, C::kPB, bar);
     }
   };
-  if (lane == 0)
+  if (lane == 0) {
+    fence_proxy_async_smem();  // the previous item's generic reads of the ring come first
     for (int u = warp; u < min(C::kNST, n_units); u += C::kWarps) issue_unit(u);
+  }
 
   // ---- query quarter of both heads: lane (t8, qtr) holds dims [qtr*D/4, +D/4)
   const int t8 = lane & 7;
@@ -164,9 +181,9 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
   float *p_w = p_s + warp * G * C::kST;
 
   for (int u = warp; u < n_units; u += C::kWarps) {
-    const int s = u % C::kNST;
+    const int s = (ubase + u) % C::kNST;
     const uint32_t bar = s_base + C::kOffBar + s * 8;
-    if (!mbar_wait_bounded(bar, (uint32_t)((u / C::kNST) & 1))) {
+    if (!mbar_wait_bounded(bar, (uint32_t)(((ubase + u) / C::kNST) & 1))) {
       aborted = true;
       break;
     }
@@ -359,7 +376,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
       if (d == 0) p.ws_ml[slot * G + g] = make_float2(M, L);
     }
   }
-  if (single) return;
+  if (single) return (uint32_t)n_units;
 
   __syncthreads();
   uint32_t *flag = reinterpret_cast<uint32_t *>(smem + C::kOffFlag);
@@ -370,7 +387,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
     flag[0] = (prev == (uint32_t)(n_splits - 1)) ? 1u : 0u;
   }
   __syncthreads();
-  if (flag[0] == 0u) return;
+  if (flag[0] == 0u) return (uint32_t)n_units;
 #pragma unroll
   for (int e0 = 0; e0 < G * D; e0 += C::kThreads) {
     const int e = e0 + tid;
@@ -391,6 +408,23 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const Decode
     out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L : 0.f);
   }
   if (tid == 0) p.counters[bk] = 0u;
+  return (uint32_t)n_units;
+}
+
+template <typename T, int BS, int D, int NST>
+__device__ __forceinline__ void decode_g2_init_ring(unsigned char *smem) {
+  using C = DecodeG2Cfg<T, BS, D, NST>;
+  if (threadIdx.x < C::kNST) mbar_init(smem_addr(smem) + C::kOffBar + threadIdx.x * 8, 1);
+  if (threadIdx.x == 0) mbar_fence_init();
+  __syncthreads();
+}
+
+// Grid form: one CTA per (split, kv head, sequence).
+template <typename T, int BS, int D, int NST, int MINB>
+__global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const DecodeParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  decode_g2_init_ring<T, BS, D, NST>(smem);
+  decode_g2_item<T, BS, D, NST>(p, smem, blockIdx.x, blockIdx.y, blockIdx.z, 0);
 }
 
 }  // namespace vasr
