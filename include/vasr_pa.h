@@ -39,11 +39,13 @@ typedef struct CUstream_st *vasr_pa_stream_t;
 
 #define VASR_PA_ABI_VERSION 1
 
-/* Element types of q, k, v and the caches (candle DType names). */
+/* Element types of q, k, v and the caches (candle DType names).
+ * VASR_PA_FP8_E4M3 is a cache storage type only (the _fp8 entry points). */
 typedef enum vasr_pa_dtype {
   VASR_PA_F32 = 0,
   VASR_PA_BF16 = 1,
-  VASR_PA_F16 = 2
+  VASR_PA_F16 = 2,
+  VASR_PA_FP8_E4M3 = 3
 } vasr_pa_dtype;
 
 typedef enum vasr_pa_status {
@@ -272,6 +274,42 @@ int32_t vasr_pa_fused_qk_norm_rope_append(
     const int64_t *slot_mapping, int64_t num_tokens, int32_t num_heads,
     int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
     int64_t num_blocks, int32_t dtype, vasr_pa_stream_t stream);
+
+/*
+ * fp8 (E4M3) KV cache with per-tensor scales — the k_scale / v_scale
+ * arguments that reshape_and_cache and paged_attention carry in the
+ * reference API (thinker_text.rs:23-28, 586-590; the Metal fp8 path,
+ * metal/varlen_prefill.rs:276-288). Pages keep the same layout with one
+ * byte per element: K [nb, Hkv, D/16, bs, 16], V [nb, Hkv, D, bs].
+ *
+ * reshape_and_cache_fp8: key/value of element type src_dtype (f32, bf16,
+ * f16) are stored as fp8(value / scale), rounded to nearest even and
+ * saturated to +-448 (NaN stays NaN); k_scale / v_scale are device f32
+ * scalars (required). Otherwise as vasr_pa_reshape_and_cache.
+ */
+int32_t vasr_pa_reshape_and_cache_fp8(
+    const void *key, const void *value, void *key_cache, void *value_cache,
+    const int64_t *slot_mapping, int64_t num_tokens, int32_t num_kv_heads,
+    int32_t head_dim, int32_t block_size, int64_t num_blocks,
+    int64_t key_token_stride, int64_t value_token_stride, int32_t src_dtype,
+    const float *k_scale, const float *v_scale, vasr_pa_stream_t stream);
+
+/*
+ * paged_attention_fp8: decode attention of bf16 / f16 queries (dtype) over
+ * fp8 pages; scores use K = stored * k_scale and the output V = stored *
+ * v_scale. GQA group 2, head_dim 128 (the Qwen3-ASR shape); other shapes
+ * return VASR_PA_ENOT_SUPPORTED. Workspace as vasr_pa_paged_attention.
+ */
+int32_t vasr_pa_paged_attention_fp8(
+    void *out, const void *query, const void *key_cache,
+    const void *value_cache, const uint32_t *block_tables,
+    const uint32_t *context_lens, int32_t num_seqs, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int64_t num_blocks, int32_t max_num_blocks_per_seq,
+    int32_t max_context_len, float scale, float softcapping,
+    int64_t q_seq_stride, int32_t dtype, const float *k_scale,
+    const float *v_scale, void *workspace, size_t workspace_bytes,
+    vasr_pa_stream_t stream);
 
 /*
  * Device-side decode step bookkeeping (no counterpart call in the reference,

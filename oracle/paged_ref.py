@@ -499,6 +499,57 @@ def pad_decode_batch_to_max(max_batch, input_ids, slot_mapping, context_lens, bl
 
 
 # =========================================== attention.rs (numpy restatement)
+# ================================================ fp8 E4M3 (OCP "e4m3fn") pages
+def _fp8_table():
+    """Values of the bytes 0x00..0x7E: sign 0, 4-bit exponent (bias 7), 3-bit
+    mantissa; exponent 0 is subnormal (m/8 * 2^-6); 0x7F is NaN (no infinities)."""
+    vals = []
+    for b in range(0x7F):
+        e, m = b >> 3, b & 7
+        vals.append((m / 8.0) * 2.0 ** -6 if e == 0 else (1 + m / 8.0) * 2.0 ** (e - 7))
+    return np.array(vals, np.float64)
+
+
+_FP8_POS = _fp8_table()
+
+
+def fp8_e4m3_decode(b) -> np.ndarray:
+    """Bytes -> f32 values (NaN for 0x7F / 0xFF)."""
+    b = np.asarray(b, np.uint8)
+    mag = b & 0x7F
+    v = np.where(mag == 0x7F, np.nan, _FP8_POS[np.minimum(mag, 0x7E)])
+    return np.where(b & 0x80, -v, v).astype(np.float32)
+
+
+def fp8_e4m3_encode(x) -> np.ndarray:
+    """f32 -> bytes, round to nearest (ties to the even mantissa), magnitudes
+    above the largest finite value (448) saturate to it, NaN -> 0x7F."""
+    x = np.asarray(x, np.float32)
+    a = np.abs(x.astype(np.float64))
+    hi = np.clip(np.searchsorted(_FP8_POS, a, side="left"), 0, 0x7E)  # first value >= a
+    lo = np.maximum(hi - 1, 0)
+    d_hi, d_lo = _FP8_POS[hi] - a, a - _FP8_POS[lo]
+    pick_lo = (d_lo < d_hi) | ((d_lo == d_hi) & (lo % 2 == 0))
+    code = np.where(pick_lo, lo, hi)
+    code = np.where(a >= _FP8_POS[-1], 0x7E, code)
+    code = np.where(np.isnan(x), 0x7F, code).astype(np.uint8)
+    return np.where(np.signbit(x), code | 0x80, code).astype(np.uint8)
+
+
+def reshape_and_cache_fp8(key, value, key_cache, value_cache, slots, block_size, k_scale, v_scale):
+    """The fp8 append: cache byte = encode(value / scale) in f32 (IEEE division)."""
+    kq = fp8_e4m3_encode(np.asarray(key, np.float32) / np.float32(k_scale))
+    vq = fp8_e4m3_encode(np.asarray(value, np.float32) / np.float32(v_scale))
+    t, hkv, d = kq.shape
+    for i in range(t):
+        s = int(slots[i])
+        if s < 0:
+            continue
+        blk, off = s // block_size, s % block_size
+        key_cache[blk, :, :, off, :] = kq[i].reshape(hkv, d // 16, 16)
+        value_cache[blk, :, :, off] = vq[i]
+
+
 # ============================================== device decode loop (host restatement)
 def decode_step_prepare(state, eos_ids, block_tables, block_table_lens, block_size, num_blocks):
     """One decode step's token feedback + metadata, as the reference host loop does it.

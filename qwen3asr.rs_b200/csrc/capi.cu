@@ -93,6 +93,70 @@ int32_t vasr_pa_reshape_and_cache(const void *key, const void *value, void *key_
   return vasr::launch_append(a, to_stream(stream));
 }
 
+int32_t vasr_pa_reshape_and_cache_fp8(const void *key, const void *value, void *key_cache,
+                                      void *value_cache, const int64_t *slot_mapping,
+                                      int64_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                                      int32_t block_size, int64_t num_blocks,
+                                      int64_t key_token_stride, int64_t value_token_stride,
+                                      int32_t src_dtype, const float *k_scale, const float *v_scale,
+                                      vasr_pa_stream_t stream) {
+  const int es = elem_size(src_dtype);
+  if (es == 0) return VASR_PA_EINVAL_DTYPE;
+  if (!block_size_ok(block_size)) return VASR_PA_EINVAL_BLOCKSIZE;
+  if (num_kv_heads <= 0 || head_dim <= 0 || num_blocks <= 0 || num_tokens < 0 ||
+      head_dim % 16 != 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_tokens == 0) return VASR_PA_OK;
+  if (key_token_stride < (int64_t)num_kv_heads * head_dim ||
+      value_token_stride < (int64_t)num_kv_heads * head_dim)
+    return VASR_PA_EINVAL_SHAPE;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping || !k_scale || !v_scale)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned(key, es) || !aligned(value, es) || !aligned16(key_cache) ||
+      !aligned16(value_cache) || !aligned(slot_mapping, 8) || !aligned(k_scale, 4) ||
+      !aligned(v_scale, 4))
+    return VASR_PA_EINVAL_ALIGN;
+  AppendArgs a{key, value, key_cache, value_cache, slot_mapping, num_tokens, num_kv_heads,
+               head_dim, block_size, num_blocks, key_token_stride, value_token_stride, src_dtype,
+               VASR_PA_FP8_E4M3, k_scale, v_scale};
+  return vasr::launch_append(a, to_stream(stream));
+}
+
+int32_t vasr_pa_paged_attention_fp8(void *out, const void *query, const void *key_cache,
+                                    const void *value_cache, const uint32_t *block_tables,
+                                    const uint32_t *context_lens, int32_t num_seqs,
+                                    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                                    int32_t block_size, int64_t num_blocks,
+                                    int32_t max_num_blocks_per_seq, int32_t max_context_len,
+                                    float scale, float softcapping, int64_t q_seq_stride,
+                                    int32_t dtype, const float *k_scale, const float *v_scale,
+                                    void *workspace, size_t workspace_bytes,
+                                    vasr_pa_stream_t stream) {
+  if (dtype != VASR_PA_BF16 && dtype != VASR_PA_F16) return VASR_PA_EINVAL_DTYPE;
+  if (!block_size_ok(block_size)) return VASR_PA_EINVAL_BLOCKSIZE;
+  if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || num_blocks <= 0 ||
+      num_heads % num_kv_heads != 0 || head_dim % 16 != 0 || max_num_blocks_per_seq <= 0 ||
+      max_context_len < 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0) return VASR_PA_OK;
+  if (num_seqs > 65535 || num_kv_heads > 65535) return VASR_PA_EINVAL_SHAPE;
+  if (q_seq_stride < (int64_t)num_heads * head_dim) return VASR_PA_EINVAL_SHAPE;
+  if (!(softcapping > 0.f)) return VASR_PA_EINVAL_SHAPE;
+  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens || !k_scale ||
+      !v_scale)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned16(query) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      (q_seq_stride * 2) % 16 != 0 || !aligned(out, 2) || !aligned(block_tables, 4) ||
+      !aligned(context_lens, 4) || (workspace && !aligned(workspace, 256)) ||
+      !aligned(k_scale, 4) || !aligned(v_scale, 4))
+    return VASR_PA_EINVAL_ALIGN;
+  DecodeArgs a{out, query, key_cache, value_cache, block_tables, context_lens, num_seqs,
+               num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_num_blocks_per_seq,
+               max_context_len > 0 ? max_context_len : 1, scale, softcapping, q_seq_stride, dtype,
+               workspace, workspace_bytes, VASR_PA_FP8_E4M3, k_scale, v_scale};
+  return vasr::launch_decode(a, to_stream(stream));
+}
+
 size_t vasr_pa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_heads,
                                               int32_t num_kv_heads, int32_t head_dim,
                                               int32_t block_size, int32_t max_context_len,

@@ -7,6 +7,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -72,6 +73,27 @@ __device__ __forceinline__ void unpack16_f16(const uint4 &u, float (&f)[8]) {
   unpack_half2(u.w, f[6], f[7]);
 }
 
+// fp8 E4M3 (KV-cache storage only): 16 values per 16-byte chunk, converted
+// through the cuda_fp8.h pair conversion to f16 (exact) and then to f32.
+template <> struct Elem<__nv_fp8_e4m3> {
+  static constexpr int kX = 16;
+  __device__ static __forceinline__ float to_f32(__nv_fp8_e4m3 v) { return float(v); }
+};
+__device__ __forceinline__ void unpack16_fp8(const uint4 &u, float (&f)[16]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xffffu), __NV_E4M3);
+    __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
+    const float2 a = __half22float2(*reinterpret_cast<__half2 *>(&lo));
+    const float2 b = __half22float2(*reinterpret_cast<__half2 *>(&hi));
+    f[4 * i + 0] = a.x;
+    f[4 * i + 1] = a.y;
+    f[4 * i + 2] = b.x;
+    f[4 * i + 3] = b.y;
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void unpack_chunk(const uint4 &u, float (&f)[Elem<T>::kX]);
 template <>
@@ -80,6 +102,10 @@ template <>
 __device__ __forceinline__ void unpack_chunk<__nv_bfloat16>(const uint4 &u, float (&f)[8]) { unpack16_bf16(u, f); }
 template <>
 __device__ __forceinline__ void unpack_chunk<__half>(const uint4 &u, float (&f)[8]) { unpack16_f16(u, f); }
+template <>
+__device__ __forceinline__ void unpack_chunk<__nv_fp8_e4m3>(const uint4 &u, float (&f)[16]) {
+  unpack16_fp8(u, f);
+}
 
 // ------------------------------------------------------- shared-memory I/O
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {

@@ -42,7 +42,7 @@ DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_
 namespace {
 
 DecodeParams make_decode_params(const DecodeArgs &a, const DecodeWorkspace &w) {
-  DecodeParams p;
+  DecodeParams p{};
   p.out = a.out;
   p.q = a.query;
   p.k_cache = a.key_cache;
@@ -63,6 +63,8 @@ DecodeParams make_decode_params(const DecodeArgs &a, const DecodeWorkspace &w) {
   p.max_splits = w.max_splits;
   p.scale = a.scale;
   p.softcap = a.softcapping;
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
   return p;
 }
 
@@ -93,16 +95,17 @@ int launch_decode_generic(const DecodeArgs &a, cudaStream_t stream) {
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
-template <typename T, int BS, int D>
+template <typename T, int BS, int D, typename TC = T>
 int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
-  constexpr int kStageBytes = 2 * ((16 > BS) ? 16 / BS : 1) * D * BS * (int)sizeof(T);
-  constexpr int kNST = kStageBytes <= 8192 ? VASR_G2_NST : 4;
-  using C = DecodeG2Cfg<T, BS, D, kNST>;
+  constexpr int kStageBytes = 2 * ((16 > BS) ? 16 / BS : 1) * D * BS * (int)sizeof(TC);
+  // same bytes in flight per CTA for any page size: twice the stages for 4 KB stages
+  constexpr int kNST = kStageBytes <= 4096 ? 2 * VASR_G2_NST : kStageBytes <= 8192 ? VASR_G2_NST : 4;
+  using C = DecodeG2Cfg<TC, BS, D, kNST>;
   DecodeWorkspace w;
   const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
   if (st != VASR_PA_OK) return st;
   const DecodeParams p = make_decode_params(a, w);
-  auto kern = paged_decode_g2_kernel<T, BS, D, kNST, VASR_G2_MINB>;
+  auto kern = paged_decode_g2_kernel<T, BS, D, kNST, VASR_G2_MINB, TC>;
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
   dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
@@ -140,9 +143,28 @@ int dispatch_g(const DecodeArgs &a, cudaStream_t s) {
   }
 }
 
+
+template <typename T>
+int dispatch_fp8(const DecodeArgs &a, cudaStream_t s) {
+  if (a.head_dim != 128 || a.num_heads != 2 * a.num_kv_heads) return VASR_PA_ENOT_SUPPORTED;
+  switch (a.block_size) {
+    case 8: return VASR_PA_ENOT_SUPPORTED;  // an 8-byte V page row is under one 16-byte vector
+    case 16: return launch_decode_g2<T, 16, 128, __nv_fp8_e4m3>(a, s);
+    case 32: return launch_decode_g2<T, 32, 128, __nv_fp8_e4m3>(a, s);
+    default: return VASR_PA_EINVAL_BLOCKSIZE;
+  }
+}
+
 }  // namespace
 
 int launch_decode(const DecodeArgs &a, cudaStream_t s) {
+  if (a.cache_dtype == VASR_PA_FP8_E4M3) {
+    switch (a.dtype) {
+      case VASR_PA_BF16: return dispatch_fp8<__nv_bfloat16>(a, s);
+      case VASR_PA_F16: return dispatch_fp8<__half>(a, s);
+      default: return VASR_PA_EINVAL_DTYPE;
+    }
+  }
   switch (a.dtype) {
     case VASR_PA_F32: return dispatch_g<float>(a, s);
     case VASR_PA_BF16: return dispatch_g<__nv_bfloat16>(a, s);

@@ -36,6 +36,8 @@ struct DecodeParams {
   float *ws_o;        // [B * Hkv * S][G][D]
   float2 *ws_ml;      // [B * Hkv * S][G]  (m in log2 units, l)
   uint32_t *counters; // [B * Hkv]
+  const float *k_scale;  // fp8 caches: per-tensor scales (device scalars), else null
+  const float *v_scale;
   int64_t q_seq_stride;
   int64_t num_blocks;
   int num_seqs;

@@ -58,11 +58,13 @@ struct DecodeG2Cfg {
 // One work item: (split, kv head, sequence). `ubase` = stage-ring units this
 // CTA consumed before (the ring's barriers keep counting across items);
 // returns the units consumed here. The barriers are initialised by the caller.
-template <typename T, int BS, int D, int NST>
+// T: query / output element; TC: cache element (T, or fp8 E4M3 with the
+// per-tensor scales p.k_scale / p.v_scale).
+template <typename T, int BS, int D, int NST, typename TC = T>
 __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsigned char *smem,
                                                    const int split, const int kvh, const int b,
                                                    const uint32_t ubase) {
-  using C = DecodeG2Cfg<T, BS, D, NST>;
+  using C = DecodeG2Cfg<TC, BS, D, NST>;
   constexpr int G = 2;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -123,8 +125,8 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
   }
   __syncthreads();
 
-  const T *kc = reinterpret_cast<const T *>(p.k_cache);
-  const T *vc = reinterpret_cast<const T *>(p.v_cache);
+  const TC *kc = reinterpret_cast<const TC *>(p.k_cache);
+  const TC *vc = reinterpret_cast<const TC *>(p.v_cache);
   const int64_t page_elems = (int64_t)D * BS;
   auto issue_unit = [&](int u) {
     const int s = (ubase + u) % C::kNST;
@@ -154,15 +156,19 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const uint4 *q4 = reinterpret_cast<const uint4 *>(qp + g * D);
+      constexpr int QX = Elem<T>::kX;
 #pragma unroll
-      for (int c = 0; c < C::kCQ; ++c) {
-        float f[C::kX];
+      for (int c = 0; c < D / 4 / QX; ++c) {
+        float f[QX];
         unpack_chunk<T>(__ldg(q4 + c), f);
 #pragma unroll
-        for (int e = 0; e < C::kX; ++e) q_reg[g][c * C::kX + e] = f[e];
+        for (int e = 0; e < QX; ++e) q_reg[g][c * QX + e] = f[e];
       }
     }
   }
+  // fp8 caches hold K / k_scale and V / v_scale
+  const float k_mul = p.k_scale ? p.scale * __ldg(p.k_scale) : p.scale;
+  const float v_mul = p.v_scale ? __ldg(p.v_scale) : 1.f;
   // score lane identity after the reduce
   const int s_tok = qb1 * 8 + t8;  // token within a 16-token sub-tile
   const int s_head = qb0;
@@ -210,7 +216,7 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
 #pragma unroll
           for (int c = 0; c < C::kCQ; ++c) {
             float kf[C::kX];
-            unpack_chunk<T>(lds128(row + c * BS * 16), kf);
+            unpack_chunk<TC>(lds128(row + c * BS * 16), kf);
 #pragma unroll
             for (int e = 0; e < C::kX; e += 2) {
 #pragma unroll
@@ -232,7 +238,7 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
       // level 2 over quarter bit 0 (xor 8): keep head qb0
       const float send2 = qb0 ? ka : kb;
       const float dot = (qb0 ? kb : ka) + __shfl_xor_sync(0xffffffffu, send2, 8);
-      float sv_ = dot * p.scale;
+      float sv_ = dot * k_mul;
       if (use_softcap) sv_ = p.softcap * tanhf(sv_ / p.softcap);
       sc[ti] = (ti * 16 + s_tok < n_valid) ? sv_ * kLog2e : -INFINITY;
     }
@@ -292,7 +298,7 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
         for (int i = 0; i < C::kNR; ++i) {
           const int d = rlo + C::kRPP * ph + 4 * C::kRPP * i;
           float vf[C::kTPS];
-          unpack_chunk<T>(lds128(vrow0 + d * C::kR), vf);
+          unpack_chunk<TC>(lds128(vrow0 + d * C::kR), vf);
           if (tail) {
 #pragma unroll
             for (int e = 0; e < C::kTPS; ++e)
@@ -369,7 +375,7 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
       }
     }
     if (single) {
-      out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L : 0.f);
+      out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L * v_mul : 0.f);
     } else {
       const int64_t slot = bk * p.max_splits + split;
       p.ws_o[(slot * G + g) * D + d] = O;
@@ -405,26 +411,26 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
         O = fmaf(__ldcg(&p.ws_o[((slot0 + s) * G + g) * D + d]), w, O);
       }
     }
-    out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L : 0.f);
+    out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L * v_mul : 0.f);
   }
   if (tid == 0) p.counters[bk] = 0u;
   return (uint32_t)n_units;
 }
 
-template <typename T, int BS, int D, int NST>
+template <typename TC, int BS, int D, int NST>
 __device__ __forceinline__ void decode_g2_init_ring(unsigned char *smem) {
-  using C = DecodeG2Cfg<T, BS, D, NST>;
+  using C = DecodeG2Cfg<TC, BS, D, NST>;
   if (threadIdx.x < C::kNST) mbar_init(smem_addr(smem) + C::kOffBar + threadIdx.x * 8, 1);
   if (threadIdx.x == 0) mbar_fence_init();
   __syncthreads();
 }
 
 // Grid form: one CTA per (split, kv head, sequence).
-template <typename T, int BS, int D, int NST, int MINB>
+template <typename T, int BS, int D, int NST, int MINB, typename TC = T>
 __global__ void __launch_bounds__(128, MINB) paged_decode_g2_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  decode_g2_init_ring<T, BS, D, NST>(smem);
-  decode_g2_item<T, BS, D, NST>(p, smem, blockIdx.x, blockIdx.y, blockIdx.z, 0);
+  decode_g2_init_ring<TC, BS, D, NST>(smem);
+  decode_g2_item<T, BS, D, NST, TC>(p, smem, blockIdx.x, blockIdx.y, blockIdx.z, 0);
 }
 
 }  // namespace vasr

@@ -156,7 +156,7 @@ int launch_t(const FusedRopeParams &p, int block_size, cudaStream_t s) {
 }  // namespace
 
 int launch_fused_rope(const FusedRopeArgs &a, cudaStream_t s) {
-  FusedRopeParams p;
+  FusedRopeParams p{};
   p.q_out = a.q_out;
   p.qkv = a.qkv;
   p.q_norm_w = a.q_norm_weight;

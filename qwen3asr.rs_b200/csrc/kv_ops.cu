@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(const AppendP
 
 template <typename T, int BS, int D>
 int launch_append_t(const AppendArgs &a, cudaStream_t stream) {
-  AppendParams p;
+  AppendParams p{};
   p.key = static_cast<const unsigned char *>(a.key);
   p.value = static_cast<const unsigned char *>(a.value);
   p.k_cache = static_cast<unsigned char *>(a.key_cache);
@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const GatherParams p) {
 
 template <typename T, int BS, int D>
 int launch_gather_t(const GatherArgs &a, cudaStream_t stream) {
-  GatherParams p;
+  GatherParams p{};
   p.k_out = static_cast<unsigned char *>(a.key_out);
   p.v_out = static_cast<unsigned char *>(a.value_out);
   p.k_cache = static_cast<const unsigned char *>(a.key_cache);
@@ -329,10 +329,109 @@ __global__ void __launch_bounds__(kCopyThreads) swap_blocks_kernel(const SwapPar
   copy_block_bytes(p.dst + dst * p.block_bytes, p.src + src * p.block_bytes, p.block_bytes);
 }
 
+// ====================================================== fp8 KV append
+// Pages of one-byte E4M3 values with per-tensor scales: cache = value / scale
+// (IEEE division), rounded to nearest even and saturated to +-448 by the
+// cuda_fp8.h conversion. One warp per (token, kv head): K as 16-byte chunks
+// of 16 dims (lane c < D / 16 writes chunk c), V one byte per dim.
+struct AppendFp8Params {
+  const unsigned char *key;
+  const unsigned char *value;
+  unsigned char *k_cache;
+  unsigned char *v_cache;
+  const int64_t *slots;
+  const float *k_scale;
+  const float *v_scale;
+  int64_t num_tokens;
+  int64_t k_stride_bytes;
+  int64_t v_stride_bytes;
+  int64_t num_blocks;
+  int num_kv_heads;
+};
+
+template <typename T, int BS, int D>
+__global__ void __launch_bounds__(128) kv_append_fp8_kernel(const AppendFp8Params p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * 4 + warp;
+  if (item >= p.num_tokens * p.num_kv_heads) return;
+  const int64_t t = item / p.num_kv_heads;
+  const int h = (int)(item % p.num_kv_heads);
+  const int64_t slot = p.slots[t];
+  if (slot < 0) return;
+  const int64_t blk = slot / BS;
+  const int off = (int)(slot % BS);
+  if (blk >= p.num_blocks) {
+    if (lane == 0) raise_device_error(VASR_PA_DERR_SLOT_RANGE);
+    return;
+  }
+  const float ks = __ldg(p.k_scale), vs = __ldg(p.v_scale);
+  const T *k = reinterpret_cast<const T *>(p.key + t * p.k_stride_bytes) + (int64_t)h * D;
+  const T *v = reinterpret_cast<const T *>(p.value + t * p.v_stride_bytes) + (int64_t)h * D;
+  const int64_t page = (int64_t)blk * p.num_kv_heads + h;
+  if (lane < D / 16) {
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = __fdiv_rn(Elem<T>::to_f32(k[lane * 16 + 2 * i]), ks);
+      const float b = __fdiv_rn(Elem<T>::to_f32(k[lane * 16 + 2 * i + 1]), ks);
+      const __nv_fp8x2_storage_t pr = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+      w[i >> 1] |= (uint32_t)pr << (16 * (i & 1));
+    }
+    *reinterpret_cast<uint4 *>(p.k_cache + ((page * (D / 16) + lane) * BS + off) * 16) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+#pragma unroll
+  for (int d = lane; d < D; d += 32) {
+    const float x = __fdiv_rn(Elem<T>::to_f32(v[d]), vs);
+    p.v_cache[(page * D + d) * BS + off] = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  }
+}
+
+template <typename T, int BS, int D>
+int launch_append_fp8_t(const AppendArgs &a, cudaStream_t stream) {
+  AppendFp8Params p{};
+  p.key = static_cast<const unsigned char *>(a.key);
+  p.value = static_cast<const unsigned char *>(a.value);
+  p.k_cache = static_cast<unsigned char *>(a.key_cache);
+  p.v_cache = static_cast<unsigned char *>(a.value_cache);
+  p.slots = a.slot_mapping;
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
+  p.num_tokens = a.num_tokens;
+  p.k_stride_bytes = a.key_token_stride * (int64_t)sizeof(T);
+  p.v_stride_bytes = a.value_token_stride * (int64_t)sizeof(T);
+  p.num_blocks = a.num_blocks;
+  p.num_kv_heads = a.num_kv_heads;
+  const int64_t items = a.num_tokens * a.num_kv_heads;
+  const int64_t ctas = (items + 3) / 4;
+  if (ctas > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+  kv_append_fp8_kernel<T, BS, D><<<(unsigned)ctas, 128, 0, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
+template <typename T>
+int launch_append_fp8_bs(const AppendArgs &a, cudaStream_t s) {
+  if (a.head_dim != 128) return VASR_PA_ENOT_SUPPORTED;
+  switch (a.block_size) {
+    case 8: return launch_append_fp8_t<T, 8, 128>(a, s);
+    case 16: return launch_append_fp8_t<T, 16, 128>(a, s);
+    case 32: return launch_append_fp8_t<T, 32, 128>(a, s);
+    default: return VASR_PA_EINVAL_BLOCKSIZE;
+  }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------- launchers
 int launch_append(const AppendArgs &a, cudaStream_t s) {
+  if (a.cache_dtype == VASR_PA_FP8_E4M3) {
+    switch (a.dtype) {
+      case VASR_PA_F32: return launch_append_fp8_bs<float>(a, s);
+      case VASR_PA_BF16: return launch_append_fp8_bs<__nv_bfloat16>(a, s);
+      case VASR_PA_F16: return launch_append_fp8_bs<__half>(a, s);
+      default: return VASR_PA_EINVAL_DTYPE;
+    }
+  }
 #define VASR_APPEND_CASE(T, BS_, D_) \
   if (a.block_size == BS_ && a.head_dim == D_) return launch_append_t<T, BS_, D_>(a, s);
 #define VASR_APPEND_T(T)                                                            \
@@ -365,7 +464,7 @@ int launch_gather(const GatherArgs &a, cudaStream_t s) {
 int launch_copy_blocks(void *const *k, void *const *v, int layers, const int64_t *mapping,
                        int64_t pairs, int64_t num_blocks, int64_t block_bytes, cudaStream_t s) {
   if (layers > kMaxLayers) return VASR_PA_EINVAL_SHAPE;
-  CopyBlocksParams p;
+  CopyBlocksParams p{};
   for (int l = 0; l < layers; ++l) {
     p.k[l] = static_cast<unsigned char *>(k[l]);
     p.v[l] = static_cast<unsigned char *>(v[l]);
@@ -383,7 +482,7 @@ int launch_copy_blocks(void *const *k, void *const *v, int layers, const int64_t
 int launch_swap_blocks(void *dst, const void *src, const int64_t *mapping, int64_t pairs,
                        int64_t src_blocks, int64_t dst_blocks, int64_t block_bytes,
                        cudaStream_t s) {
-  SwapParams p;
+  SwapParams p{};
   p.dst = static_cast<unsigned char *>(dst);
   p.src = static_cast<const unsigned char *>(src);
   p.mapping = mapping;

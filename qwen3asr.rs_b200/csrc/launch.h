@@ -24,7 +24,10 @@ struct AppendArgs {
   int64_t num_blocks;
   int64_t key_token_stride;
   int64_t value_token_stride;
-  int dtype;
+  int dtype;                       // element type of key / value
+  int cache_dtype = -1;            // -1: same as dtype; VASR_PA_FP8_E4M3: scaled fp8 pages
+  const float *k_scale = nullptr;  // fp8: device scalars, cache = value / scale
+  const float *v_scale = nullptr;
 };
 
 struct DecodeArgs {
@@ -45,9 +48,12 @@ struct DecodeArgs {
   float scale;
   float softcapping;
   int64_t q_seq_stride;
-  int dtype;
+  int dtype;                       // element type of query / out
   void *workspace;
   size_t workspace_bytes;
+  int cache_dtype = -1;            // -1: same as dtype; VASR_PA_FP8_E4M3: scaled fp8 pages
+  const float *k_scale = nullptr;  // fp8: device scalars, real K = stored K * k_scale
+  const float *v_scale = nullptr;
 };
 
 struct GatherArgs {

@@ -521,7 +521,7 @@ int scalar_launch(const PrefillArgs &a, const PrefillParams &p, cudaStream_t s) 
 
 int launch_prefill(const PrefillArgs &a, cudaStream_t s) {
   if (a.num_kv_heads > 65535) return VASR_PA_EINVAL_SHAPE;
-  PrefillParams p;
+  PrefillParams p{};
   p.out = a.out;
   p.q = a.query;
   p.k_cache = a.key_cache;

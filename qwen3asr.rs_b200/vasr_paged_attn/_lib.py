@@ -14,7 +14,7 @@ _PKG_ROOT = Path(__file__).resolve().parent.parent
 LIB_PATH = Path(os.environ.get("VASR_PA_LIB", _PKG_ROOT / "lib" / "libvasr_pa.so"))
 
 # vasr_pa_dtype
-F32, BF16, F16 = 0, 1, 2
+F32, BF16, F16, FP8_E4M3 = 0, 1, 2, 3
 # vasr_pa_status
 OK = 0
 EINVAL_SHAPE = -1
@@ -85,6 +85,17 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _f32, _c_void_p, _c_void_p, _i64,
          _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i32, _i64, _i32,
+         _c_void_p],
+    ),
+    "vasr_pa_reshape_and_cache_fp8": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i64,
+         _i64, _i64, _i32, _c_void_p, _c_void_p, _c_void_p],
+    ),
+    "vasr_pa_paged_attention_fp8": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32,
+         _i32, _i64, _i32, _i32, _f32, _f32, _i64, _i32, _c_void_p, _c_void_p, _c_void_p, _size,
          _c_void_p],
     ),
     "vasr_pa_decode_step_prepare": (

@@ -26,6 +26,17 @@ _DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16
 _INDEX32 = (torch.int32, torch.uint32)
 
 
+# fp8 (E4M3) pages: one byte per element, per-tensor f32 scales on the device
+FP8_CACHE = torch.float8_e4m3fn
+
+
+def _check_scales(k_scale, v_scale, dev) -> None:
+    for sc in (k_scale, v_scale):
+        if sc is None or sc.dtype != torch.float32 or sc.numel() != 1 or sc.device != dev:
+            raise _lib.VasrPaError(_lib.EINVAL_POINTER,
+                                   "fp8 caches need k_scale / v_scale as f32 scalars on the cache device")
+
+
 def dtype_code(dt: torch.dtype) -> int:
     try:
         return _DTYPE_CODE[dt]
@@ -70,7 +81,12 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_scale: Optional[
     nb, hkv, d, bs = cache_geometry(key_cache, value_cache)
     if key.dim() != 3 or value.shape != key.shape or tuple(key.shape[1:]) != (hkv, d):
         raise _lib.VasrPaError(_lib.EINVAL_SHAPE, f"key/value shape {tuple(key.shape)} vs cache heads={hkv} dim={d}")
-    if key.dtype != key_cache.dtype or value.dtype != key_cache.dtype:
+    fp8 = key_cache.dtype == FP8_CACHE
+    if fp8:
+        _check_scales(k_scale, v_scale, dev)
+        if value.dtype != key.dtype:
+            raise _lib.VasrPaError(_lib.EINVAL_DTYPE, "key/value dtype mismatch")
+    elif key.dtype != key_cache.dtype or value.dtype != key_cache.dtype:
         raise _lib.VasrPaError(_lib.EINVAL_DTYPE, "key/value dtype must equal the cache dtype")
     for t in (key, value):
         if t.stride(2) != 1 or t.stride(1) != d:
@@ -78,6 +94,13 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, k_scale: Optional[
     if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or slot_mapping.shape[0] != key.shape[0]:
         raise _lib.VasrPaError(_lib.EINVAL_SHAPE, "slot_mapping must be int64 [num_tokens]")
     slot_mapping = slot_mapping.contiguous()
+    if fp8:
+        st = _lib.lib().vasr_pa_reshape_and_cache_fp8(
+            key.data_ptr(), value.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            slot_mapping.data_ptr(), key.shape[0], hkv, d, bs, nb, key.stride(0), value.stride(0),
+            dtype_code(key.dtype), k_scale.data_ptr(), v_scale.data_ptr(), _stream(dev))
+        _lib.check(st, "reshape_and_cache (fp8 cache)")
+        return
     st = _lib.lib().vasr_pa_reshape_and_cache(
         key.data_ptr(), value.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
         slot_mapping.data_ptr(), key.shape[0], hkv, d, bs, nb, key.stride(0), value.stride(0),
@@ -126,14 +149,16 @@ def paged_attention(q: torch.Tensor, k_scale: Optional[torch.Tensor], v_scale: O
                     softmax_scale: float, softcapping: float = 1.0,
                     sinks: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Single-token decode attention over the pages; returns ``[B, Hq, D]`` in q's dtype."""
-    del k_scale, v_scale  # fp8 scales: unused when the cache dtype equals q's dtype
     if alibi is not None or sinks is not None:
         raise _lib.VasrPaError(_lib.ENOT_SUPPORTED, "alibi / attention sinks are not used by Qwen3-ASR")
     dev = _require_cuda(q, key_cache, value_cache, block_tables, context_lens)
     nb, hkv, d, bs = cache_geometry(key_cache, value_cache)
     if q.dim() != 3 or q.shape[2] != d or q.stride(2) != 1 or q.stride(1) != d:
         raise _lib.VasrPaError(_lib.EINVAL_SHAPE, f"q must be [B, Hq, {d}] with packed heads, got {tuple(q.shape)}")
-    if q.dtype != key_cache.dtype:
+    fp8 = key_cache.dtype == FP8_CACHE
+    if fp8:
+        _check_scales(k_scale, v_scale, dev)
+    elif q.dtype != key_cache.dtype:
         raise _lib.VasrPaError(_lib.EINVAL_DTYPE, "q dtype must equal the cache dtype")
     b, hq = int(q.shape[0]), int(q.shape[1])
     if block_tables.dtype not in _INDEX32 or block_tables.dim() != 2 or block_tables.shape[0] != b:
@@ -146,6 +171,15 @@ def paged_attention(q: torch.Tensor, k_scale: Optional[torch.Tensor], v_scale: O
         out = torch.empty((b, hq, d), dtype=q.dtype, device=dev)
     need = paged_attention_workspace_bytes(b, hq, hkv, d, bs, max_context_len, q.dtype)
     ws = reserve_paged_attention_workspace(dev, need)
+    if fp8:
+        st = _lib.lib().vasr_pa_paged_attention_fp8(
+            out.data_ptr(), q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            block_tables.data_ptr(), context_lens.data_ptr(), b, hq, hkv, d, bs, nb,
+            int(block_tables.shape[1]), int(max_context_len), float(softmax_scale), float(softcapping),
+            q.stride(0), dtype_code(q.dtype), k_scale.data_ptr(), v_scale.data_ptr(), ws.data_ptr(),
+            ws.numel(), _stream(dev))
+        _lib.check(st, "paged_attention (fp8 cache)")
+        return out
     st = _lib.lib().vasr_pa_paged_attention(
         out.data_ptr(), q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), b, hq, hkv, d, bs, nb,

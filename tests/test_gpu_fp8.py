@@ -1,0 +1,144 @@
+"""fp8 (E4M3) KV cache: the append is byte-exact against the oracle's encoder,
+decode attention over fp8 pages is within the bf16 tolerance (2e-2) of the
+f64 oracle run on the dequantised pages (stored byte value x scale)."""
+import numpy as np
+import pytest
+import torch
+
+import paged_ref as ref
+from cases import disjoint_block_tables
+from vasr_paged_attn import _lib
+from vasr_paged_attn import mistralrs_paged_attn as pa
+
+pytestmark = pytest.mark.gpu
+
+HKV, HQ, D = 8, 16, 128
+SENTINEL = 0x5A
+
+
+@pytest.fixture(autouse=True)
+def _clear(cuda_device):
+    pa.device_error(clear=True)
+    yield
+    assert pa.device_error() == 0
+
+
+def _u8_cache(nb, bs, dev, fill=SENTINEL):
+    kc = torch.full((nb, HKV, D // 16, bs, 16), fill, dtype=torch.uint8, device=dev)
+    vc = torch.full((nb, HKV, D, bs), fill, dtype=torch.uint8, device=dev)
+    return kc, vc
+
+
+def _scales(dev, ks, vs):
+    return (torch.tensor([ks], dtype=torch.float32, device=dev),
+            torch.tensor([vs], dtype=torch.float32, device=dev))
+
+
+@pytest.mark.parametrize("src", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_fp8_append_is_byte_exact(cuda_device, src, bs):
+    rng = np.random.default_rng(bs)
+    t, nb = 77, 40
+    k = (rng.standard_normal((t, HKV, D)) * 3).astype(np.float32)
+    v = (rng.standard_normal((t, HKV, D)) * 3).astype(np.float32)
+    k[0, 0, :7] = [1e4, -1e4, 0.0, -0.0, 1e-12, 449 * 0.05, 448 * 0.05]  # saturation, signed zeros
+    slots = rng.permutation(nb * bs)[:t].astype(np.int64)
+    slots[::9] = -1
+    kt, vt = torch.from_numpy(k).to(src), torch.from_numpy(v).to(src)
+    ks, vs = 0.05, 0.02
+    kc, vc = _u8_cache(nb, bs, cuda_device)
+    sk, sv = _scales(cuda_device, ks, vs)
+    pa.reshape_and_cache(kt.to(cuda_device), vt.to(cuda_device), sk, sv, kc.view(torch.float8_e4m3fn),
+                         vc.view(torch.float8_e4m3fn), torch.from_numpy(slots).to(cuda_device))
+    ek = np.full((nb, HKV, D // 16, bs, 16), SENTINEL, np.uint8)
+    ev = np.full((nb, HKV, D, bs), SENTINEL, np.uint8)
+    ref.reshape_and_cache_fp8(kt.float().numpy(), vt.float().numpy(), ek, ev, slots, bs, ks, vs)
+    assert np.array_equal(kc.cpu().numpy(), ek)
+    assert np.array_equal(vc.cpu().numpy(), ev)
+
+
+def _fp8_decode_case(rng, ctx, bs, ks, vs):
+    blocks = [-(-int(c) // bs) for c in ctx]
+    nb = sum(blocks) + 4
+    tables = disjoint_block_tables(rng, blocks, nb)
+    kc = np.full((nb, HKV, D // 16, bs, 16), 0x7F, np.uint8)  # NaN bytes where nothing was written
+    vc = np.full((nb, HKV, D, bs), 0x7F, np.uint8)
+    for i, n in enumerate(ctx):
+        k = rng.standard_normal((int(n), HKV, D)).astype(np.float32)
+        v = rng.standard_normal((int(n), HKV, D)).astype(np.float32)
+        pos = np.arange(int(n))
+        slots = tables[i, pos // bs].astype(np.int64) * bs + pos % bs
+        ref.reshape_and_cache_fp8(k, v, kc, vc, slots, bs, ks, vs)
+    return tables, kc, vc
+
+
+@pytest.mark.parametrize("bs", [16, 32])
+def test_fp8_decode_matches_oracle(cuda_device, bs):
+    rng = np.random.default_rng(100 + bs)
+    ctx = np.array([1, 17, 200, 513, 1024, 1500, 2049], np.int64)
+    ks, vs = 0.02, 0.015
+    tables, kc, vc = _fp8_decode_case(rng, ctx, bs, ks, vs)
+    q = torch.from_numpy(rng.standard_normal((len(ctx), HQ, D)).astype(np.float32)).to(torch.bfloat16)
+    sk, sv = _scales(cuda_device, ks, vs)
+    out = pa.paged_attention(q.to(cuda_device), sk, sv,
+                             torch.from_numpy(kc).to(cuda_device).view(torch.float8_e4m3fn),
+                             torch.from_numpy(vc).to(cuda_device).view(torch.float8_e4m3fn),
+                             torch.from_numpy(tables.astype(np.int32)).to(cuda_device),
+                             torch.from_numpy(ctx.astype(np.int32)).to(cuda_device), None,
+                             int(ctx.max()), D ** -0.5, 1.0, None).float().cpu().numpy()
+    kf = np.ascontiguousarray(ref.fp8_e4m3_decode(kc) * np.float32(ks))
+    vf = np.ascontiguousarray(ref.fp8_e4m3_decode(vc) * np.float32(vs))
+    exp = ref.paged_attention(np.ascontiguousarray(q.float().numpy()), kf, vf,
+                              np.ascontiguousarray(tables.astype(np.uint32)), ctx.astype(np.uint32),
+                              D ** -0.5)
+    assert np.abs(out - exp).max() <= 2e-2
+
+
+def test_fp8_append_then_decode(cuda_device):
+    """Append bf16 K/V into fp8 pages on the GPU, then decode; the oracle quantises the same values."""
+    rng = np.random.default_rng(9)
+    bs, ctx = 16, np.array([300, 45, 1200], np.int64)
+    blocks = [-(-int(c) // bs) for c in ctx]
+    nb = sum(blocks) + 2
+    tables = disjoint_block_tables(rng, blocks, nb)
+    kc, vc = _u8_cache(nb, bs, cuda_device, fill=0)
+    ks, vs = 0.03, 0.02
+    sk, sv = _scales(cuda_device, ks, vs)
+    ek = np.zeros((nb, HKV, D // 16, bs, 16), np.uint8)
+    ev = np.zeros((nb, HKV, D, bs), np.uint8)
+    for i, n in enumerate(ctx):
+        k = torch.from_numpy(rng.standard_normal((int(n), HKV, D)).astype(np.float32)).to(torch.bfloat16)
+        v = torch.from_numpy(rng.standard_normal((int(n), HKV, D)).astype(np.float32)).to(torch.bfloat16)
+        pos = np.arange(int(n))
+        slots = tables[i, pos // bs].astype(np.int64) * bs + pos % bs
+        pa.reshape_and_cache(k.to(cuda_device), v.to(cuda_device), sk, sv, kc.view(torch.float8_e4m3fn),
+                             vc.view(torch.float8_e4m3fn), torch.from_numpy(slots).to(cuda_device))
+        ref.reshape_and_cache_fp8(k.float().numpy(), v.float().numpy(), ek, ev, slots, bs, ks, vs)
+    q = torch.from_numpy(rng.standard_normal((len(ctx), HQ, D)).astype(np.float32)).to(torch.bfloat16)
+    out = pa.paged_attention(q.to(cuda_device), sk, sv, kc.view(torch.float8_e4m3fn),
+                             vc.view(torch.float8_e4m3fn),
+                             torch.from_numpy(tables.astype(np.int32)).to(cuda_device),
+                             torch.from_numpy(ctx.astype(np.int32)).to(cuda_device), None,
+                             int(ctx.max()), D ** -0.5, 1.0, None).float().cpu().numpy()
+    assert np.array_equal(kc.cpu().numpy(), ek) and np.array_equal(vc.cpu().numpy(), ev)
+    exp = ref.paged_attention(np.ascontiguousarray(q.float().numpy()),
+                              np.ascontiguousarray(ref.fp8_e4m3_decode(ek) * np.float32(ks)),
+                              np.ascontiguousarray(ref.fp8_e4m3_decode(ev) * np.float32(vs)),
+                              np.ascontiguousarray(tables.astype(np.uint32)), ctx.astype(np.uint32),
+                              D ** -0.5)
+    assert np.abs(out - exp).max() <= 2e-2
+
+
+def test_fp8_rejects_missing_scales_and_bs8_decode(cuda_device):
+    kc, vc = _u8_cache(4, 8, cuda_device)
+    q = torch.zeros(1, HQ, D, dtype=torch.bfloat16, device=cuda_device)
+    t = torch.ones(1, 1, dtype=torch.int32, device=cuda_device)
+    c = torch.ones(1, dtype=torch.int32, device=cuda_device)
+    with pytest.raises(_lib.VasrPaError):
+        pa.paged_attention(q, None, None, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), t, c,
+                           None, 8, 0.1, 1.0, None)
+    sk, sv = _scales(cuda_device, 1.0, 1.0)
+    with pytest.raises(_lib.VasrPaError) as e:
+        pa.paged_attention(q, sk, sv, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), t, c,
+                           None, 8, 0.1, 1.0, None)
+    assert e.value.status == _lib.ENOT_SUPPORTED
