@@ -61,7 +61,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kernel", default=None,
-                   choices=["decode", "append", "prefill", "copy", "swap", "config1"],
+                   choices=["decode", "decode_fp8", "append", "prefill", "copy", "swap", "config1"],
                    help="microbenchmark one kernel on its BASELINE config instead of the decode step")
     p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
     p.add_argument("--layers", type=int, default=28,
@@ -574,6 +574,33 @@ def run_kernel_bench(args):
             alg = 4 * hkv * d * 4 * 2 * 2
             lines.append({"kernel": "kv_append", "config": "config1", "us": ms * 1e3, "bytes": alg,
                           "GB/s": alg / ms / 1e6})
+    elif k == "decode_fp8":
+        # config 2 shapes over fp8 (E4M3) pages with per-tensor scales (half the KV bytes)
+        lens = context_lens(args.seed, 0)
+        nb = sum(-(-int(n) // bs) for n in lens) + 1
+        layers = args.layers
+        caches = []
+        for _ in range(layers):
+            kc = (torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn)
+            vc = (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)
+            caches.append((kc, vc))
+        sk = torch.tensor([0.125], device=dev)
+        sv = torch.tensor([0.125], device=dev)
+        t = torch.from_numpy(tables_for(lens, nb)).to(dev)
+        ctx = torch.from_numpy(lens.astype(np.int32)).to(dev)
+        q = torch.randn(len(lens), hq, d, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+
+        def launch(i):
+            kc, vc = caches[i % layers]
+            pa.paged_attention(q, sk, sv, kc, vc, t, ctx, None, int(lens.max()), d ** -0.5, 1.0, None,
+                               out=out)
+
+        ms = _events_time(launch, args.iters)
+        alg = int(lens.sum()) * hkv * d * 2 + q.numel() * 2 * 2
+        lines.append({"kernel": "paged_decode_fp8", "config": "config2 shapes, fp8 E4M3 pages",
+                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
+                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "layers_cycled": layers})
     elif k == "append":
         for name, ntok, per_seq in (("config2_decode", 64, 1), ("config3_chunk", 32 * 256, 256)):
             nb = ntok // per_seq * (-(-per_seq // bs)) + 16 + 1

@@ -183,6 +183,16 @@ __device__ __forceinline__ float warp_sum_xor(float v, int lanes) {
   return v;
 }
 
+// d0 += a0 * b0, d1 += a1 * b1 as one sm_100 packed f32x2 FMA (each lane a
+// fused multiply-add rounded to nearest, exactly as fmaf).
+__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rd;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 constexpr float kLog2e = 1.4426950408889634f;
 
 }  // namespace vasr

@@ -3,7 +3,10 @@
 // GQA group 2 (Qwen3-ASR: 16 query / 8 kv heads) runs paged_decode_g2_kernel
 // (decode_g2.cuh); groups 1 and 4 run the generic paged_decode_kernel
 // (decode.cuh). Both use the same split-K workspace layout.
+#include <type_traits>
+
 #include "decode_g2.cuh"
+#include "decode_mma.cuh"
 #include "launch.h"
 
 // Launch-shape constants of the GQA-2 kernel (stages per CTA and resident
@@ -13,6 +16,10 @@
 #endif
 #ifndef VASR_G2_MINB
 #define VASR_G2_MINB 3
+#endif
+// GQA-2 bf16 / f16 pages: tensor-core score and P.V tiles (decode_mma.cuh)
+#ifndef VASR_DECODE_MMA
+#define VASR_DECODE_MMA 1
 #endif
 
 namespace vasr {
@@ -105,6 +112,14 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
   const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
   if (st != VASR_PA_OK) return st;
   const DecodeParams p = make_decode_params(a, w);
+  if constexpr (VASR_DECODE_MMA && std::is_same<T, TC>::value && !std::is_same<T, float>::value) {
+    auto kern = paged_decode_mma_kernel<T, BS, D, kNST, VASR_G2_MINB>;
+    static std::atomic<uint64_t> attr_done{0};
+    if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
+    dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+    kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(p);
+    return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+  }
   auto kern = paged_decode_g2_kernel<T, BS, D, kNST, VASR_G2_MINB, TC>;
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;

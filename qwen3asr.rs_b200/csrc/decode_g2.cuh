@@ -14,6 +14,9 @@
 
 #include "decode.cuh"
 
+#ifndef VASR_DECODE_FFMA2
+#define VASR_DECODE_FFMA2 1  // packed f32x2 FMAs (same rounding as two fmaf)
+#endif
 #ifndef VASR_DECODE_BALANCED
 #define VASR_DECODE_BALANCED 1  // share a sequence's pages evenly among its splits
 #endif
@@ -221,8 +224,13 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
             for (int e = 0; e < C::kX; e += 2) {
 #pragma unroll
               for (int g = 0; g < G; ++g) {
+#if VASR_DECODE_FFMA2
+                fma2(v0[r][g], v1[r][g], q_reg[g][c * C::kX + e], q_reg[g][c * C::kX + e + 1],
+                     kf[e], kf[e + 1]);
+#else
                 v0[r][g] = fmaf(q_reg[g][c * C::kX + e], kf[e], v0[r][g]);
                 v1[r][g] = fmaf(q_reg[g][c * C::kX + e + 1], kf[e + 1], v1[r][g]);
+#endif
               }
             }
           }
@@ -304,10 +312,15 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
             for (int e = 0; e < C::kTPS; ++e)
               if (seg_tok0 + e >= n_valid) vf[e] = 0.f;
           }
+#if VASR_DECODE_FFMA2
+#pragma unroll
+          for (int e = 0; e < C::kTPS; ++e) fma2(acc[i][0], acc[i][1], pw[0][e], pw[1][e], vf[e], vf[e]);
+#else
 #pragma unroll
           for (int g = 0; g < G; ++g)
 #pragma unroll
             for (int e = 0; e < C::kTPS; ++e) acc[i][g] = fmaf(pw[g][e], vf[e], acc[i][g]);
+#endif
         }
       }
     }

@@ -1,0 +1,338 @@
+// decode_mma.cuh — paged decode attention for GQA group 2 with the dot
+// products on the tensor cores (mma.sync m16n8k16, f32 accumulate).
+//
+// Same split-K decomposition, stage ring and merges as paged_decode_g2_kernel
+// (decode_g2.cuh); what differs is the per-stage math. The g2 kernel spends
+// ~400 instructions per warp on every 16 tokens (FMA dot products in f32 and
+// the shuffles around them), which — not the bytes — limits it: fp8 pages
+// (half the bytes) run no faster. Here a warp treats its 16 tokens as one
+// MMA tile:
+//   S[16 x 16] = Q[16 x 128] K^T   rows 0, 1 = the two query heads of the
+//                                  kv head, rows 2-15 zero; 8 k-steps x 2
+//                                  n-tiles, K read by ldmatrix straight from
+//                                  the K page ([D/8][bs][8]: a row of 8 dims
+//                                  of one token is one 16-byte ldmatrix row)
+//   O[16 x 128] += P[16 x 16] V    16 n-tiles of 8 dims, V read by ldmatrix
+//                                  from the V page ([D][bs]: 8 tokens of one
+//                                  dim per row)
+// ~100 instructions per 16 tokens. Only lanes 0-7 (rows 0 and 1) carry
+// results. The softmax keeps a per-row running maximum that moves only when
+// a tile's maximum exceeds it by more than 2^8 (O is then rescaled), exact in
+// real arithmetic because numerator and denominator share the offset.
+// Tokens past the split's end are masked in S and their V entries zeroed in
+// registers, so stale or non-finite page bytes never reach O.
+#pragma once
+
+#include "decode_g2.cuh"
+
+namespace vasr {
+
+__device__ __forceinline__ void dec_ldmatrix_x4(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                                uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <typename T>
+__device__ __forceinline__ void dec_mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void dec_mma<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                       uint32_t a2, uint32_t a3, uint32_t b0,
+                                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void dec_mma<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t dec_pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t dec_pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t dec_pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+template <typename T, int BS, int D, int NST, int MINB>
+__global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const DecodeParams p) {
+  using C = DecodeG2Cfg<T, BS, D, NST>;
+  constexpr int G = 2;
+  constexpr int kKS = D / 16;  // k-steps of the score MMA
+  constexpr float kRescale = 8.f;
+  extern __shared__ __align__(128) unsigned char smem[];
+  decode_g2_init_ring<T, BS, D, NST>(smem);
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = lane >> 2, tig = lane & 3;
+  const int P = p.pages_per_split * BS;
+
+  uint32_t spec_id = 0;
+  const int spec_col = split * p.pages_per_split + tid;
+  if (tid < p.pages_per_split && spec_col < p.cols)
+    spec_id = __ldg(p.block_tables + (int64_t)b * p.cols + spec_col);
+  // query fragments (A operand, rows = heads): lanes 0-7 hold rows 0 / 1
+  uint32_t qa[kKS][2];
+  {
+    const T *qp = reinterpret_cast<const T *>(p.q) + (int64_t)b * p.q_seq_stride +
+                  (int64_t)(kvh * G + (grp & 1)) * D;
+#pragma unroll
+    for (int ks = 0; ks < kKS; ++ks) {
+      qa[ks][0] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + tig * 2)) : 0u;
+      qa[ks][1] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + 8 + tig * 2)) : 0u;
+    }
+  }
+  int ctx = (int)p.context_lens[b];
+  const int cap_tables = p.cols * BS;
+  const int cap_splits = p.max_splits * P;
+  if (ctx > cap_tables || ctx > cap_splits) {
+    if (split == 0 && tid == 0) raise_device_error(VASR_PA_DERR_CTX_RANGE);
+    ctx = min(ctx, min(cap_tables, cap_splits));
+  }
+  T *out = reinterpret_cast<T *>(p.out) + ((int64_t)b * p.num_heads + (int64_t)kvh * G) * D;
+  if (ctx <= 0) {
+    if (split == 0)
+      for (int e = tid; e < G * D; e += C::kThreads) out[e] = Elem<T>::from_f32(0.f);
+    return;
+  }
+  const int n_splits = (ctx + P - 1) / P;
+  if (split >= n_splits) return;
+  const int seq_pages = (ctx + BS - 1) / BS;
+  const int per = (seq_pages + n_splits - 1) / n_splits;  // pages shared evenly by the splits
+  const int page_begin = split * per;
+  const int tok_begin = page_begin * BS;
+  const int tok_end = min(ctx, tok_begin + per * BS);
+  const int n_pages = (tok_end - tok_begin + BS - 1) / BS;
+  const int n_units = (n_pages + C::kSP - 1) / C::kSP;
+
+  const uint32_t s_base = smem_addr(smem);
+  uint32_t *blk = reinterpret_cast<uint32_t *>(smem + C::kOffBlk);
+  if (tid < n_pages) {
+    uint32_t id = spec_id;
+    if (page_begin != split * p.pages_per_split)
+      id = __ldg(p.block_tables + (int64_t)b * p.cols + page_begin + tid);
+    if ((int64_t)id >= p.num_blocks) {
+      raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
+      id = 0;
+    }
+    blk[tid] = id;
+  }
+  __syncthreads();
+
+  const T *kc = reinterpret_cast<const T *>(p.k_cache);
+  const T *vc = reinterpret_cast<const T *>(p.v_cache);
+  const int64_t page_elems = (int64_t)D * BS;
+  auto issue_unit = [&](int u) {
+    const int s = u % C::kNST;
+    const int pg0 = u * C::kSP;
+    const int np = min(C::kSP, n_pages - pg0);
+    const uint32_t bar = s_base + C::kOffBar + s * 8;
+    mbar_arrive_expect_tx(bar, (uint32_t)(2 * np * C::kPB));
+    for (int i = 0; i < np; ++i) {
+      const int64_t off = ((int64_t)blk[pg0 + i] * p.num_kv_heads + kvh) * page_elems;
+      bulk_g2s(s_base + C::kOffK + (s * C::kSP + i) * C::kPB, kc + off, C::kPB, bar);
+      bulk_g2s(s_base + C::kOffV + (s * C::kSP + i) * C::kPB, vc + off, C::kPB, bar);
+    }
+  };
+  if (lane == 0)
+    for (int u = warp; u < min(C::kNST, n_units); u += C::kWarps) issue_unit(u);
+
+  const float c_log2 = p.scale * kLog2e;
+  const bool use_softcap = (p.softcap != 1.0f) && (p.softcap > 0.f);
+  float o[D / 8][4];
+#pragma unroll
+  for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_used = -INFINITY, l_part = 0.f;  // row grp (lanes 0-7 meaningful)
+  bool aborted = false;
+
+  for (int u = warp; u < n_units; u += C::kWarps) {
+    const int s = u % C::kNST;
+    if (!mbar_wait_bounded(s_base + C::kOffBar + s * 8, (uint32_t)((u / C::kNST) & 1))) {
+      aborted = true;
+      break;
+    }
+    const int n_valid = min(C::kST, tok_end - (tok_begin + u * C::kST));
+    const uint32_t sk = s_base + C::kOffK + s * C::kSP * C::kPB;
+    const uint32_t sv = s_base + C::kOffV + s * C::kSP * C::kPB;
+#pragma unroll
+    for (int ti = 0; ti < C::kNTT; ++ti) {
+      const int t0 = ti * 16;  // first token of this 16-token tile within the stage
+      if (t0 >= n_valid) break;
+      // ---- S = Q K^T (two 8-token n-tiles)
+      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const int ktok = t0 + (lane & 7) + (lane >> 4) * 8;
+      const uint32_t krow = sk + (ktok / BS) * C::kPB + (ktok % BS) * 16 + ((lane >> 3) & 1) * (BS * 16);
+#pragma unroll
+      for (int ks = 0; ks < kKS; ++ks) {
+        uint32_t b0, b1, b2, b3;
+        dec_ldmatrix_x4(krow + ks * 2 * (BS * 16), b0, b1, b2, b3);
+        dec_mma<T>(sacc[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+        dec_mma<T>(sacc[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+      }
+      // ---- scores of row grp: tokens t0 + n*8 + tig*2 + {0, 1}
+      float x[4];
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float v = sacc[n][e];
+          if (use_softcap) v = p.softcap * tanhf(v * p.scale / p.softcap) * kLog2e;
+          else v *= c_log2;
+          x[n * 2 + e] = (t0 + n * 8 + tig * 2 + e < n_valid) ? v : -INFINITY;
+        }
+      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if (__any_sync(0xffffffffu, mx > m_used + kRescale)) {
+        const float m_new = fmaxf(m_used, mx);
+        const float alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
+        m_used = m_new;
+        l_part *= alpha;
+#pragma unroll
+        for (int j = 0; j < D / 8; ++j) {
+          o[j][0] *= alpha;
+          o[j][1] *= alpha;
+        }
+      }
+      const float off = (m_used == -INFINITY) ? 0.f : m_used;
+      float pv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pv[e] = exp2f(x[e] - off);
+        l_part += pv[e];
+      }
+      // P as the A operand (rows 8-15 zero): k = tokens of the tile
+      const uint32_t pa0 = dec_pack2<T>(pv[0], pv[1]), pa2 = dec_pack2<T>(pv[2], pv[3]);
+      // ---- O += P V: V rows = dims, 8 tokens per ldmatrix row
+      const int vd = (lane & 7) + (lane >> 4) * 8;
+      const int vtok = t0 + ((lane >> 3) & 1) * 8;
+      const uint32_t vrow = sv + (vtok / BS) * C::kPB + (vd * BS + vtok % BS) * 2;
+      const bool tail = (t0 + 16 > n_valid);
+      const int tk0 = t0 + tig * 2;  // tokens of b0 / b2 halves; b1 / b3: +8
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        dec_ldmatrix_x4(vrow + dp * 16 * BS * 2, b0, b1, b2, b3);
+        if (tail) {
+          const uint32_t m0 = (tk0 < n_valid ? 0xffffu : 0u) | (tk0 + 1 < n_valid ? 0xffff0000u : 0u);
+          const uint32_t m1 = (tk0 + 8 < n_valid ? 0xffffu : 0u) | (tk0 + 9 < n_valid ? 0xffff0000u : 0u);
+          b0 &= m0;
+          b2 &= m0;
+          b1 &= m1;
+          b3 &= m1;
+        }
+        dec_mma<T>(o[2 * dp], pa0, 0u, pa2, 0u, b0, b1);
+        dec_mma<T>(o[2 * dp + 1], pa0, 0u, pa2, 0u, b2, b3);
+      }
+    }
+    __syncwarp();
+    const int nu = u + C::kNST;
+    if (nu < n_units && lane == 0) {
+      fence_proxy_async_smem();
+      issue_unit(nu);
+    }
+  }
+
+  // ---- warp results -> shared memory (rows 0 and 1 live in lanes 0-7)
+  float l_row = l_part;
+  l_row += __shfl_xor_sync(0xffffffffu, l_row, 1);
+  l_row += __shfl_xor_sync(0xffffffffu, l_row, 2);
+  float *co = reinterpret_cast<float *>(smem + C::kOffCO);
+  float *cm = reinterpret_cast<float *>(smem + C::kOffCM);
+  float *cl = reinterpret_cast<float *>(smem + C::kOffCL);
+  if (aborted) {
+    m_used = -INFINITY;
+    l_row = 0.f;
+  }
+  if (grp < G) {
+    if (tig == 0) {
+      cm[warp * G + grp] = m_used;
+      cl[warp * G + grp] = l_row;
+    }
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) {
+      co[(warp * G + grp) * D + j * 8 + tig * 2] = aborted ? 0.f : o[j][0];
+      co[(warp * G + grp) * D + j * 8 + tig * 2 + 1] = aborted ? 0.f : o[j][1];
+    }
+  }
+  __syncthreads();
+
+  const int64_t bk = (int64_t)b * p.num_kv_heads + kvh;
+  const bool single = (n_splits == 1);
+#pragma unroll
+  for (int e0 = 0; e0 < G * D; e0 += C::kThreads) {
+    const int e = e0 + tid;
+    const int g = e / D;
+    const int d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < C::kWarps; ++w) M = fmaxf(M, cm[w * G + g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < C::kWarps; ++w) {
+        const float f = exp2f(cm[w * G + g] - M);
+        L = fmaf(cl[w * G + g], f, L);
+        O = fmaf(co[(w * G + g) * D + d], f, O);
+      }
+    }
+    if (single) {
+      out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L : 0.f);
+    } else {
+      const int64_t slot = bk * p.max_splits + split;
+      p.ws_o[(slot * G + g) * D + d] = O;
+      if (d == 0) p.ws_ml[slot * G + g] = make_float2(M, L);
+    }
+  }
+  if (single) return;
+
+  __syncthreads();
+  uint32_t *flag = reinterpret_cast<uint32_t *>(smem + C::kOffFlag);
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(p.counters + bk, 1u);
+    __threadfence();
+    flag[0] = (prev == (uint32_t)(n_splits - 1)) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (flag[0] == 0u) return;
+#pragma unroll
+  for (int e0 = 0; e0 < G * D; e0 += C::kThreads) {
+    const int e = e0 + tid;
+    const int g = e / D;
+    const int d = e % D;
+    const int64_t slot0 = bk * p.max_splits;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < n_splits; ++s2) M = fmaxf(M, __ldcg(&p.ws_ml[(slot0 + s2) * G + g].x));
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int s2 = 0; s2 < n_splits; ++s2) {
+        const float2 ml = __ldcg(&p.ws_ml[(slot0 + s2) * G + g]);
+        const float w = exp2f(ml.x - M);
+        L = fmaf(ml.y, w, L);
+        O = fmaf(__ldcg(&p.ws_o[((slot0 + s2) * G + g) * D + d]), w, O);
+      }
+    }
+    out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L : 0.f);
+  }
+  if (tid == 0) p.counters[bk] = 0u;
+}
+
+}  // namespace vasr
