@@ -456,7 +456,7 @@ def run_ours(args):
                        "seq_len": int(lens0.mean()), "parallelism": f"dp{world} (request-sharded)",
                        "graph_cols": cols, "l2": "inputs larger than L2 (per step ~6.2 GB KV + 1.2 GB weights)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "kernel": "paged_decode_g2_kernel",
+                         "frac": achieved / peak, "traffic": traffic, "kernel": "paged_decode_mma_kernel",
                          "peak_source": peak_kind, "launch_us": launch_ms * 1e3,
                          "algorithmic_bytes_per_launch": alg_bytes},
             "cpu_baseline": cpu,

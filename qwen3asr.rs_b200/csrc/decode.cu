@@ -29,7 +29,12 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_heads,
                                         int head_dim, int block_size, int max_context_len) {
   DecodeWorkspace w;
-  w.pages_per_split = decode_pages_per_split(num_seqs, num_kv_heads, block_size, max_context_len);
+  // GQA 2 (bf16 / f16 run the tensor-core kernel) takes longer splits
+  const int split_tokens = (num_kv_heads > 0 && num_heads == 2 * num_kv_heads)
+                               ? VASR_DECODE_SPLIT_TOKENS_G2
+                               : VASR_DECODE_SPLIT_TOKENS;
+  w.pages_per_split =
+      decode_pages_per_split(num_seqs, num_kv_heads, block_size, max_context_len, split_tokens);
   const int P = w.pages_per_split * block_size;
   w.max_splits = (max_context_len + P - 1) / P;
   if (w.max_splits < 1) w.max_splits = 1;

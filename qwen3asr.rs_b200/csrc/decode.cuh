@@ -433,23 +433,30 @@ __global__ void __launch_bounds__(128, 2) paged_decode_kernel(const DecodeParams
 }
 
 // Split size chosen from host-visible arguments only, so that the workspace
-// size and the launch always agree: VASR_DECODE_SPLIT_TOKENS tokens per split,
-// halved (down to 64) while fewer than 2 CTAs per B200 SM would be launched.
-// 512 measured best on B200 for config 2 (46.8 us vs 50.7 us at 256, 47.6 at
-// 768, 49.8 at 1024): fewer CTA start-ups per byte, still ~2 waves of CTAs.
+// size and the launch always agree: `split_tokens` tokens per split, halved
+// (down to 64) while fewer than 2 CTAs per B200 SM would be launched, and at
+// most kDecodeMaxPagesPerSplit pages. Measured on B200 for config 2: the
+// tensor-core GQA-2 kernel is fastest at 1024 (41.6 us vs 42.6 at 768 and
+// 44.0 at 512), the CUDA-core kernels at 512 (46.8 us vs 50.7 at 256, 47.6 at
+// 768, 49.8 at 1024).
 #ifndef VASR_DECODE_SPLIT_TOKENS
 #define VASR_DECODE_SPLIT_TOKENS 512
 #endif
+#ifndef VASR_DECODE_SPLIT_TOKENS_G2
+#define VASR_DECODE_SPLIT_TOKENS_G2 1024
+#endif
+constexpr int kDecodeMaxPagesPerSplit = 64;
 inline int decode_pages_per_split(int num_seqs, int num_kv_heads, int block_size,
-                                  int max_context_len) {
+                                  int max_context_len, int split_tokens) {
   const int kTargetCtas = 2 * 148;
-  int tokens = VASR_DECODE_SPLIT_TOKENS;
+  int tokens = split_tokens;
   auto ctas = [&](int t) {
     return (int64_t)num_seqs * num_kv_heads * ((max_context_len + t - 1) / t);
   };
   while (tokens > 64 && ctas(tokens) < kTargetCtas) tokens >>= 1;
   if (tokens < block_size) tokens = block_size;
   int pps = tokens / block_size;
+  if (pps > kDecodeMaxPagesPerSplit) pps = kDecodeMaxPagesPerSplit;
   if (pps < 1) pps = 1;
   return pps;
 }
