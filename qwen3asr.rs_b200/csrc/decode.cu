@@ -117,8 +117,10 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
   const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
   if (st != VASR_PA_OK) return st;
   const DecodeParams p = make_decode_params(a, w);
-  if constexpr (VASR_DECODE_MMA && std::is_same<T, TC>::value && !std::is_same<T, float>::value) {
-    auto kern = paged_decode_mma_kernel<T, BS, D, kNST, VASR_G2_MINB>;
+  constexpr bool kMma = VASR_DECODE_MMA && !std::is_same<T, float>::value &&
+                        (std::is_same<T, TC>::value || BS >= 16);
+  if constexpr (kMma) {
+    auto kern = paged_decode_mma_kernel<T, BS, D, kNST, VASR_G2_MINB, TC>;
     static std::atomic<uint64_t> attr_done{0};
     if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
     dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);

@@ -23,6 +23,8 @@
 // registers, so stale or non-finite page bytes never reach O.
 #pragma once
 
+#include <type_traits>
+
 #include "decode_g2.cuh"
 
 namespace vasr {
@@ -70,14 +72,32 @@ __device__ __forceinline__ uint32_t dec_pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-template <typename T, int BS, int D, int NST, int MINB>
+// fp8 E4M3 pair -> f16 pair (exact), as one 32-bit A/B fragment register
+__device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t v16) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v16 & 0xffffu), __NV_E4M3);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// TC = T: bf16 / f16 pages, the MMAs in T. TC = fp8 E4M3 (bs 16 or 32): the
+// MMAs run in f16 on pages converted in registers, and the reduction index is
+// permuted so one ldmatrix row of 16 fp8 bytes feeds one k-step: lane tig
+// holds dims / tokens 4 tig .. 4 tig + 3 of its row, used as the logical
+// k = 2 tig, 2 tig + 1 (low pair) and 2 tig + 8, 2 tig + 9 (high pair). Q
+// fragments follow the same permutation over dims; the score tiles list their
+// tokens as n-tile 0 = {0,1,4,5,8,9,12,13}, n-tile 1 = {2,3,6,7,...}, so that
+// P's C fragments are already the A fragments of the P V product over the
+// same permuted token order.
+template <typename T, int BS, int D, int NST, int MINB, typename TC = T>
 __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const DecodeParams p) {
-  using C = DecodeG2Cfg<T, BS, D, NST>;
+  constexpr bool kFp8 = std::is_same<TC, __nv_fp8_e4m3>::value;
+  using TM = typename std::conditional<kFp8, __half, T>::type;  // MMA operand type
+  using C = DecodeG2Cfg<TC, BS, D, NST>;
   constexpr int G = 2;
   constexpr int kKS = D / 16;  // k-steps of the score MMA
   constexpr float kRescale = 8.f;
+  static_assert(!kFp8 || BS >= 16, "fp8 pages need 16-byte V rows");
   extern __shared__ __align__(128) unsigned char smem[];
-  decode_g2_init_ring<T, BS, D, NST>(smem);
+  decode_g2_init_ring<TC, BS, D, NST>(smem);
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -95,8 +115,17 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
                   (int64_t)(kvh * G + (grp & 1)) * D;
 #pragma unroll
     for (int ks = 0; ks < kKS; ++ks) {
-      qa[ks][0] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + tig * 2)) : 0u;
-      qa[ks][1] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + 8 + tig * 2)) : 0u;
+      if constexpr (kFp8) {  // dims 4 tig .. 4 tig + 3 of the k-step, as f16 pairs
+        qa[ks][0] = qa[ks][1] = 0u;
+        if (grp < G) {
+          const T *q4 = qp + ks * 16 + tig * 4;
+          qa[ks][0] = dec_pack2<__half>(Elem<T>::to_f32(q4[0]), Elem<T>::to_f32(q4[1]));
+          qa[ks][1] = dec_pack2<__half>(Elem<T>::to_f32(q4[2]), Elem<T>::to_f32(q4[3]));
+        }
+      } else {
+        qa[ks][0] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + tig * 2)) : 0u;
+        qa[ks][1] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + 8 + tig * 2)) : 0u;
+      }
     }
   }
   int ctx = (int)p.context_lens[b];
@@ -136,8 +165,8 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
   }
   __syncthreads();
 
-  const T *kc = reinterpret_cast<const T *>(p.k_cache);
-  const T *vc = reinterpret_cast<const T *>(p.v_cache);
+  const TC *kc = reinterpret_cast<const TC *>(p.k_cache);
+  const TC *vc = reinterpret_cast<const TC *>(p.v_cache);
   const int64_t page_elems = (int64_t)D * BS;
   auto issue_unit = [&](int u) {
     const int s = u % C::kNST;
@@ -154,7 +183,10 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
   if (lane == 0)
     for (int u = warp; u < min(C::kNST, n_units); u += C::kWarps) issue_unit(u);
 
-  const float c_log2 = p.scale * kLog2e;
+  // fp8 pages hold K / k_scale and V / v_scale
+  const float k_mul = p.k_scale ? p.scale * __ldg(p.k_scale) : p.scale;
+  const float v_mul = p.v_scale ? __ldg(p.v_scale) : 1.f;
+  const float c_log2 = k_mul * kLog2e;
   const bool use_softcap = (p.softcap != 1.0f) && (p.softcap > 0.f);
   float o[D / 8][4];
 #pragma unroll
@@ -177,14 +209,32 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
       if (t0 >= n_valid) break;
       // ---- S = Q K^T (two 8-token n-tiles)
       float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      const int ktok = t0 + (lane & 7) + (lane >> 4) * 8;
-      const uint32_t krow = sk + (ktok / BS) * C::kPB + (ktok % BS) * 16 + ((lane >> 3) & 1) * (BS * 16);
+      if constexpr (kFp8) {
+        // matrices: (n-tile 0, chunk 2kp), (n-tile 1, 2kp), (n-tile 0, 2kp+1), (n-tile 1, 2kp+1)
+        const int r = lane & 7;
+        const int ktok = t0 + 4 * (r >> 1) + 2 * ((lane >> 3) & 1) + (r & 1);
+        const uint32_t krow = sk + (ktok / BS) * C::kPB + ((lane >> 4) * BS + ktok % BS) * 16;
 #pragma unroll
-      for (int ks = 0; ks < kKS; ++ks) {
-        uint32_t b0, b1, b2, b3;
-        dec_ldmatrix_x4(krow + ks * 2 * (BS * 16), b0, b1, b2, b3);
-        dec_mma<T>(sacc[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
-        dec_mma<T>(sacc[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+        for (int kp = 0; kp < kKS / 2; ++kp) {
+          uint32_t r0, r1, r2, r3;
+          dec_ldmatrix_x4(krow + kp * 2 * (BS * 16), r0, r1, r2, r3);
+          dec_mma<TM>(sacc[0], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r0), fp8x2_to_h2(r0 >> 16));
+          dec_mma<TM>(sacc[1], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r1), fp8x2_to_h2(r1 >> 16));
+          dec_mma<TM>(sacc[0], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r2),
+                      fp8x2_to_h2(r2 >> 16));
+          dec_mma<TM>(sacc[1], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r3),
+                      fp8x2_to_h2(r3 >> 16));
+        }
+      } else {
+        const int ktok = t0 + (lane & 7) + (lane >> 4) * 8;
+        const uint32_t krow = sk + (ktok / BS) * C::kPB + (ktok % BS) * 16 + ((lane >> 3) & 1) * (BS * 16);
+#pragma unroll
+        for (int ks = 0; ks < kKS; ++ks) {
+          uint32_t b0, b1, b2, b3;
+          dec_ldmatrix_x4(krow + ks * 2 * (BS * 16), b0, b1, b2, b3);
+          dec_mma<TM>(sacc[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+          dec_mma<TM>(sacc[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+        }
       }
       // ---- scores of row grp: tokens t0 + n*8 + tig*2 + {0, 1}
       float x[4];
@@ -195,7 +245,8 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
           float v = sacc[n][e];
           if (use_softcap) v = p.softcap * tanhf(v * p.scale / p.softcap) * kLog2e;
           else v *= c_log2;
-          x[n * 2 + e] = (t0 + n * 8 + tig * 2 + e < n_valid) ? v : -INFINITY;
+          const int tok = kFp8 ? t0 + 4 * tig + 2 * n + e : t0 + n * 8 + tig * 2 + e;
+          x[n * 2 + e] = (tok < n_valid) ? v : -INFINITY;
         }
       float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -219,12 +270,36 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
         l_part += pv[e];
       }
       // P as the A operand (rows 8-15 zero): k = tokens of the tile
-      const uint32_t pa0 = dec_pack2<T>(pv[0], pv[1]), pa2 = dec_pack2<T>(pv[2], pv[3]);
+      const uint32_t pa0 = dec_pack2<TM>(pv[0], pv[1]), pa2 = dec_pack2<TM>(pv[2], pv[3]);
+      const bool tail = (t0 + 16 > n_valid);
+      if constexpr (kFp8) {
+        // ---- O += P V: one ldmatrix row = the tile's 16 tokens of one dim;
+        // matrix j of an x4 = 8 dims, lane tig holds tokens 4 tig .. 4 tig + 3
+        const int vd = (lane >> 3) * 8 + (lane & 7);
+        const uint32_t vrow = sv + (t0 / BS) * C::kPB + vd * BS + t0 % BS;
+        const int tk = t0 + 4 * tig;
+        const uint32_t mlo = (tk < n_valid ? 0xffffu : 0u) | (tk + 1 < n_valid ? 0xffff0000u : 0u);
+        const uint32_t mhi = (tk + 2 < n_valid ? 0xffffu : 0u) | (tk + 3 < n_valid ? 0xffff0000u : 0u);
+#pragma unroll
+        for (int dq = 0; dq < D / 32; ++dq) {
+          uint32_t r[4];
+          dec_ldmatrix_x4(vrow + dq * 32 * BS, r[0], r[1], r[2], r[3]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t b0 = fp8x2_to_h2(r[j]), b1 = fp8x2_to_h2(r[j] >> 16);
+            if (tail) {
+              b0 &= mlo;
+              b1 &= mhi;
+            }
+            dec_mma<TM>(o[dq * 4 + j], pa0, 0u, pa2, 0u, b0, b1);
+          }
+        }
+        continue;
+      }
       // ---- O += P V: V rows = dims, 8 tokens per ldmatrix row
       const int vd = (lane & 7) + (lane >> 4) * 8;
       const int vtok = t0 + ((lane >> 3) & 1) * 8;
       const uint32_t vrow = sv + (vtok / BS) * C::kPB + (vd * BS + vtok % BS) * 2;
-      const bool tail = (t0 + 16 > n_valid);
       const int tk0 = t0 + tig * 2;  // tokens of b0 / b2 halves; b1 / b3: +8
 #pragma unroll
       for (int dp = 0; dp < D / 16; ++dp) {
@@ -238,8 +313,8 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
           b1 &= m1;
           b3 &= m1;
         }
-        dec_mma<T>(o[2 * dp], pa0, 0u, pa2, 0u, b0, b1);
-        dec_mma<T>(o[2 * dp + 1], pa0, 0u, pa2, 0u, b2, b3);
+        dec_mma<TM>(o[2 * dp], pa0, 0u, pa2, 0u, b0, b1);
+        dec_mma<TM>(o[2 * dp + 1], pa0, 0u, pa2, 0u, b2, b3);
       }
     }
     __syncwarp();
@@ -294,7 +369,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
       }
     }
     if (single) {
-      out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L : 0.f);
+      out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L * v_mul : 0.f);
     } else {
       const int64_t slot = bk * p.max_splits + split;
       p.ws_o[(slot * G + g) * D + d] = O;
@@ -330,7 +405,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
         O = fmaf(__ldcg(&p.ws_o[((slot0 + s2) * G + g) * D + d]), w, O);
       }
     }
-    out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L : 0.f);
+    out[g * D + d] = Elem<T>::from_f32(L > 0.f ? O / L * v_mul : 0.f);
   }
   if (tid == 0) p.counters[bk] = 0u;
 }
