@@ -17,12 +17,15 @@
 // Warp roles (192 threads): warps 0-3 own TMEM lanes 0-127 (one row per
 // thread: softmax, O rescale, epilogue); warp 4 issues the MMAs; warp 5
 // stages Q, K and V with TMA. S is double-buffered in TMEM, so Q K^T of
-// tile j + 1 is ready while the softmax warps work on tile j.
+// tile j + 1 is ready while the softmax warps work on tile j, and the
+// softmax of tile j + 1 does not wait for P V of tile j unless O needs a
+// rescale.
 //
 // Shared-memory operand layouts (all "K-major", the reduction dim inside a
 // 16-byte chunk):
-//   Q  [16 dim chunks][128 rows][16 B]   no swizzle, LBO 2048, SBO 128; one
-//      4-D TMA load (chunk x token x head x 8 elements)
+//   Q  [2 dim halves][128 rows][128 B]   the 128-byte swizzle (SBO 1024),
+//      the canonical SW128 K-major layout; one 3-D TMA load per half
+//      (64 elements x head x token), 128-byte rows
 //   K  [16 dim chunks][64 keys][16 B]    no swizzle, LBO 1024, SBO 128; per
 //      dim chunk one TMA gather4 of that chunk's 256-byte row in 4 pages
 //   V  one page = [128 dims][16 tokens] rows of 32 B, one 2-D TMA load with
@@ -59,12 +62,15 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVTile;
 constexpr int kOffBar = kOffV + kStages * kKVTile;
-constexpr int kBarFullK = 0, kBarFullV = 2, kBarEmptyK = 4, kBarEmptyV = 6, kBarSFull = 8,
-              kBarPFull = 10, kBarPvDone = 12, kBarQ = 13;
-constexpr int kNumBars = 14;
+// One commit per MMA group: "Q K^T j done" both fills S j and frees K
+// stage j & 1; "P V j done" both frees V stage j & 1 and the S buffer of j.
+constexpr int kBarFullK = 0, kBarFullV = 2, kBarSFull = 4, kBarPFull = 6, kBarPvDone = 8,
+              kBarQ = 10;
+constexpr int kBarEmptyK = kBarSFull, kBarEmptyV = kBarPvDone;
+constexpr int kNumBars = 11;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemUsed = kOffTmemSlot + 16;
-constexpr int kSmemAlign = 256;              // SW32 pages need 256-byte alignment
+constexpr int kSmemAlign = 1024;             // SW128 Q tile: 1024-byte alignment
 constexpr int kSmemBytes = kSmemUsed + kSmemAlign;
 constexpr int kTmemCols = 256;               // S ring 2 x 64 columns + O 128 columns
 constexpr int kTmemS = 0, kTmemO = 128;
@@ -93,28 +99,35 @@ __device__ __forceinline__ uint32_t idesc_f16(int n) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(kM >> 4) << 24);
 }
+// The MMA helpers are called by a whole converged warp with warp-uniform
+// operands; elect.sync picks the issuing lane inside the asm (always the
+// same lane, so its commits track its own MMAs). Issued this way an MMA
+// costs about half the issue time of one issued from a single-lane branch.
 // A from tensor memory: row i in lane i, 16-bit K pairs packed per 32-bit column.
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
                                             uint32_t idesc, uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// Arrive (count 1) on `bar` once every tcgen05 op issued so far by this thread completed.
+// Arrive (count 1) on `bar` once every tcgen05 op issued so far by the
+// elected lane completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
+          bar)
+      : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -219,14 +232,39 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map
       "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
       : "memory");
 }
-// 4-D tiled TMA load (the Q tile: 16-byte chunks x heads x tokens x chunk index).
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
-                                            int c2, int c3, uint32_t bar) {
+// 3-D tiled TMA load (the Q tile: 64 elements x heads x tokens).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
-      "[%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
+      "[%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
+}
+
+// Zero tokens >= valid of one V page in the SW32 layout (a 32-byte row per
+// dim; the 16-byte half with tokens 8h..8h+7 of dim d sits at half
+// h ^ ((d >> 2) & 1), token 8h + e at byte 2e). One warp, 16-byte accesses.
+__device__ __forceinline__ void zero_v_page_tail(unsigned char *vp, int valid, int lane) {
+#pragma unroll
+  for (int i = 0; i < kD / 32; ++i) {
+    const int d = lane + 32 * i;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int lo = valid - 8 * h;  // tokens 8h + e with e < lo stay
+      if (lo >= 8) continue;
+      uint4 *c = reinterpret_cast<uint4 *>(vp + d * 32 + ((h ^ ((d >> 2) & 1)) * 16));
+      if (lo <= 0) {
+        *c = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      uint4 v = *c;
+      uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = (2 * e >= lo) ? 0u : (2 * e + 1 >= lo) ? (w[e] & 0xFFFFu) : w[e];
+      *c = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
 }
 
 template <typename T>
@@ -315,7 +353,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int i = 0; i < kNumBars; ++i) mbar_init(B(i), (i == kBarPFull || i == kBarPFull + 1) ? 4 * 32 : 1);
       mbar_fence_init();
       mbar_arrive_expect_tx(B(kBarQ), (uint32_t)kQBytes);
-      tma_load_4d(sbase + kOffQ, &q_map, 0, kvh * G, (int)(q0 + i0), 0, B(kBarQ));
+      tma_load_3d(sbase + kOffQ, &q_map, 0, kvh * G, (int)(q0 + i0), B(kBarQ));
+      tma_load_3d(sbase + kOffQ + kQBytes / 2, &q_map, kD / 2, kvh * G, (int)(q0 + i0), B(kBarQ));
     }
     __syncwarp();
     auto tile_page = [&](int j, int &np) -> uint32_t {  // page id of tile j held by this lane
@@ -397,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffTmemSlot);
+  const uint32_t tmem = *reinterpret_cast<const uint32_t *>(smem + kOffTmemSlot);
   bool dead = false;  // this warp gave up on a wait
 
   if (warp == kMmaWarp) {
@@ -408,15 +447,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     auto issue_s = [&](int j) {  // S(j & 1) = Q K_j^T
       wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
       tc_fence_after();
-      if (lane == 0) {
+      {
         const uint32_t sk = sbase + kOffK + (j & 1) * kKVTile;
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks)
           umma_f16(tmem + kTmemS + (j & 1) * kNT,
-                   sdesc(sbase + kOffQ + ks * 2 * (kM * 16), kM * 16, 128, 0),
+                   sdesc(sbase + kOffQ + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32, 16, 1024, 2),
                    sdesc(sk + ks * 2 * (kNT * 16), kNT * 16, 128, 0), idesc_s, ks > 0);
-        umma_commit(B(kBarSFull + (j & 1)));
-        umma_commit(B(kBarEmptyK + (j & 1)));
+        umma_commit(B(kBarSFull + (j & 1)));  // = kBarEmptyK
       }
       __syncwarp();
     };
@@ -430,35 +468,27 @@ __global__ void __launch_bounds__(kThreads, 2)
         // non-finite); zero it so that P = 0 there contributes exactly 0.
         const int pl = (kv_end - 1) / kBS - j * kPagesPerTile;
         const int valid = kv_end - (j * kPagesPerTile + pl) * kBS;
-        unsigned char *vp = smem + kOffV + (j & 1) * kKVTile + pl * kPageBytes;
-        for (int e = lane; e < kD * kBS; e += 32) {
-          const int d = e >> 4, key = e & 15;
-          if (key >= valid) {
-            const int chunk = (key >> 3) ^ ((d >> 2) & 1);  // 32-byte swizzle
-            *reinterpret_cast<uint16_t *>(vp + d * 32 + chunk * 16 + (key & 7) * 2) = 0;
-          }
-        }
+        zero_v_page_tail(smem + kOffV + (j & 1) * kKVTile + pl * kPageBytes, valid, lane);
         fence_proxy_async_smem();
         __syncwarp();
       }
       // P of tile j (a ring of two: the softmax warps may run one tile ahead)
       wait_phase(B(kBarPFull + (j & 1)), (j >> 1) & 1, dead);
       tc_fence_after();
-      if (lane == 0) {
+      {
         const int np = min(kPagesPerTile, n_pages - j * kPagesPerTile);
         const uint32_t sv = sbase + kOffV + (j & 1) * kKVTile;
         for (int pg = 0; pg < np; ++pg)
           umma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * kNT + pg * (kBS / 2),
                       sdesc(sv + pg * kPageBytes, 16, 256, 6), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
-        umma_commit(B(kBarEmptyV + (j & 1)));
-        umma_commit(B(kBarPvDone));
+        umma_commit(B(kBarPvDone + (j & 1)));  // = kBarEmptyV
       }
       __syncwarp();
       if (j + 2 < n_kt) {
         // Q K^T j + 2 overwrites the S buffer that holds P j: the tensor core
         // does not order a later MMA's D writes after an earlier MMA's TMEM A
         // reads, so P V j must have completed first.
-        wait_phase(B(kBarPvDone), j & 1, dead);
+        wait_phase(B(kBarPvDone + (j & 1)), (j >> 1) & 1, dead);
         tc_fence_after();
         issue_s(j + 2);
       }
@@ -518,13 +548,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       pk[k] = pack2f<T>(p0, p1);
     }
     l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
-    if (j > 0) {
-      // Wait for P V of the previous tile every tile, also when O needs no
-      // rescale: a parity wait is only exact while the barrier is at most one
-      // phase away, and the epilogue relies on it.
-      wait_phase(B(kBarPvDone), (j - 1) & 1, dead);
+    if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      // O moves to the new offset once P V of the previous tile is complete.
+      // P V completion has one barrier per S buffer and this thread skips
+      // the waits it does not need: the barrier of P V j - 1 is never two
+      // phases away, since P V j - 3 completed before Q K^T j - 1 (whose S
+      // this thread already read) and P V j + 1 needs this thread's P.
+      wait_phase(B(kBarPvDone + ((j - 1) & 1)), ((j - 1) >> 1) & 1, dead);
       tc_fence_after();
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      {
 #pragma unroll 1
         for (int cc = 0; cc < kD; cc += 32) {
           uint32_t o[32];
@@ -539,6 +571,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // P (16-bit pairs) replaces the first 32 columns of its S buffer; P V of
     // the tile two back, which read them last, completed before this S did.
+    // P V of the previous tile may still run: it reads the other buffer and
+    // accumulates into O, which this store does not touch.
     tmem_st32(ts, pk);
     tmem_wait_st();
     tc_fence_before();
@@ -546,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---- epilogue: O / l -> out (the last P V commit covers every MMA)
-  wait_phase(B(kBarPvDone), (n_kt - 1) & 1, dead);
+  wait_phase(B(kBarPvDone + ((n_kt - 1) & 1)), ((n_kt - 1) >> 1) & 1, dead);
   tc_fence_after();
   const float inv = l > 0.f ? 1.f / l : 0.f;
   T *dst = out + (q0 + i0 + r / G) * row_stride + (int64_t)(kvh * G + r % G) * kD;
@@ -625,20 +659,20 @@ bool make_k_map(CUtensorMap *map, const void *k_cache, int64_t num_blocks, int n
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Q viewed as [16 dim chunks][tokens][heads][8 elements]: a box of
-// (8, G, 128 / G, 16) lands as [chunk][position][head][16 B], the canonical
-// no-swizzle K-major layout of the CTA's 128 rows (row = position * G + head).
-// Rows past the last token read zeros.
+// Q viewed as [tokens][heads][128 elements]: a box of (64, G, 128 / G) at
+// element offset 0 or 64 lands as 128 rows (row = position * G + head) of
+// 128 bytes with the 128-byte swizzle, half of the CTA's Q in the canonical
+// SW128 K-major layout. Rows past the last token read zeros.
 bool make_q_map(CUtensorMap *map, const PrefillArgs &a, int g) {
   EncodeTiledFn enc = tensor_map_encoder();
   if (!enc) return false;
-  const cuuint64_t dims[4] = {8, (cuuint64_t)a.num_heads, (cuuint64_t)a.total_q_tokens, kD / 8};
-  const cuuint64_t strides[3] = {(cuuint64_t)kD * 2, (cuuint64_t)a.q_token_stride * 2, 16};
-  const cuuint32_t box[4] = {8, (cuuint32_t)g, (cuuint32_t)(kM / g), kD / 8};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const cuuint64_t dims[3] = {kD, (cuuint64_t)a.num_heads, (cuuint64_t)a.total_q_tokens};
+  const cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)a.q_token_stride * 2};
+  const cuuint32_t box[3] = {kD / 2, (cuuint32_t)g, (cuuint32_t)(kM / g)};
+  const cuuint32_t estr[3] = {1, 1, 1};
   std::memset(map, 0, sizeof(*map));
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void *>(a.query), dims, strides,
-             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void *>(a.query), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -666,6 +700,12 @@ int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s) {
   if ((int64_t)a.num_blocks * a.num_kv_heads * kD >= (int64_t(1) << 31))
     return VASR_PA_ENOT_SUPPORTED;  // int32 TMA row coordinates
   if (a.total_q_tokens >= (int64_t(1) << 31)) return VASR_PA_ENOT_SUPPORTED;
+  // tensor maps want 16-byte aligned bases and strides; other views take the
+  // mma.sync kernel
+  if ((reinterpret_cast<uintptr_t>(a.query) | reinterpret_cast<uintptr_t>(a.key_cache) |
+       reinterpret_cast<uintptr_t>(a.value_cache)) % 16 != 0 ||
+      (a.q_token_stride * 2) % 16 != 0)
+    return VASR_PA_ENOT_SUPPORTED;
   CUtensorMap qmap, kmap, map;
   if (!make_v_map(&map, a.value_cache, a.num_blocks, a.num_kv_heads)) return VASR_PA_ELAUNCH;
   if (!make_k_map(&kmap, a.key_cache, a.num_blocks, a.num_kv_heads)) return VASR_PA_ELAUNCH;
