@@ -292,16 +292,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t sbase = (raw + kSmemAlign - 1) & ~(uint32_t)(kSmemAlign - 1);
   unsigned char *smem = smem_raw + (sbase - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kvh = blockIdx.y;
+  // ---- work item: blockIdx.x = (r * num_seqs + b) * Hkv + kv head, tile =
+  // tiles - 1 - r. The hardware hands out CTAs in index order, so every
+  // sequence's last position tile (the one with the most keys) goes first
+  // and the kv heads of one (sequence, tile) run side by side.
+  const int kvh = (int)(blockIdx.x % (unsigned)p.num_kv_heads);
+  const int item = (int)(blockIdx.x / (unsigned)p.num_kv_heads);
+  const int b = item % p.num_seqs, tile = tiles - 1 - item / p.num_seqs;
   if (warp == kLoadWarp && lane == 0) {
     prefetch_tensormap(&q_map);
     prefetch_tensormap(&k_map);
     prefetch_tensormap(&v_map);
   }
 
-  // ---- (sequence, position tile) of this CTA: blockIdx.x = b * tiles + tile
-  // (the last position tile of a sequence, the one with the most keys, first)
-  const int b = (int)blockIdx.x / tiles, tile = tiles - 1 - (int)blockIdx.x % tiles;
   const int cols = p.max_num_blocks_per_seq;
   // The load warp fetches the sequence's first block ids (pages lane + 32 i)
   // together with its lengths, before it knows how many it needs.
@@ -683,8 +686,8 @@ int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, const CUtensorMap &k
   if (!ensure_smem_attr(prefill_umma_kernel<T, G>, kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
   constexpr int kPos = kM / G;
   const int64_t tiles = prefill_tiles_per_seq(a, kPos);
-  if (tiles <= 0 || tiles * a.num_seqs > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
-  dim3 grid((unsigned)(tiles * a.num_seqs), (unsigned)a.num_kv_heads);
+  if (tiles <= 0 || tiles * a.num_seqs * a.num_kv_heads > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+  dim3 grid((unsigned)(tiles * a.num_seqs * a.num_kv_heads));
   prefill_umma_kernel<T, G><<<grid, kThreads, kSmemBytes, s>>>(a, (int)tiles, qmap, kmap, map);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
@@ -694,7 +697,6 @@ int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, const CUtensorMap &k
 int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s) {
   if (a.head_dim != kD || a.block_size != kBS) return VASR_PA_ENOT_SUPPORTED;
   if (a.dtype != VASR_PA_BF16 && a.dtype != VASR_PA_F16) return VASR_PA_ENOT_SUPPORTED;
-  if (a.num_kv_heads > 65535) return VASR_PA_EINVAL_SHAPE;
   const int g = a.num_heads / a.num_kv_heads;
   if (g != 1 && g != 2 && g != 4) return VASR_PA_ENOT_SUPPORTED;
   if ((int64_t)a.num_blocks * a.num_kv_heads * kD >= (int64_t(1) << 31))
