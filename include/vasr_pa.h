@@ -295,6 +295,23 @@ int32_t vasr_pa_reshape_and_cache_fp8(
     const float *k_scale, const float *v_scale, vasr_pa_stream_t stream);
 
 /*
+ * gather_kv_cache_fp8: vasr_pa_gather_kv_cache over fp8 pages, the form the
+ * call site at thinker_text.rs:190-198 / :1344-1352 takes with k_scale /
+ * v_scale and the model dtype as out_dtype: packed rows of out_dtype (f32,
+ * bf16, f16) holding float(stored byte) * scale, rounded to nearest even.
+ */
+int32_t vasr_pa_gather_kv_cache_fp8(void *key_out, void *value_out,
+                                    const void *key_cache, const void *value_cache,
+                                    const uint32_t *block_tables,
+                                    const uint32_t *cu_seqlens_kv, int32_t num_seqs,
+                                    int32_t max_num_blocks_per_seq,
+                                    int64_t total_tokens, int32_t num_kv_heads,
+                                    int32_t head_dim, int32_t block_size,
+                                    int64_t num_blocks, int32_t out_dtype,
+                                    const float *k_scale, const float *v_scale,
+                                    vasr_pa_stream_t stream);
+
+/*
  * paged_attention_fp8: decode attention of bf16 / f16 queries (dtype) over
  * fp8 pages; scores use K = stored * k_scale and the output V = stored *
  * v_scale. GQA group 2, head_dim 128 (the Qwen3-ASR shape); other shapes

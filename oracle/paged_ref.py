@@ -550,6 +550,15 @@ def reshape_and_cache_fp8(key, value, key_cache, value_cache, slots, block_size,
         value_cache[blk, :, :, off] = vq[i]
 
 
+def gather_kv_cache_fp8(key_cache, value_cache, block_tables, cu, num_kv_heads, head_dim,
+                        block_size, k_scale, v_scale):
+    """gather_kv_cache over fp8 pages: the byte gather, then decode(byte) * scale in f32
+    (the caller rounds to its out dtype)."""
+    kb, vb = gather_kv_cache(key_cache, value_cache, block_tables, cu, num_kv_heads, head_dim,
+                             block_size)
+    return (fp8_e4m3_decode(kb) * np.float32(k_scale), fp8_e4m3_decode(vb) * np.float32(v_scale))
+
+
 # ============================================== device decode loop (host restatement)
 def decode_step_prepare(state, eos_ids, block_tables, block_table_lens, block_size, num_blocks):
     """One decode step's token feedback + metadata, as the reference host loop does it.

@@ -224,6 +224,34 @@ int32_t vasr_pa_gather_kv_cache(void *key_out, void *value_out, const void *key_
   return vasr::launch_gather(a, to_stream(stream));
 }
 
+int32_t vasr_pa_gather_kv_cache_fp8(void *key_out, void *value_out, const void *key_cache,
+                                    const void *value_cache, const uint32_t *block_tables,
+                                    const uint32_t *cu_seqlens_kv, int32_t num_seqs,
+                                    int32_t max_num_blocks_per_seq, int64_t total_tokens,
+                                    int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                    int64_t num_blocks, int32_t out_dtype, const float *k_scale,
+                                    const float *v_scale, vasr_pa_stream_t stream) {
+  const int g = check_geometry(out_dtype, num_kv_heads, head_dim, block_size, num_blocks);
+  if (g != VASR_PA_OK) return g;
+  if (num_seqs < 0 || max_num_blocks_per_seq <= 0 || total_tokens < 0) return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0 || total_tokens == 0) return VASR_PA_OK;
+  if (num_seqs > 65535) return VASR_PA_EINVAL_SHAPE;
+  if (!key_out || !value_out || !key_cache || !value_cache || !block_tables || !cu_seqlens_kv ||
+      !k_scale || !v_scale)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned16(key_out) || !aligned16(value_out) || !aligned16(key_cache) ||
+      !aligned16(value_cache) || !aligned(block_tables, 4) || !aligned(cu_seqlens_kv, 4) ||
+      !aligned(k_scale, 4) || !aligned(v_scale, 4))
+    return VASR_PA_EINVAL_ALIGN;
+  GatherArgs a{key_out, value_out, key_cache, value_cache, block_tables, cu_seqlens_kv, num_seqs,
+               max_num_blocks_per_seq, total_tokens, num_kv_heads, head_dim, block_size,
+               num_blocks, out_dtype};
+  a.cache_dtype = VASR_PA_FP8_E4M3;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  return vasr::launch_gather(a, to_stream(stream));
+}
+
 int32_t vasr_pa_paged_attention_varlen_prefill(
     void *out, const void *query, const void *key_cache, const void *value_cache,
     const uint32_t *block_tables, const uint32_t *context_lens, const uint32_t *cu_seqlens_q,

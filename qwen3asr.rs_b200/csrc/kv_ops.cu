@@ -4,6 +4,8 @@
 // None of these does arithmetic on the values: every kernel is a byte-exact
 // permutation of its input, moved in 16-byte vectors wherever the cache
 // layout allows it.
+#include <type_traits>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -264,6 +266,112 @@ int launch_gather_t(const GatherArgs &a, cudaStream_t stream) {
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
+// ================================================ gather_kv_cache, fp8 pages
+// The fp8 form of the same gather: the call site passes k_scale / v_scale
+// and the model dtype as out_dtype, and the packed rows hold
+// float(stored byte) * scale rounded to that dtype. One CTA per (page,
+// sequence); K chunks of 16 bytes become 16 outputs, V pages [D][BS] are
+// transposed through shared memory.
+struct GatherFp8Params {
+  GatherParams g;
+  const float *k_scale;
+  const float *v_scale;
+};
+
+template <typename TO>
+__device__ __forceinline__ void store16_scaled(TO *dst, const float (&f)[16], float scale) {
+  if constexpr (std::is_same<TO, float>::value) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      reinterpret_cast<float4 *>(dst)[i] =
+          make_float4(f[4 * i] * scale, f[4 * i + 1] * scale, f[4 * i + 2] * scale, f[4 * i + 3] * scale);
+  } else {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const TO lo = Elem<TO>::from_f32(f[2 * i] * scale), hi = Elem<TO>::from_f32(f[2 * i + 1] * scale);
+      w[i] = (uint32_t)(*reinterpret_cast<const uint16_t *>(&lo)) |
+             ((uint32_t)(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
+    }
+    reinterpret_cast<uint4 *>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4 *>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+template <typename TO, int BS, int D>
+__global__ void __launch_bounds__(256) gather_fp8_kernel(const GatherFp8Params q) {
+  const GatherParams &p = q.g;
+  constexpr int kCH = D / 16;            // 16-byte chunks of a K row
+  constexpr int kRowWords = BS / 4 + 1;  // padded V row (BS bytes), in 32-bit words
+  extern __shared__ __align__(16) uint32_t vsm[];
+  const int page = blockIdx.x;
+  const int b = blockIdx.y;
+  const int64_t start = p.cu[b];
+  const int64_t len = (int64_t)p.cu[b + 1] - start;
+  if ((int64_t)page * BS >= len) return;
+  const int n = (int)min((int64_t)BS, len - (int64_t)page * BS);
+  uint32_t blk = p.block_tables[(int64_t)b * p.cols + page];
+  if ((int64_t)blk >= p.num_blocks) {
+    if (threadIdx.x == 0) raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
+    blk = 0;
+  }
+  const float ks = __ldg(q.k_scale), vs = __ldg(q.v_scale);
+  const int H = p.num_kv_heads;
+  const int64_t tok0 = start + (int64_t)page * BS;
+  const int64_t page_bytes = (int64_t)D * BS;
+  TO *k_out = reinterpret_cast<TO *>(p.k_out);
+  TO *v_out = reinterpret_cast<TO *>(p.v_out);
+  // K
+  for (int i = threadIdx.x; i < n * H * kCH; i += blockDim.x) {
+    const int c = i % kCH;
+    const int h = (i / kCH) % H;
+    const int t = i / (kCH * H);
+    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(
+        p.k_cache + ((int64_t)blk * H + h) * page_bytes + ((int64_t)c * BS + t) * 16));
+    float f[16];
+    unpack16_fp8(raw, f);
+    store16_scaled<TO>(k_out + ((tok0 + t) * H + h) * (int64_t)D + c * 16, f, ks);
+  }
+  // V, one head at a time through shared memory
+  for (int h = 0; h < H; ++h) {
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(p.v_cache + ((int64_t)blk * H + h) * page_bytes);
+    for (int w = threadIdx.x; w < D * BS / 4; w += blockDim.x) {
+      const int d = w / (BS / 4);
+      vsm[d * kRowWords + (w - d * (BS / 4))] = __ldg(src + w);
+    }
+    __syncthreads();
+    const unsigned char *vb = reinterpret_cast<const unsigned char *>(vsm);
+    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
+      const int d = i % D;
+      const int t = i / D;
+      __nv_fp8_e4m3 e;
+      e.__x = vb[d * kRowWords * 4 + t];
+      v_out[((tok0 + t) * H + h) * (int64_t)D + d] = Elem<TO>::from_f32(static_cast<float>(e) * vs);
+    }
+    __syncthreads();
+  }
+}
+
+template <typename TO, int BS, int D>
+int launch_gather_fp8_t(const GatherArgs &a, cudaStream_t stream) {
+  GatherFp8Params q{};
+  q.g.k_out = static_cast<unsigned char *>(a.key_out);
+  q.g.v_out = static_cast<unsigned char *>(a.value_out);
+  q.g.k_cache = static_cast<const unsigned char *>(a.key_cache);
+  q.g.v_cache = static_cast<const unsigned char *>(a.value_cache);
+  q.g.block_tables = a.block_tables;
+  q.g.cu = a.cu_seqlens_kv;
+  q.g.num_blocks = a.num_blocks;
+  q.g.cols = a.max_num_blocks_per_seq;
+  q.g.num_kv_heads = a.num_kv_heads;
+  q.k_scale = a.k_scale;
+  q.v_scale = a.v_scale;
+  const int smem = D * (BS / 4 + 1) * 4;
+  dim3 grid((unsigned)a.max_num_blocks_per_seq, (unsigned)a.num_seqs);
+  gather_fp8_kernel<TO, BS, D><<<grid, 256, smem, stream>>>(q);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
 // ============================================================ block copies
 // copy_blocks: one CTA per (pair, layer, K|V) moves one block with 16-byte
 // loads; each thread keeps kCopyUnroll loads in flight.
@@ -447,6 +555,21 @@ int launch_append(const AppendArgs &a, cudaStream_t s) {
 }
 
 int launch_gather(const GatherArgs &a, cudaStream_t s) {
+  if (a.cache_dtype == VASR_PA_FP8_E4M3) {
+    if (a.k_scale == nullptr || a.v_scale == nullptr) return VASR_PA_EINVAL_POINTER;
+#define VASR_GATHER8_CASE(T, BS_, D_) \
+  if (a.block_size == BS_ && a.head_dim == D_) return launch_gather_fp8_t<T, BS_, D_>(a, s);
+#define VASR_GATHER8_T(T)                                                              \
+  VASR_GATHER8_CASE(T, 8, 64) VASR_GATHER8_CASE(T, 16, 64) VASR_GATHER8_CASE(T, 32, 64) \
+  VASR_GATHER8_CASE(T, 8, 128) VASR_GATHER8_CASE(T, 16, 128) VASR_GATHER8_CASE(T, 32, 128) \
+  VASR_GATHER8_CASE(T, 8, 256) VASR_GATHER8_CASE(T, 16, 256) VASR_GATHER8_CASE(T, 32, 256)
+    if (a.dtype == VASR_PA_F32) { VASR_GATHER8_T(float) }
+    if (a.dtype == VASR_PA_BF16) { VASR_GATHER8_T(__nv_bfloat16) }
+    if (a.dtype == VASR_PA_F16) { VASR_GATHER8_T(__half) }
+#undef VASR_GATHER8_T
+#undef VASR_GATHER8_CASE
+    return VASR_PA_ENOT_SUPPORTED;
+  }
 #define VASR_GATHER_CASE(T, BS_, D_) \
   if (a.block_size == BS_ && a.head_dim == D_) return launch_gather_t<T, BS_, D_>(a, s);
 #define VASR_GATHER_T(T)                                                             \

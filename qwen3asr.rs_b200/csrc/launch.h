@@ -70,7 +70,10 @@ struct GatherArgs {
   int head_dim;
   int block_size;
   int64_t num_blocks;
-  int dtype;
+  int dtype;  // element type of the outputs (and of the cache unless cache_dtype is set)
+  int cache_dtype = -1;  // VASR_PA_FP8_E4M3: one-byte pages, outputs = byte * scale
+  const float *k_scale = nullptr;
+  const float *v_scale = nullptr;
 };
 
 struct PrefillArgs {

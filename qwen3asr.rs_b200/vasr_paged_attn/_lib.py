@@ -92,6 +92,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _i64,
          _i64, _i64, _i32, _c_void_p, _c_void_p, _c_void_p],
     ),
+    "vasr_pa_gather_kv_cache_fp8": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i64, _i32,
+         _i32, _i32, _i64, _i32, _c_void_p, _c_void_p, _c_void_p],
+    ),
     "vasr_pa_paged_attention_fp8": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32, _i32,

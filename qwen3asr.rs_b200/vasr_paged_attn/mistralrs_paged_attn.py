@@ -194,12 +194,20 @@ def gather_kv_cache(key_cache: torch.Tensor, value_cache: torch.Tensor,
                     block_tables: torch.Tensor, cu_seqlens_kv: torch.Tensor,
                     out_dtype: Optional[torch.dtype] = None,
                     total_tokens: Optional[int] = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Packed ``[sum kv, Hkv, D]`` copies of each sequence's first kv_len tokens."""
-    del k_scale, v_scale
+    """Packed ``[sum kv, Hkv, D]`` copies of each sequence's first kv_len tokens.
+
+    fp8 (E4M3) pages need k_scale / v_scale and give ``byte * scale`` in
+    out_dtype (bf16 when None); other caches keep their dtype."""
     dev = _require_cuda(key_cache, value_cache, block_tables, cu_seqlens_kv)
     nb, hkv, d, bs = cache_geometry(key_cache, value_cache)
-    if out_dtype is not None and out_dtype != key_cache.dtype:
+    fp8 = key_cache.dtype == FP8_CACHE
+    if fp8:
+        _check_scales(k_scale, v_scale, dev)
+        out_dtype = torch.bfloat16 if out_dtype is None else out_dtype
+    elif out_dtype is not None and out_dtype != key_cache.dtype:
         raise _lib.VasrPaError(_lib.EINVAL_DTYPE, "gather_kv_cache keeps the cache dtype")
+    else:
+        out_dtype = key_cache.dtype
     if block_tables.dtype not in _INDEX32 or cu_seqlens_kv.dtype not in _INDEX32:
         raise _lib.VasrPaError(_lib.EINVAL_SHAPE, "block_tables / cu_seqlens_kv must be u32/i32")
     b = int(block_tables.shape[0])
@@ -207,14 +215,20 @@ def gather_kv_cache(key_cache: torch.Tensor, value_cache: torch.Tensor,
         raise _lib.VasrPaError(_lib.EINVAL_SHAPE, "cu_seqlens_kv must be [B + 1]")
     if total_tokens is None:
         total_tokens = int(cu_seqlens_kv[-1].item())  # host read, as the Rust wrapper sizes outputs
-    k_out = torch.empty((total_tokens, hkv, d), dtype=key_cache.dtype, device=dev)
+    k_out = torch.empty((total_tokens, hkv, d), dtype=out_dtype, device=dev)
     v_out = torch.empty_like(k_out)
     bt = block_tables.contiguous()
     cu = cu_seqlens_kv.contiguous()
-    st = _lib.lib().vasr_pa_gather_kv_cache(
-        k_out.data_ptr(), v_out.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
-        bt.data_ptr(), cu.data_ptr(), b, int(bt.shape[1]), total_tokens, hkv, d, bs, nb,
-        dtype_code(key_cache.dtype), _stream(dev))
+    if fp8:
+        st = _lib.lib().vasr_pa_gather_kv_cache_fp8(
+            k_out.data_ptr(), v_out.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            bt.data_ptr(), cu.data_ptr(), b, int(bt.shape[1]), total_tokens, hkv, d, bs, nb,
+            dtype_code(out_dtype), k_scale.data_ptr(), v_scale.data_ptr(), _stream(dev))
+    else:
+        st = _lib.lib().vasr_pa_gather_kv_cache(
+            k_out.data_ptr(), v_out.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            bt.data_ptr(), cu.data_ptr(), b, int(bt.shape[1]), total_tokens, hkv, d, bs, nb,
+            dtype_code(key_cache.dtype), _stream(dev))
     _lib.check(st, "gather_kv_cache")
     return k_out, v_out
 

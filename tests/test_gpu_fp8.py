@@ -142,3 +142,40 @@ def test_fp8_rejects_missing_scales_and_bs8_decode(cuda_device):
         pa.paged_attention(q, sk, sv, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), t, c,
                            None, 8, 0.1, 1.0, None)
     assert e.value.status == _lib.ENOT_SUPPORTED
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_fp8_gather_is_exact(cuda_device, out_dtype, bs):
+    """gather_kv_cache over fp8 pages: byte * scale rounded to out_dtype, bit for bit."""
+    rng = np.random.default_rng(300 + bs)
+    ctx = np.array([1, bs - 1, bs, bs + 1, 77, 300], np.int64)
+    blocks = [-(-int(c) // bs) for c in ctx]
+    nb = sum(blocks) + 3
+    tables = disjoint_block_tables(rng, blocks, nb)
+    kc = rng.integers(0, 256, size=(nb, HKV, D // 16, bs, 16), dtype=np.uint8)
+    vc = rng.integers(0, 256, size=(nb, HKV, D, bs), dtype=np.uint8)
+    for c in (kc, vc):  # no NaN bytes: NaN payloads need not match
+        c[(c & 0x7F) == 0x7F] = 0x11
+    ks, vs = 0.037, 1.5
+    cu = np.concatenate([[0], np.cumsum(ctx)]).astype(np.uint32)
+    sk, sv = _scales(cuda_device, ks, vs)
+    k, v = pa.gather_kv_cache(torch.from_numpy(kc).to(cuda_device).view(torch.float8_e4m3fn),
+                              torch.from_numpy(vc).to(cuda_device).view(torch.float8_e4m3fn), sk, sv,
+                              torch.from_numpy(tables.astype(np.int32)).to(cuda_device),
+                              torch.from_numpy(cu.astype(np.int32)).to(cuda_device), out_dtype)
+    assert k.dtype == out_dtype and k.shape == (int(cu[-1]), HKV, D)
+    kr, vr = ref.gather_kv_cache_fp8(kc, vc, np.ascontiguousarray(tables.astype(np.uint32)), cu, HKV, D,
+                                     bs, ks, vs)
+    for got, exp in ((k, kr), (v, vr)):
+        want = torch.from_numpy(exp).to(out_dtype)
+        assert torch.equal(got.cpu().view(torch.int16 if out_dtype != torch.float32 else torch.int32),
+                           want.view(torch.int16 if out_dtype != torch.float32 else torch.int32))
+
+
+def test_fp8_gather_requires_scales(cuda_device):
+    kc, vc = _u8_cache(4, 16, cuda_device)
+    t = torch.ones(1, 1, dtype=torch.int32, device=cuda_device)
+    cu = torch.tensor([0, 5], dtype=torch.int32, device=cuda_device)
+    with pytest.raises(_lib.VasrPaError):
+        pa.gather_kv_cache(kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), None, None, t, cu)
