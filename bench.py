@@ -61,7 +61,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kernel", default=None,
-                   choices=["decode", "decode_fp8", "append", "prefill", "copy", "swap", "config1"],
+                   choices=["decode", "decode_fp8", "append", "gather", "prefill", "copy", "swap", "config1"],
                    help="microbenchmark one kernel on its BASELINE config instead of the decode step")
     p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
     p.add_argument("--layers", type=int, default=28,
@@ -615,10 +615,41 @@ def run_kernel_bench(args):
             alg = ntok * hkv * d * 2 * 2 * 2
             lines.append({"kernel": "kv_append", "config": name, "tokens": ntok, "us": ms * 1e3,
                           "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
+            # the same tokens into fp8 (E4M3) pages: bf16 read, one byte per element written
+            kc8 = torch.zeros(nb, hkv, d // 16, bs, 16, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+            vc8 = torch.zeros(nb, hkv, d, bs, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+            sk = torch.tensor([0.05], device=dev)
+            ms = _events_time(lambda i: pa.reshape_and_cache(kv, kv, sk, sk, kc8, vc8, sl), args.iters)
+            alg = ntok * hkv * d * 2 * (2 + 1)
+            lines.append({"kernel": "kv_append_fp8", "config": name, "tokens": ntok, "us": ms * 1e3,
+                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
+    elif k == "gather":
+        # gather_kv_cache of config 3's full prompts (32 x U[100, 800] tokens) from bf16 and fp8 pages
+        from vasr_paged_attn.workloads import config3_rounds
+
+        lens, _ = config3_rounds(args.seed)
+        lens = np.asarray(lens, np.int64)
+        nb = sum(-(-int(n) // bs) for n in lens) + 1
+        t = torch.from_numpy(tables_for(lens, nb)).to(dev)
+        cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).to(dev)
+        total = int(lens.sum())
+        kc, vc = pool(nb, 1)[0]
+        ms = _events_time(lambda i: pa.gather_kv_cache(kc, vc, None, None, t, cu, None, total), args.iters)
+        alg = total * hkv * d * 2 * 2 * 2
+        lines.append({"kernel": "gather_kv_cache", "config": "config3 prompts, bf16 pages", "tokens": total,
+                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
+                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
+        kc8 = (torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn)
+        vc8 = (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)
+        sk = torch.tensor([0.125], device=dev)
+        ms = _events_time(lambda i: pa.gather_kv_cache(kc8, vc8, sk, sk, t, cu, torch.bfloat16, total),
+                          args.iters)
+        alg = total * hkv * d * 2 * (1 + 2)
+        lines.append({"kernel": "gather_kv_cache_fp8", "config": "config3 prompts, fp8 pages -> bf16",
+                      "tokens": total, "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
+                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
     elif k == "prefill":
-        sys.path.insert(0, str(REPO / "tests"))
-        sys.path.insert(0, str(REPO / "oracle"))
-        from cases import config3_rounds
+        from vasr_paged_attn.workloads import config3_rounds
 
         lens, rounds = config3_rounds(args.seed)
         nb = sum(-(-int(n) // bs) for n in lens) + 1

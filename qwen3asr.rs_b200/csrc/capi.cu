@@ -112,9 +112,9 @@ int32_t vasr_pa_reshape_and_cache_fp8(const void *key, const void *value, void *
     return VASR_PA_EINVAL_SHAPE;
   if (!key || !value || !key_cache || !value_cache || !slot_mapping || !k_scale || !v_scale)
     return VASR_PA_EINVAL_POINTER;
-  if (!aligned(key, es) || !aligned(value, es) || !aligned16(key_cache) ||
-      !aligned16(value_cache) || !aligned(slot_mapping, 8) || !aligned(k_scale, 4) ||
-      !aligned(v_scale, 4))
+  if (!aligned16(key) || !aligned16(value) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      (key_token_stride * es) % 16 != 0 || (value_token_stride * es) % 16 != 0 ||
+      !aligned(slot_mapping, 8) || !aligned(k_scale, 4) || !aligned(v_scale, 4))
     return VASR_PA_EINVAL_ALIGN;
   AppendArgs a{key, value, key_cache, value_cache, slot_mapping, num_tokens, num_kv_heads,
                head_dim, block_size, num_blocks, key_token_stride, value_token_stride, src_dtype,

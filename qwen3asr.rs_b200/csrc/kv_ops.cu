@@ -440,8 +440,12 @@ __global__ void __launch_bounds__(kCopyThreads) swap_blocks_kernel(const SwapPar
 // ====================================================== fp8 KV append
 // Pages of one-byte E4M3 values with per-tensor scales: cache = value / scale
 // (IEEE division), rounded to nearest even and saturated to +-448 by the
-// cuda_fp8.h conversion. One warp per (token, kv head): K as 16-byte chunks
-// of 16 dims (lane c < D / 16 writes chunk c), V one byte per dim.
+// cuda_fp8.h conversion. Calls of 128 tokens or more use the tiling of
+// kv_append_kernel: a tile of tokens (all kv heads) is quantised into shared
+// memory as bytes; K goes out as
+// 16-byte chunks (16 dims of one token), V by runs of consecutive slots of
+// one page row, as one vector store when a run fills an aligned group of
+// min(16, BS) tokens.
 struct AppendFp8Params {
   const unsigned char *key;
   const unsigned char *value;
@@ -455,10 +459,146 @@ struct AppendFp8Params {
   int64_t v_stride_bytes;
   int64_t num_blocks;
   int num_kv_heads;
+  int tile_tokens;
+  int heads_per_tile;
 };
 
+// 16 source elements at src (16-byte aligned) -> 16 E4M3 bytes of x / scale.
+template <typename T>
+__device__ __forceinline__ uint4 quantize16(const unsigned char *src, float scale) {
+  constexpr int kPer = Elem<T>::kX;  // elements per 16-byte load
+  float f[16];
+#pragma unroll
+  for (int q = 0; q < 16 / kPer; ++q) {
+    float g[kPer];
+    unpack_chunk<T>(__ldg(reinterpret_cast<const uint4 *>(src) + q), g);
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) f[q * kPer + e] = g[e];
+  }
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __nv_fp8x2_storage_t pr = __nv_cvt_float2_to_fp8x2(
+        make_float2(__fdiv_rn(f[2 * i], scale), __fdiv_rn(f[2 * i + 1], scale)), __NV_SATFINITE, __NV_E4M3);
+    w[i >> 1] |= (uint32_t)pr << (16 * (i & 1));
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <typename T, int BS, int D>
-__global__ void __launch_bounds__(128) kv_append_fp8_kernel(const AppendFp8Params p) {
+__global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const AppendFp8Params p) {
+  constexpr int kCH = D / 16;                 // 16-byte K chunks per (token, head)
+  constexpr int kTPS = BS < 16 ? BS : 16;     // tokens per vector V store
+  constexpr int kES = (int)sizeof(T);
+  extern __shared__ __align__(16) unsigned char sm[];
+  unsigned char *kt = sm;
+  unsigned char *vt = sm + kAppendMaxTokens * kAppendRowPitch;
+  int64_t *s_slot = reinterpret_cast<int64_t *>(vt + kAppendMaxTokens * kAppendRowPitch);
+  int *s_run_start = reinterpret_cast<int *>(s_slot + kAppendMaxTokens);
+  int *s_run_len = s_run_start + kAppendMaxTokens;
+  int *s_nruns = s_run_len + kAppendMaxTokens;
+
+  const int TT = p.tile_tokens;
+  const int64_t t0 = (int64_t)blockIdx.x * TT;
+  const int h0 = blockIdx.y * p.heads_per_tile;
+  const int HC = min(p.heads_per_tile, p.num_kv_heads - h0);
+  const int ntok = (int)min((int64_t)TT, p.num_tokens - t0);
+  const int64_t max_slot = p.num_blocks * BS;
+  const int tid = threadIdx.x;
+  const float ks = __ldg(p.k_scale), vs = __ldg(p.v_scale);
+
+  if (tid < ntok) {
+    int64_t s = p.slots[t0 + tid];
+    if (s >= max_slot) {
+      raise_device_error(VASR_PA_DERR_SLOT_RANGE);
+      s = -1;
+    }
+    s_slot[tid] = s;
+  }
+  // quantise the tile: (token, 16-element chunk) -> 16 bytes
+  const int row_chunks = HC * kCH;
+  for (int i = tid; i < ntok * row_chunks; i += kAppendThreads) {
+    const int tt = i / row_chunks;
+    const int r = i - tt * row_chunks;
+    const int64_t col = ((int64_t)h0 * D + (int64_t)r * 16) * kES;
+    *reinterpret_cast<uint4 *>(kt + tt * kAppendRowPitch + r * 16) =
+        quantize16<T>(p.key + (t0 + tt) * p.k_stride_bytes + col, ks);
+    *reinterpret_cast<uint4 *>(vt + tt * kAppendRowPitch + r * 16) =
+        quantize16<T>(p.value + (t0 + tt) * p.v_stride_bytes + col, vs);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // split the tile into V runs (consecutive slots, same aligned group)
+    int n = 0;
+    int tt = 0;
+    while (tt < ntok) {
+      const int64_t s = s_slot[tt];
+      if (s < 0) {
+        ++tt;
+        continue;
+      }
+      int len = 1;
+      while (tt + len < ntok && len < kTPS && s_slot[tt + len] == s + len && ((s + len) % kTPS) != 0)
+        ++len;
+      s_run_start[n] = tt;
+      s_run_len[n] = len;
+      ++n;
+      tt += len;
+    }
+    s_nruns[0] = n;
+  }
+  // K: (head, chunk, token) with token fastest
+  for (int i = tid; i < ntok * row_chunks; i += kAppendThreads) {
+    const int tt = i % ntok;
+    const int r = i / ntok;
+    const int64_t s = s_slot[tt];
+    if (s < 0) continue;
+    const int hc = r / kCH;
+    const int c = r - hc * kCH;
+    const int64_t blk = s / BS;
+    const int off = (int)(s - blk * BS);
+    const int64_t dst = ((((blk * p.num_kv_heads + h0 + hc) * kCH + c) * BS) + off) * 16;
+    *reinterpret_cast<uint4 *>(p.k_cache + dst) =
+        *reinterpret_cast<const uint4 *>(kt + tt * kAppendRowPitch + r * 16);
+  }
+  __syncthreads();
+  // V: (head, dim, run) with run fastest
+  const int nruns = s_nruns[0];
+  const int nitems = nruns * HC * D;
+  for (int i = tid; i < nitems; i += kAppendThreads) {
+    const int j = i % nruns;
+    const int hd = i / nruns;
+    const int hc = hd / D;
+    const int d = hd - hc * D;
+    const int tt0 = s_run_start[j];
+    const int len = s_run_len[j];
+    const int64_t s = s_slot[tt0];
+    const int64_t blk = s / BS;
+    const int off = (int)(s - blk * BS);
+    const unsigned char *src = vt + tt0 * kAppendRowPitch + hc * D + d;
+    unsigned char *dst = p.v_cache + ((blk * p.num_kv_heads + h0 + hc) * D + d) * BS + off;
+    if (len == kTPS && (off % kTPS) == 0) {
+      uint32_t w[kTPS / 4];
+#pragma unroll
+      for (int q = 0; q < kTPS / 4; ++q)
+        w[q] = (uint32_t)src[(4 * q) * kAppendRowPitch] | ((uint32_t)src[(4 * q + 1) * kAppendRowPitch] << 8) |
+               ((uint32_t)src[(4 * q + 2) * kAppendRowPitch] << 16) |
+               ((uint32_t)src[(4 * q + 3) * kAppendRowPitch] << 24);
+      if constexpr (kTPS == 16)
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      else
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+    } else {
+      for (int e = 0; e < len; ++e) dst[e] = src[e * kAppendRowPitch];
+    }
+  }
+}
+
+// Decode-sized fp8 appends (a few tokens, one per page row): one warp per
+// (token, kv head), K as 16-byte chunks (lane c < D / 16 writes chunk c), V
+// one byte per dim — the layout admits no wider V store for a lone token.
+template <typename T, int BS, int D>
+__global__ void __launch_bounds__(128) kv_append_fp8_token_kernel(const AppendFp8Params p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * 4 + warp;
   if (item >= p.num_tokens * p.num_kv_heads) return;
@@ -473,21 +613,12 @@ __global__ void __launch_bounds__(128) kv_append_fp8_kernel(const AppendFp8Param
     return;
   }
   const float ks = __ldg(p.k_scale), vs = __ldg(p.v_scale);
-  const T *k = reinterpret_cast<const T *>(p.key + t * p.k_stride_bytes) + (int64_t)h * D;
+  const unsigned char *k = p.key + t * p.k_stride_bytes + (int64_t)h * D * sizeof(T);
   const T *v = reinterpret_cast<const T *>(p.value + t * p.v_stride_bytes) + (int64_t)h * D;
   const int64_t page = (int64_t)blk * p.num_kv_heads + h;
-  if (lane < D / 16) {
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float a = __fdiv_rn(Elem<T>::to_f32(k[lane * 16 + 2 * i]), ks);
-      const float b = __fdiv_rn(Elem<T>::to_f32(k[lane * 16 + 2 * i + 1]), ks);
-      const __nv_fp8x2_storage_t pr = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
-      w[i >> 1] |= (uint32_t)pr << (16 * (i & 1));
-    }
+  if (lane < D / 16)
     *reinterpret_cast<uint4 *>(p.k_cache + ((page * (D / 16) + lane) * BS + off) * 16) =
-        make_uint4(w[0], w[1], w[2], w[3]);
-  }
+        quantize16<T>(k + lane * 16 * sizeof(T), ks);
 #pragma unroll
   for (int d = lane; d < D; d += 32) {
     const float x = __fdiv_rn(Elem<T>::to_f32(v[d]), vs);
@@ -510,10 +641,23 @@ int launch_append_fp8_t(const AppendArgs &a, cudaStream_t stream) {
   p.v_stride_bytes = a.value_token_stride * (int64_t)sizeof(T);
   p.num_blocks = a.num_blocks;
   p.num_kv_heads = a.num_kv_heads;
-  const int64_t items = a.num_tokens * a.num_kv_heads;
-  const int64_t ctas = (items + 3) / 4;
-  if (ctas > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
-  kv_append_fp8_kernel<T, BS, D><<<(unsigned)ctas, 128, 0, stream>>>(p);
+  if (a.num_tokens < 128) {  // decode-sized: a warp per (token, kv head)
+    const int64_t ctas = (a.num_tokens * a.num_kv_heads + 3) / 4;
+    if (ctas > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+    kv_append_fp8_token_kernel<T, BS, D><<<(unsigned)ctas, 128, 0, stream>>>(p);
+    return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+  }
+  const int tt = a.num_tokens >= 4096 ? 16 : 8;  // prefill-sized: 8 / 16-token tiles
+  p.tile_tokens = tt;
+  p.heads_per_tile = kAppendRowBytes / D;  // one byte per staged element
+  const int smem = 2 * kAppendMaxTokens * kAppendRowPitch + kAppendMaxTokens * 8 +
+                   (2 * kAppendMaxTokens + 1) * 4;
+  static std::atomic<uint64_t> attr_done{0};
+  if (!ensure_smem_attr(kv_append_fp8_kernel<T, BS, D>, smem, attr_done)) return VASR_PA_ELAUNCH;
+  const int64_t tiles = (a.num_tokens + tt - 1) / tt;
+  if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+  dim3 grid((unsigned)tiles, (unsigned)((a.num_kv_heads + p.heads_per_tile - 1) / p.heads_per_tile));
+  kv_append_fp8_kernel<T, BS, D><<<grid, kAppendThreads, smem, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 

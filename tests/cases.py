@@ -12,6 +12,7 @@ from dataclasses import dataclass
 import numpy as np
 
 import paged_ref as ref
+from vasr_paged_attn.workloads import config3_rounds, uniform_lens  # noqa: F401
 
 F32_SENTINEL = np.uint32(0x7FC0DEAD)  # a quiet NaN
 BF16_SENTINEL = np.uint16(0x7FC1)     # a quiet NaN
@@ -128,8 +129,6 @@ def config1_case() -> PagedCase:
     return make_decode_case(0, CONFIG1_CACHED, dtype="f32", num_blocks=512)
 
 
-def uniform_lens(seed, n, lo, hi):
-    return np.random.default_rng(seed).integers(lo, hi + 1, size=n)
 
 
 def loguniform_lens(seed, n, lo, hi):
@@ -195,16 +194,3 @@ def oracle_prefill(case: PrefillCase, scale=None, softcap=1.0, use_double=True):
                               use_double=use_double)
 
 
-def config3_rounds(seed=0, n=32, lo=100, hi=800, chunk=256):
-    """Config 3: prompt lengths ~U[lo, hi]; round r prefills tokens [256 r, 256 r + 256) of each."""
-    lens = uniform_lens(seed, n, lo, hi)
-    rounds = []
-    r = 0
-    while True:
-        start = r * chunk
-        active = [i for i in range(n) if lens[i] > start]
-        if not active:
-            break
-        rounds.append([(i, start, int(min(chunk, lens[i] - start))) for i in active])
-        r += 1
-    return lens, rounds

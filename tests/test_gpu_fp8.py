@@ -34,15 +34,19 @@ def _scales(dev, ks, vs):
             torch.tensor([vs], dtype=torch.float32, device=dev))
 
 
+@pytest.mark.parametrize("t", [77, 600])  # a warp per (token, head) / 8-token tiles with V runs
 @pytest.mark.parametrize("src", [torch.bfloat16, torch.float32, torch.float16])
 @pytest.mark.parametrize("bs", [8, 16, 32])
-def test_fp8_append_is_byte_exact(cuda_device, src, bs):
-    rng = np.random.default_rng(bs)
-    t, nb = 77, 40
+def test_fp8_append_is_byte_exact(cuda_device, src, bs, t):
+    rng = np.random.default_rng(bs + t)
+    nb = 40 if t < 128 else t // bs + 8
     k = (rng.standard_normal((t, HKV, D)) * 3).astype(np.float32)
     v = (rng.standard_normal((t, HKV, D)) * 3).astype(np.float32)
     k[0, 0, :7] = [1e4, -1e4, 0.0, -0.0, 1e-12, 449 * 0.05, 448 * 0.05]  # saturation, signed zeros
     slots = rng.permutation(nb * bs)[:t].astype(np.int64)
+    if t >= 128:  # runs of consecutive slots, some page-aligned, some not
+        slots[: t // 2] = np.arange(bs * 3 + 5, bs * 3 + 5 + t // 2)
+        slots[t // 2:] = rng.permutation(np.arange(bs * 3 + 5 + t // 2, nb * bs))[: t - t // 2]
     slots[::9] = -1
     kt, vt = torch.from_numpy(k).to(src), torch.from_numpy(v).to(src)
     ks, vs = 0.05, 0.02
