@@ -348,10 +348,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ loads
-    // K tile j -> K stage j & 1 as 64 bulk copies (one 256-byte dim chunk of
-    // one page each); V tile j -> V stage j & 1 as one swizzled 2-D TMA load
-    // per page. K j + 2 waits for Q K^T j, V j + 2 for P V j. Lane l keeps
-    // the block ids of pages l, l + 32, l + 64, l + 96 in registers.
+    // K tile j -> K stage j & 1 as 16 TMA gathers (one 16-byte dim chunk of
+    // four pages each); V tile j -> V stage j & 1 as one swizzled 2-D TMA
+    // load per page. K j + 2 waits for Q K^T j, V j + 2 for P V j. Lane l
+    // keeps the block ids of pages l, l + 32, l + 64, l + 96 in registers.
     if (lane == 0) {
       for (int i = 0; i < kNumBars; ++i) mbar_init(B(i), (i == kBarPFull || i == kBarPFull + 1) ? 4 * 32 : 1);
       mbar_fence_init();
