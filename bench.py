@@ -13,7 +13,9 @@ the reference (vasr-paged-attn/src/cuda_graph.rs).
              graph buffers + replay).
   e2e        tokens/s through the engine's host-facing call: per step the
              host builds the step metadata, copies it from pinned memory,
-             replays, and reads the next token ids back (synchronising).
+             replays, and reads the next token ids back (synchronising);
+             the host builds step s + 1's metadata (double-buffered pinned
+             memory) while the GPU runs step s.
   roofline   the paged decode kernel alone: algorithmic KV bytes per launch
              / CUDA-event launch time vs the measured HBM copy bandwidth.
   device_loop  tokens/s of the device-side decode loop: step prepare (token
@@ -338,35 +340,47 @@ def run_ours(args):
     clk = clocks.stop()
     value = world * BATCH * k_steps / (dev_ms / 1e3)
 
-    # ---- e2e: host-built metadata, pinned H2D, replay, D2H of next ids
+    # ---- e2e: host-built metadata, pinned H2D, replay, D2H of next ids. The
+    # pinned metadata is double-buffered so that the host builds step s + 1
+    # while the GPU runs step s; every step still copies its inputs H2D, reads
+    # its next ids D2H and synchronises before the next step starts.
     meta_cache = host.metadata_cache(nb, cfg.num_kv_heads, cfg.head_dim, BLOCK_SIZE, "bf16")
-    h_ids = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
-    h_pos = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
-    h_slots = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
-    h_ctx = torch.zeros(BATCH, dtype=torch.int32).pin_memory()
-    h_tables = torch.zeros(BATCH, cols, dtype=torch.int32).pin_memory()
+
+    def pinned_set():
+        return {"ids": torch.zeros(BATCH, dtype=torch.int64).pin_memory(),
+                "pos": torch.zeros(BATCH, dtype=torch.int64).pin_memory(),
+                "slots": torch.zeros(BATCH, dtype=torch.int64).pin_memory(),
+                "ctx": torch.zeros(BATCH, dtype=torch.int32).pin_memory(),
+                "tables": torch.zeros(BATCH, cols, dtype=torch.int32).pin_memory()}
+
+    sets = [pinned_set(), pinned_set()]
     h_next = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
     prompt_lens = [int(x) for x in lens0]
     table_rows = [list(map(int, r[:n])) for r, n in zip(tables, blocks)]
     stream = torch.cuda.current_stream()
 
-    def e2e_step(s):
+    def build(s, st):
         # host metadata through the C++ mirror of decode_metadata_for_batch_step
         meta = meta_cache.decode_metadata_for_batch_step(table_rows, prompt_lens, s, True)
-        h_slots.numpy()[:] = meta.slot_mapping
-        h_ctx.numpy()[:] = meta.context_lens
-        h_pos.numpy()[:] = np.asarray(meta.context_lens, dtype=np.int64) - 1
-        h_tables.numpy().reshape(-1)[:] = meta.block_tables_flat
-        graph.input_ids.copy_(h_ids, non_blocking=True)
-        graph.positions.copy_(h_pos, non_blocking=True)
-        graph.slot_mapping.copy_(h_slots, non_blocking=True)
-        graph.context_lens.copy_(h_ctx, non_blocking=True)
-        graph.block_tables.copy_(h_tables, non_blocking=True)
+        st["slots"].numpy()[:] = meta.slot_mapping
+        st["ctx"].numpy()[:] = meta.context_lens
+        st["pos"].numpy()[:] = np.asarray(meta.context_lens, dtype=np.int64) - 1
+        st["tables"].numpy().reshape(-1)[:] = meta.block_tables_flat
+
+    def e2e_step(s):
+        st = sets[s % 2]
+        st["ids"].copy_(h_next)  # the previous step's tokens, read back by the host
+        graph.input_ids.copy_(st["ids"], non_blocking=True)
+        graph.positions.copy_(st["pos"], non_blocking=True)
+        graph.slot_mapping.copy_(st["slots"], non_blocking=True)
+        graph.context_lens.copy_(st["ctx"], non_blocking=True)
+        graph.block_tables.copy_(st["tables"], non_blocking=True)
         graph.replay()
         h_next.copy_(graph.next_ids, non_blocking=True)
+        build(s + 1, sets[(s + 1) % 2])  # overlaps the GPU step
         stream.synchronize()
-        h_ids.copy_(h_next)
 
+    build(s_idx, sets[s_idx % 2])
     for _ in range(w_steps):
         e2e_step(s_idx)
         s_idx += 1
@@ -380,8 +394,7 @@ def run_ours(args):
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
     e2e_value = world * BATCH * k_steps / e2e_s
-    h2d = (h_ids.numel() * 8 + h_pos.numel() * 8 + h_slots.numel() * 8 + h_ctx.numel() * 4 +
-           h_tables.numel() * 4)
+    h2d = sum(t.numel() * t.element_size() for t in sets[0].values())
     d2h = h_next.numel() * 8
 
     # ---- device decode loop: prepare -> forward -> argmax replayed with no host round trip
