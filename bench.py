@@ -33,6 +33,7 @@ restatement in oracle/, all host threads) on the same contexts.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -55,7 +56,7 @@ BLOCK_SIZE = 16
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
@@ -95,9 +96,11 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples (every 100 ms) kept for the
+    timed regions: each sample carries nvidia-smi's timestamp and only those
+    inside a region passed to stop() count (all samples if none falls inside)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -107,11 +110,17 @@ class ClockSampler:
         self.lines: list[str] = []
         self.thread = None
 
+    def wait_first(self, timeout: float = 5.0):
+        """Block until the sampler delivered its first sample (it starts slowly)."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.02)
+
     def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -123,7 +132,7 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def stop(self):
+    def stop(self, windows=()):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -133,23 +142,26 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for ln in self.lines:
             parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]),
+                             {n for n, v in zip(names, parts[6:10]) if v.lower().startswith("active")}))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
+        inside = [r for r in rows if any(a - 0.05 <= r[0] <= b + 0.05 for a, b in windows)]
+        use = inside or rows
+        sm = [r[1] for r in use]
+        reasons = set().union(*[r[3] for r in use]) if use else set()
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "sm_max_mhz": max(r[2] for r in use) if use else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "samples_in_timed_regions": len(inside)}
 
 
 # ------------------------------------------------------------ CPU baseline
@@ -324,8 +336,11 @@ def run_ours(args):
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
+    clocks.wait_first()
+    windows = []  # host wall-clock spans of the timed regions, for the clock samples
     torch.cuda.synchronize()
+    barrier()
+    w0 = time.time()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed_steps")  # lets ncu --nvtx-include select the timed launches
     e0.record()
@@ -337,7 +352,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     dev_ms = max_over_ranks(e0.elapsed_time(e1))
-    clk = clocks.stop()
+    windows.append((w0, time.time()))
     value = world * BATCH * k_steps / (dev_ms / 1e3)
 
     # ---- e2e: host-built metadata, pinned H2D, replay, D2H of next ids. The
@@ -387,10 +402,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
+    w0 = time.time()
     for _ in range(k_steps):
         e2e_step(s_idx)
         s_idx += 1
     torch.cuda.synchronize()
+    windows.append((w0, time.time()))
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
     e2e_value = world * BATCH * k_steps / e2e_s
@@ -410,11 +427,14 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
     l0.record()
     for _ in range(k_steps):
         loop.replay()
     l1.record()
     torch.cuda.synchronize()
+    windows.append((w0, time.time()))
+    clk = clocks.stop(windows)
     loop_ms = max_over_ranks(l0.elapsed_time(l1))
     barrier()
     fin, gen_counts, _ = loop_state.read_back()
