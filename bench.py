@@ -64,7 +64,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kernel", default=None,
-                   choices=["decode", "decode_fp8", "append", "gather", "prefill", "copy", "swap", "config1"],
+                   choices=["decode", "decode5", "decode_fp8", "append", "gather", "prefill", "copy", "swap",
+                            "config1"],
                    help="microbenchmark one kernel on its BASELINE config instead of the decode step")
     p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
     p.add_argument("--layers", type=int, default=28,
@@ -573,11 +574,17 @@ def run_kernel_bench(args):
         return t
 
     k = args.kernel
-    if k in ("decode", "config1"):
+    if k in ("decode", "config1", "decode5"):
         dtype = torch.float32 if k == "config1" else torch.bfloat16
         if k == "config1":
             lens = np.array([138, 513, 1024, 2049])
             nb, layers = 512, 1
+        elif k == "decode5":  # config 5 attention shapes: 512 sequences, ctx ~log-U[64, 4096]
+            from vasr_paged_attn.workloads import config5_context_lens
+
+            lens = config5_context_lens(args.seed)
+            nb = sum(-(-int(n) // bs) for n in lens) + 1
+            layers = min(args.layers, 4)  # 4 x 2 GB pools: well above L2
         else:
             lens = context_lens(args.seed, 0)
             nb = sum(-(-int(n) // bs) for n in lens) + 1
@@ -596,7 +603,7 @@ def run_kernel_bench(args):
 
         ms = _events_time(launch, args.iters)
         alg = int(lens.sum()) * hkv * d * 2 * es + q.numel() * es * 2
-        lines.append({"kernel": "paged_decode", "config": "config1" if k == "config1" else "config2",
+        lines.append({"kernel": "paged_decode", "config": {"config1": "config1", "decode5": "config5"}.get(k, "config2"),
                       "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
                       "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "layers_cycled": layers})
         if k == "config1":

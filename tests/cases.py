@@ -12,7 +12,7 @@ from dataclasses import dataclass
 import numpy as np
 
 import paged_ref as ref
-from vasr_paged_attn.workloads import config3_rounds, uniform_lens  # noqa: F401
+from vasr_paged_attn.workloads import config3_rounds, loguniform_lens, uniform_lens  # noqa: F401
 
 F32_SENTINEL = np.uint32(0x7FC0DEAD)  # a quiet NaN
 BF16_SENTINEL = np.uint16(0x7FC1)     # a quiet NaN
@@ -131,9 +131,6 @@ def config1_case() -> PagedCase:
 
 
 
-def loguniform_lens(seed, n, lo, hi):
-    r = np.random.default_rng(seed)
-    return np.exp(r.uniform(np.log(lo), np.log(hi), size=n)).astype(np.int64)
 
 
 @dataclass
