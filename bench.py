@@ -64,8 +64,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kernel", default=None,
-                   choices=["decode", "decode5", "decode_fp8", "append", "gather", "prefill", "copy", "swap",
-                            "config1"],
+                   choices=["decode", "decode5", "decode_fp8", "append", "gather", "prefill", "prefill_fp8",
+                            "copy", "swap", "config1"],
                    help="microbenchmark one kernel on its BASELINE config instead of the decode step")
     p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
     p.add_argument("--layers", type=int, default=28,
@@ -688,12 +688,17 @@ def run_kernel_bench(args):
         lines.append({"kernel": "gather_kv_cache_fp8", "config": "config3 prompts, fp8 pages -> bf16",
                       "tokens": total, "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
                       "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
-    elif k == "prefill":
+    elif k in ("prefill", "prefill_fp8"):
         from vasr_paged_attn.workloads import config3_rounds
 
         lens, rounds = config3_rounds(args.seed)
         nb = sum(-(-int(n) // bs) for n in lens) + 1
         kc, vc = pool(nb, 1)[0]
+        sk = sv = None
+        if k == "prefill_fp8":  # the same pages in E4M3 with per-tensor scales
+            kc = (torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn)
+            vc = (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)
+            sk = sv = torch.tensor([0.125], device=dev)
         t_all = tables_for(lens, nb)
         total_flops, total_ms = 0.0, 0.0
         for r in rounds:
@@ -706,7 +711,7 @@ def run_kernel_bench(args):
             dctx = torch.from_numpy(ctx.astype(np.int32)).to(dev)
             dcu = torch.from_numpy(cu).to(dev)
             mq = int(chunk.max())
-            ms = _events_time(lambda i: pa.paged_attention_varlen_prefill(q, kc, vc, bt, dctx, dcu, None, None,
+            ms = _events_time(lambda i: pa.paged_attention_varlen_prefill(q, kc, vc, bt, dctx, dcu, sk, sv,
                                                                           d ** -0.5, 1.0, mq), args.iters)
             vis = sum(sum(int(s) + j + 1 for j in range(int(n))) for (_, s, n) in r)
             total_flops += 4.0 * d * hq * vis
@@ -714,7 +719,8 @@ def run_kernel_bench(args):
         tflops = total_flops / (total_ms / 1e3) / 1e12
         mp = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
         tpeak = float(mp.get("bf16_tflops", 1590.0))
-        lines.append({"kernel": "paged_prefill_varlen", "config": "config3 (one layer, all chunk rounds)",
+        lines.append({"kernel": "paged_prefill_varlen" + ("_fp8" if k == "prefill_fp8" else ""),
+                      "config": "config3 (one layer, all chunk rounds)",
                       "rounds": len(rounds), "us_per_layer": total_ms * 1e3, "flops_per_layer": total_flops,
                       "TFLOP/s": tflops, "frac_of_bf16_peak": tflops / tpeak,
                       "tflops_28_layers": total_flops * 28 / 1e12})

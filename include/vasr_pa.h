@@ -312,6 +312,31 @@ int32_t vasr_pa_gather_kv_cache_fp8(void *key_out, void *value_out,
                                     vasr_pa_stream_t stream);
 
 /*
+ * paged_attention_varlen_prefill_fp8: the varlen prefill over fp8 pages for
+ * bf16 / f16 queries (dtype). The pages of each sequence's context are first
+ * written to a 16-bit scratch pool in the workspace (byte * scale in dtype,
+ * the 16-bit page layouts), then the prefill runs on that pool — the same
+ * numbers as gather_kv_cache_fp8 followed by attention, without the packed
+ * copy. workspace_size: bytes for num_seqs x max_num_blocks_per_seq pages of
+ * every kv head (K and V) plus a block table. The workspace is scratch (its
+ * contents are overwritten): not the paged_attention workspace, whose
+ * counters must stay zero. head_dim 128.
+ */
+int32_t vasr_pa_paged_attention_varlen_prefill_fp8(
+    void *out, const void *query, const void *key_cache,
+    const void *value_cache, const uint32_t *block_tables,
+    const uint32_t *context_lens, const uint32_t *cu_seqlens_q,
+    int32_t num_seqs, int64_t total_q_tokens, int32_t max_query_len,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+    int32_t block_size, int64_t num_blocks, int32_t max_num_blocks_per_seq,
+    float scale, float softcapping, int64_t q_token_stride, int32_t dtype,
+    const float *k_scale, const float *v_scale, void *workspace,
+    size_t workspace_bytes, vasr_pa_stream_t stream);
+size_t vasr_pa_paged_attention_varlen_prefill_fp8_workspace_size(
+    int32_t num_seqs, int32_t num_kv_heads, int32_t head_dim,
+    int32_t block_size, int32_t max_num_blocks_per_seq);
+
+/*
  * paged_attention_fp8: decode attention of bf16 / f16 queries (dtype) over
  * fp8 pages; scores use K = stored * k_scale and the output V = stored *
  * v_scale. GQA group 2, head_dim 128 (the Qwen3-ASR shape); other shapes

@@ -282,6 +282,80 @@ int32_t vasr_pa_paged_attention_varlen_prefill(
   return vasr::launch_prefill(a, to_stream(stream));
 }
 
+namespace {
+struct PrefillFp8Layout {
+  size_t off_k, off_v, off_table, total;
+};
+PrefillFp8Layout prefill_fp8_layout(int32_t num_seqs, int32_t num_kv_heads, int32_t head_dim,
+                                    int32_t block_size, int32_t cols) {
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t blocks = (size_t)num_seqs * (size_t)cols;
+  const size_t pool = blocks * (size_t)num_kv_heads * head_dim * block_size * 2;
+  PrefillFp8Layout l;
+  l.off_k = 0;
+  l.off_v = al(pool);
+  l.off_table = al(l.off_v + pool);
+  l.total = al(l.off_table + blocks * 4);
+  return l;
+}
+}  // namespace
+
+size_t vasr_pa_paged_attention_varlen_prefill_fp8_workspace_size(int32_t num_seqs,
+                                                                 int32_t num_kv_heads,
+                                                                 int32_t head_dim,
+                                                                 int32_t block_size,
+                                                                 int32_t max_num_blocks_per_seq) {
+  if (num_seqs <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      max_num_blocks_per_seq <= 0)
+    return 0;
+  return prefill_fp8_layout(num_seqs, num_kv_heads, head_dim, block_size, max_num_blocks_per_seq).total;
+}
+
+int32_t vasr_pa_paged_attention_varlen_prefill_fp8(
+    void *out, const void *query, const void *key_cache, const void *value_cache,
+    const uint32_t *block_tables, const uint32_t *context_lens, const uint32_t *cu_seqlens_q,
+    int32_t num_seqs, int64_t total_q_tokens, int32_t max_query_len, int32_t num_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int64_t num_blocks,
+    int32_t max_num_blocks_per_seq, float scale, float softcapping, int64_t q_token_stride,
+    int32_t dtype, const float *k_scale, const float *v_scale, void *workspace,
+    size_t workspace_bytes, vasr_pa_stream_t stream) {
+  if (dtype != VASR_PA_BF16 && dtype != VASR_PA_F16) return VASR_PA_EINVAL_DTYPE;
+  const int g = check_geometry(dtype, num_kv_heads, head_dim, block_size, num_blocks);
+  if (g != VASR_PA_OK) return g;
+  if (num_seqs < 0 || total_q_tokens < 0 || max_query_len < 0 || num_heads <= 0 ||
+      num_heads % num_kv_heads != 0 || max_num_blocks_per_seq <= 0)
+    return VASR_PA_EINVAL_SHAPE;
+  if (num_seqs == 0 || total_q_tokens == 0) return VASR_PA_OK;
+  if (q_token_stride < (int64_t)num_heads * head_dim) return VASR_PA_EINVAL_SHAPE;
+  if (!(softcapping > 0.f)) return VASR_PA_EINVAL_SHAPE;
+  if (head_dim != 128 || num_seqs > 65535) return VASR_PA_ENOT_SUPPORTED;
+  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens ||
+      !cu_seqlens_q || !k_scale || !v_scale)
+    return VASR_PA_EINVAL_POINTER;
+  if (!aligned16(query) || !aligned16(out) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      (q_token_stride * 2) % 16 != 0 || !aligned(block_tables, 4) || !aligned(context_lens, 4) ||
+      !aligned(cu_seqlens_q, 4) || !aligned(k_scale, 4) || !aligned(v_scale, 4))
+    return VASR_PA_EINVAL_ALIGN;
+  const PrefillFp8Layout l =
+      prefill_fp8_layout(num_seqs, num_kv_heads, head_dim, block_size, max_num_blocks_per_seq);
+  if (workspace == nullptr || workspace_bytes < l.total || !aligned16(workspace))
+    return VASR_PA_EINVAL_WORKSPACE;
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
+  vasr::DequantArgs d{key_cache, value_cache, block_tables, context_lens, num_seqs,
+                      max_num_blocks_per_seq, num_kv_heads, head_dim, block_size, num_blocks,
+                      dtype, k_scale, v_scale, ws + l.off_k, ws + l.off_v,
+                      reinterpret_cast<uint32_t *>(ws + l.off_table)};
+  const cudaStream_t st = to_stream(stream);
+  const int32_t r = vasr::launch_dequant_pages(d, st);
+  if (r != VASR_PA_OK) return r;
+  vasr::PrefillArgs a{out, query, ws + l.off_k, ws + l.off_v,
+                      reinterpret_cast<const uint32_t *>(ws + l.off_table), context_lens,
+                      cu_seqlens_q, num_seqs, total_q_tokens, max_query_len, num_heads, num_kv_heads,
+                      head_dim, block_size, (int64_t)num_seqs * max_num_blocks_per_seq,
+                      max_num_blocks_per_seq, scale, softcapping, q_token_stride, dtype};
+  return vasr::launch_prefill(a, st);
+}
+
 int32_t vasr_pa_copy_blocks(void *const *key_caches, void *const *value_caches,
                             int32_t num_layers, const int64_t *block_mapping, int64_t num_pairs,
                             int64_t num_blocks, int64_t block_bytes, vasr_pa_stream_t stream) {

@@ -372,6 +372,76 @@ int launch_gather_fp8_t(const GatherArgs &a, cudaStream_t stream) {
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
+// ============================================ fp8 pages -> 16-bit scratch pool
+// Prefill over fp8 pages runs the 16-bit kernels on a scratch pool: entry
+// (b, i) of the block table (i < pages of sequence b) becomes block
+// b * cols + i of the pool, holding the page's K and V as T(byte * scale) in
+// the 16-bit page layouts (K [D/8][BS][8], V [D][BS]); the remapped table is
+// written too. One CTA per (table entry, kv head).
+template <typename TO, int BS, int D>
+__global__ void __launch_bounds__(128) dequant_pages_kernel(
+    const unsigned char *k_cache, const unsigned char *v_cache, const uint32_t *block_tables,
+    const uint32_t *context_lens, int cols, int num_kv_heads, int64_t num_blocks,
+    const float *k_scale, const float *v_scale, TO *k_out, TO *v_out, uint32_t *table_out) {
+  const int i = blockIdx.x, b = blockIdx.y, h = blockIdx.z;
+  const int64_t dst = (int64_t)b * cols + i;
+  if (h == 0 && threadIdx.x == 0) table_out[dst] = (uint32_t)dst;
+  const int64_t ctx = min((int64_t)context_lens[b], (int64_t)cols * BS);
+  if ((int64_t)i * BS >= ctx) return;
+  uint32_t blk = block_tables[(int64_t)b * cols + i];
+  if ((int64_t)blk >= num_blocks) {
+    if (threadIdx.x == 0) raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
+    blk = 0;
+  }
+  const float ks = __ldg(k_scale), vs = __ldg(v_scale);
+  const int64_t src_page = ((int64_t)blk * num_kv_heads + h) * D * BS;  // bytes
+  const int64_t dst_page = (dst * num_kv_heads + h) * D * BS;           // elements
+  // K: fp8 chunk c (16 dims) of token t -> 16-bit chunks 2c, 2c + 1 of token t
+  for (int e = threadIdx.x; e < (D / 16) * BS; e += blockDim.x) {
+    const int c = e / BS, t = e % BS;
+    float f[16];
+    unpack16_fp8(__ldg(reinterpret_cast<const uint4 *>(k_cache + src_page + (int64_t)e * 16)), f);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const TO lo = Elem<TO>::from_f32(f[8 * half + 2 * j] * ks);
+        const TO hi = Elem<TO>::from_f32(f[8 * half + 2 * j + 1] * ks);
+        w[j] = (uint32_t)(*reinterpret_cast<const uint16_t *>(&lo)) |
+               ((uint32_t)(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
+      }
+      *reinterpret_cast<uint4 *>(k_out + dst_page + ((int64_t)(2 * c + half) * BS + t) * 8) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  // V: same [D][BS] order, 16 bytes -> 16 elements
+  for (int e = threadIdx.x; e < D * BS / 16; e += blockDim.x) {
+    float f[16];
+    unpack16_fp8(__ldg(reinterpret_cast<const uint4 *>(v_cache + src_page + (int64_t)e * 16)), f);
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const TO lo = Elem<TO>::from_f32(f[2 * j] * vs), hi = Elem<TO>::from_f32(f[2 * j + 1] * vs);
+      w[j] = (uint32_t)(*reinterpret_cast<const uint16_t *>(&lo)) |
+             ((uint32_t)(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
+    }
+    uint4 *d4 = reinterpret_cast<uint4 *>(v_out + dst_page + (int64_t)e * 16);
+    d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+template <typename TO, int BS>
+int launch_dequant_t(const DequantArgs &a, cudaStream_t s) {
+  dim3 grid((unsigned)a.cols, (unsigned)a.num_seqs, (unsigned)a.num_kv_heads);
+  dequant_pages_kernel<TO, BS, 128><<<grid, 128, 0, s>>>(
+      static_cast<const unsigned char *>(a.key_cache), static_cast<const unsigned char *>(a.value_cache),
+      a.block_tables, a.context_lens, a.cols, a.num_kv_heads, a.num_blocks, a.k_scale, a.v_scale,
+      static_cast<TO *>(a.key_out), static_cast<TO *>(a.value_out), a.table_out);
+  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+}
+
 // ============================================================ block copies
 // copy_blocks: one CTA per (pair, layer, K|V) moves one block with 16-byte
 // loads; each thread keeps kCopyUnroll loads in flight.
@@ -696,6 +766,18 @@ int launch_append(const AppendArgs &a, cudaStream_t s) {
 #undef VASR_APPEND_T
 #undef VASR_APPEND_CASE
   return VASR_PA_ENOT_SUPPORTED;
+}
+
+int launch_dequant_pages(const DequantArgs &a, cudaStream_t s) {
+  if (a.head_dim != 128 || a.num_seqs > 65535 || a.num_kv_heads > 65535) return VASR_PA_ENOT_SUPPORTED;
+  const bool bf = a.dtype == VASR_PA_BF16;
+  if (!bf && a.dtype != VASR_PA_F16) return VASR_PA_EINVAL_DTYPE;
+  switch (a.block_size) {
+    case 8: return bf ? launch_dequant_t<__nv_bfloat16, 8>(a, s) : launch_dequant_t<__half, 8>(a, s);
+    case 16: return bf ? launch_dequant_t<__nv_bfloat16, 16>(a, s) : launch_dequant_t<__half, 16>(a, s);
+    case 32: return bf ? launch_dequant_t<__nv_bfloat16, 32>(a, s) : launch_dequant_t<__half, 32>(a, s);
+    default: return VASR_PA_EINVAL_BLOCKSIZE;
+  }
 }
 
 int launch_gather(const GatherArgs &a, cudaStream_t s) {

@@ -181,6 +181,28 @@ DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_
 int launch_append(const AppendArgs &a, cudaStream_t s);
 int launch_decode(const DecodeArgs &a, cudaStream_t s);
 int launch_gather(const GatherArgs &a, cudaStream_t s);
+
+// fp8 pages of the block tables' live entries -> a 16-bit scratch pool
+// (block b * cols + i) and the remapped table; dtype = the pool's type.
+struct DequantArgs {
+  const void *key_cache;
+  const void *value_cache;
+  const uint32_t *block_tables;
+  const uint32_t *context_lens;
+  int num_seqs;
+  int cols;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  int64_t num_blocks;
+  int dtype;
+  const float *k_scale;
+  const float *v_scale;
+  void *key_out;
+  void *value_out;
+  uint32_t *table_out;
+};
+int launch_dequant_pages(const DequantArgs &a, cudaStream_t s);
 int launch_prefill(const PrefillArgs &a, cudaStream_t s);
 // Position tiles per sequence for CTAs of `positions` query positions:
 // ceil(max_query_len / positions); max_query_len 0 (unknown) counts as

@@ -66,6 +66,13 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64,
          _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _f32, _i64, _i32, _c_void_p],
     ),
+    "vasr_pa_paged_attention_varlen_prefill_fp8": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64,
+         _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _f32, _i64, _i32, _c_void_p, _c_void_p,
+         _c_void_p, _size, _c_void_p],
+    ),
+    "vasr_pa_paged_attention_varlen_prefill_fp8_workspace_size": (_size, [_i32, _i32, _i32, _i32, _i32]),
     "vasr_pa_copy_blocks": (
         _i32,
         [ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p), _i32, _c_void_p, _i64, _i64, _i64,

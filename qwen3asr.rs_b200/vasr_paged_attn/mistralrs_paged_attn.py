@@ -143,6 +143,26 @@ def reserve_paged_attention_workspace(device: torch.device, nbytes: int,
     return ws
 
 
+_PREFILL_SCRATCH: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _reserve_prefill_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The (device, stream) scratch of the fp8 prefill (a 16-bit copy of the live pages).
+
+    Separate from the paged-attention workspace, whose counters must stay zero."""
+    device = torch.device(device)
+    s = torch.cuda.current_stream(device)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), s.cuda_stream)
+    ws = _PREFILL_SCRATCH.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise _lib.VasrPaError(_lib.EINVAL_WORKSPACE,
+                                   "fp8 prefill scratch must be reserved before CUDA graph capture")
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _PREFILL_SCRATCH[key] = ws
+    return ws
+
+
 def paged_attention(q: torch.Tensor, k_scale: Optional[torch.Tensor], v_scale: Optional[torch.Tensor],
                     key_cache: torch.Tensor, value_cache: torch.Tensor, block_tables: torch.Tensor,
                     context_lens: torch.Tensor, alibi: Optional[torch.Tensor], max_context_len: int,
@@ -239,13 +259,18 @@ def paged_attention_varlen_prefill(q: torch.Tensor, key_cache: torch.Tensor, val
                                    v_scale: Optional[torch.Tensor], scale: float,
                                    softcapping: float = 1.0, max_query_len: Optional[int] = None,
                                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Causal chunked prefill: packed q ``[T, Hq, D]`` against each sequence's pages."""
-    del k_scale, v_scale
+    """Causal chunked prefill: packed q ``[T, Hq, D]`` against each sequence's pages.
+
+    fp8 (E4M3) pages need k_scale / v_scale; the pages are scaled into a 16-bit
+    scratch pool in the stream's workspace first."""
     dev = _require_cuda(q, key_cache, value_cache, block_tables, context_lens, cu_seqlens_q)
     nb, hkv, d, bs = cache_geometry(key_cache, value_cache)
     if q.dim() != 3 or q.shape[2] != d or q.stride(2) != 1 or q.stride(1) != d:
         raise _lib.VasrPaError(_lib.EINVAL_SHAPE, f"q must be [T, Hq, {d}] with packed heads")
-    if q.dtype != key_cache.dtype:
+    fp8 = key_cache.dtype == FP8_CACHE
+    if fp8:
+        _check_scales(k_scale, v_scale, dev)
+    elif q.dtype != key_cache.dtype:
         raise _lib.VasrPaError(_lib.EINVAL_DTYPE, "q dtype must equal the cache dtype")
     b = int(block_tables.shape[0])
     if cu_seqlens_q.shape != (b + 1,) or context_lens.shape != (b,):
@@ -256,6 +281,18 @@ def paged_attention_varlen_prefill(q: torch.Tensor, key_cache: torch.Tensor, val
     if out is None:
         out = torch.empty((t, hq, d), dtype=q.dtype, device=dev)
     bt = block_tables.contiguous()
+    if fp8:
+        need = int(_lib.lib().vasr_pa_paged_attention_varlen_prefill_fp8_workspace_size(
+            b, hkv, d, bs, int(bt.shape[1])))
+        ws = _reserve_prefill_scratch(dev, need)
+        st = _lib.lib().vasr_pa_paged_attention_varlen_prefill_fp8(
+            out.data_ptr(), q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), bt.data_ptr(),
+            context_lens.contiguous().data_ptr(), cu_seqlens_q.contiguous().data_ptr(), b, t,
+            int(max_query_len), hq, hkv, d, bs, nb, int(bt.shape[1]), float(scale),
+            float(softcapping), q.stride(0), dtype_code(q.dtype), k_scale.data_ptr(),
+            v_scale.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
+        _lib.check(st, "paged_attention_varlen_prefill (fp8 pages)")
+        return out
     st = _lib.lib().vasr_pa_paged_attention_varlen_prefill(
         out.data_ptr(), q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), bt.data_ptr(),
         context_lens.contiguous().data_ptr(), cu_seqlens_q.contiguous().data_ptr(), b, t,
