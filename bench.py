@@ -27,6 +27,11 @@ decoder replica and page pool and decodes its own 64 sequences (weak
 scaling, no collective on the hot path; one all-reduce of the elapsed time
 outside the timed region).
 
+``--config 5`` runs the same step for benchmark config 5 instead: a
+Qwen3-ASR-1.7B-shaped decoder (hidden 2048, MLP 6144) and 512 sequences with
+contexts ~log-U[64, 4096], split over the ranks by expected KV bytes (strong
+scaling: the 512 sequences are the whole job at every N), 64 timed steps.
+
 ``--impl reference`` times the reference's CPU attention path (the C
 restatement in oracle/, all host threads) on the same contexts.
 """
@@ -56,13 +61,17 @@ BLOCK_SIZE = 16
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default 100 for config 2, 64 for config 5)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the bounded cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--config", type=int, choices=[2, 5], default=2,
+                   help="decode-step workload: 2 = 0.6B decoder, 64 sequences per GPU (weak scaling); "
+                        "5 = 1.7B decoder, 512 sequences sharded over the GPUs (strong scaling)")
     p.add_argument("--kernel", default=None,
                    choices=["decode", "decode5", "decode_fp8", "append", "gather", "prefill", "prefill_fp8",
                             "copy", "swap", "config1"],
@@ -70,7 +79,10 @@ def parse_args():
     p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
     p.add_argument("--layers", type=int, default=28,
                    help="distinct per-layer caches cycled through by --kernel decode/copy")
-    return p.parse_args()
+    args = p.parse_args()
+    if args.steps is None:
+        args.steps = 64 if args.config == 5 else 100
+    return args
 
 
 # ------------------------------------------------------------------ helpers
@@ -166,20 +178,21 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_attention_sample(seed: int, target_seconds: float, steps: int | None = None):
+def cpu_attention_sample(seed: int, target_seconds: float, steps: int | None = None, lens=None):
     """Time the oracle's f32 decode attention (reference CPU path restated in C, all threads).
 
-    A step is 28 layers of decode attention over the config-2 context set;
-    one layer's cache is generated and attended 28 times per step (the cost
-    per layer is identical). GEMMs are excluded, so this is an upper bound on
-    the CPU's decode tok/s.
+    A step is 28 layers of decode attention over ``lens`` (default: the
+    config-2 context set); one layer's cache is generated and attended 28
+    times per step (the cost per layer is identical). GEMMs are excluded, so
+    this is an upper bound on the CPU's decode tok/s.
     """
     import numpy as np
 
     sys.path.insert(0, str(REPO / "oracle"))
     import paged_ref as ref
 
-    lens = context_lens(seed, 0)
+    lens = context_lens(seed, 0) if lens is None else np.asarray(lens, dtype=np.int64)
+    batch = len(lens)
     hq, hkv, d, bs = 16, 8, 128, BLOCK_SIZE
     blocks = [-(-int(n) // bs) for n in lens]
     nb = sum(blocks) + 1
@@ -187,12 +200,12 @@ def cpu_attention_sample(seed: int, target_seconds: float, steps: int | None = N
     kc = rng.standard_normal((nb, hkv, d // 4, bs, 4), dtype=np.float32)
     vc = rng.standard_normal((nb, hkv, d, bs), dtype=np.float32)
     perm = rng.permutation(np.arange(1, nb))
-    tables = np.zeros((BATCH, max(blocks)), np.uint32)
+    tables = np.zeros((batch, max(blocks)), np.uint32)
     off = 0
     for i, n in enumerate(blocks):
         tables[i, :n] = perm[off:off + n]
         off += n
-    q = rng.standard_normal((BATCH, hq, d), dtype=np.float32)
+    q = rng.standard_normal((batch, hq, d), dtype=np.float32)
     ctx = lens.astype(np.uint32)
     # all host cores this process may run on (torchrun sets OMP_NUM_THREADS=1 per worker,
     # so the OpenMP default would under-report the CPU path)
@@ -208,7 +221,7 @@ def cpu_attention_sample(seed: int, target_seconds: float, steps: int | None = N
         for _ in range(reps):
             ref.paged_attention(q, kc, vc, tables, ctx, d ** -0.5, use_double=False, threads=threads)
         t_layer = (time.perf_counter() - t0) / reps
-        return dict(tok_s=BATCH / (n_layers * t_layer), t_layer=t_layer, reps=reps, threads=threads)
+        return dict(tok_s=batch / (n_layers * t_layer), t_layer=t_layer, reps=reps, threads=threads)
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
@@ -271,11 +284,22 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
-    cfg = eng.DecoderConfig.qwen3_asr_0_6b()
+    if args.config == 5:
+        # 1.7B decoder; the 512 sequences are split over the ranks by expected KV bytes
+        from vasr_paged_attn.sharding import lpt_shard
+        from vasr_paged_attn.workloads import config5_context_lens
+        cfg = eng.DecoderConfig.qwen3_asr_1_7b()
+        all_lens = config5_context_lens(args.seed)
+        lens0 = np.asarray(all_lens[sorted(lpt_shard(all_lens.tolist(), world)[rank])], dtype=np.int64)
+        global_batch = len(all_lens)
+    else:
+        cfg = eng.DecoderConfig.qwen3_asr_0_6b()
+        lens0 = context_lens(args.seed, rank)
+        global_batch = BATCH * world
+    batch = len(lens0)
     model = eng.RandomQwen3Decoder(cfg, dev, torch.bfloat16, seed=args.seed)
     k_steps, w_steps = args.steps, max(3, args.warmup)
     total_steps = 3 * (w_steps + k_steps) + 2  # device-resident, e2e and device-loop runs
-    lens0 = context_lens(args.seed, rank)
     need_tok = lens0 + total_steps
     blocks = np.array([-(-int(n) // BLOCK_SIZE) for n in need_tok])
     nb = int(blocks.sum()) + 1
@@ -284,7 +308,7 @@ def run_ours(args):
     raw_cols = int(blocks.max())
     from vasr_paged_attn import host
     cols = host.bucket_block_table_cols(raw_cols, BLOCK_SIZE)
-    tables = np.zeros((BATCH, cols), np.int32)
+    tables = np.zeros((batch, cols), np.int32)
     off = 0
     for i, n in enumerate(blocks):
         tables[i, :n] = perm[off:off + n]
@@ -295,19 +319,19 @@ def run_ours(args):
         kc.normal_(generator=gen)
         vc.normal_(generator=gen)
 
-    graph = eng.DecodeGraph(model, caches, BATCH, cols, BLOCK_SIZE)
+    graph = eng.DecodeGraph(model, caches, batch, cols, BLOCK_SIZE)
     graph.capture()
 
     # per-step metadata, device resident: positions advance by one per step
     steps_all = np.arange(total_steps)[:, None]
     pos = lens0[None, :] + steps_all                                    # [S, B]
-    slots = tables[np.arange(BATCH)[None, :], pos // BLOCK_SIZE].astype(np.int64) * BLOCK_SIZE + pos % BLOCK_SIZE
+    slots = tables[np.arange(batch)[None, :], pos // BLOCK_SIZE].astype(np.int64) * BLOCK_SIZE + pos % BLOCK_SIZE
     ctx = (pos + 1).astype(np.int32)
     d_pos = torch.from_numpy(pos.astype(np.int64)).to(dev)
     d_slots = torch.from_numpy(slots).to(dev)
     d_ctx = torch.from_numpy(ctx).to(dev)
     d_tables = torch.from_numpy(tables).to(dev)
-    d_ids = torch.zeros(BATCH, dtype=torch.int64, device=dev)
+    d_ids = torch.zeros(batch, dtype=torch.int64, device=dev)
 
     def device_step(s):
         graph.input_ids.copy_(graph.next_ids if s > 0 else d_ids)
@@ -354,7 +378,7 @@ def run_ours(args):
     barrier()
     dev_ms = max_over_ranks(e0.elapsed_time(e1))
     windows.append((w0, time.time()))
-    value = world * BATCH * k_steps / (dev_ms / 1e3)
+    value = global_batch * k_steps / (dev_ms / 1e3)
 
     # ---- e2e: host-built metadata, pinned H2D, replay, D2H of next ids. The
     # pinned metadata is double-buffered so that the host builds step s + 1
@@ -363,14 +387,14 @@ def run_ours(args):
     meta_cache = host.metadata_cache(nb, cfg.num_kv_heads, cfg.head_dim, BLOCK_SIZE, "bf16")
 
     def pinned_set():
-        return {"ids": torch.zeros(BATCH, dtype=torch.int64).pin_memory(),
-                "pos": torch.zeros(BATCH, dtype=torch.int64).pin_memory(),
-                "slots": torch.zeros(BATCH, dtype=torch.int64).pin_memory(),
-                "ctx": torch.zeros(BATCH, dtype=torch.int32).pin_memory(),
-                "tables": torch.zeros(BATCH, cols, dtype=torch.int32).pin_memory()}
+        return {"ids": torch.zeros(batch, dtype=torch.int64).pin_memory(),
+                "pos": torch.zeros(batch, dtype=torch.int64).pin_memory(),
+                "slots": torch.zeros(batch, dtype=torch.int64).pin_memory(),
+                "ctx": torch.zeros(batch, dtype=torch.int32).pin_memory(),
+                "tables": torch.zeros(batch, cols, dtype=torch.int32).pin_memory()}
 
     sets = [pinned_set(), pinned_set()]
-    h_next = torch.zeros(BATCH, dtype=torch.int64).pin_memory()
+    h_next = torch.zeros(batch, dtype=torch.int64).pin_memory()
     prompt_lens = [int(x) for x in lens0]
     table_rows = [list(map(int, r[:n])) for r, n in zip(tables, blocks)]
     stream = torch.cuda.current_stream()
@@ -411,14 +435,14 @@ def run_ours(args):
     windows.append((w0, time.time()))
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
-    e2e_value = world * BATCH * k_steps / e2e_s
+    e2e_value = global_batch * k_steps / e2e_s
     h2d = sum(t.numel() * t.element_size() for t in sets[0].values())
     d2h = h_next.numel() * 8
 
     # ---- device decode loop: prepare -> forward -> argmax replayed with no host round trip
     from vasr_paged_attn import decode_loop as dloop
     loop_state = dloop.DecodeLoopState(
-        [int(x) + s_idx for x in lens0], [0] * BATCH, [cfg.vocab_size],  # EOS id outside the vocab:
+        [int(x) + s_idx for x in lens0], [0] * batch, [cfg.vocab_size],  # EOS id outside the vocab:
         torch.from_numpy(tables).to(dev), blocks.tolist(), BLOCK_SIZE, nb,  # every row stays active
         cfg.vocab_size, device=dev)
     loop = eng.DecodeLoopGraph(model, caches, loop_state, BLOCK_SIZE)
@@ -439,14 +463,14 @@ def run_ours(args):
     loop_ms = max_over_ranks(l0.elapsed_time(l1))
     barrier()
     fin, gen_counts, _ = loop_state.read_back()
-    loop_value = world * BATCH * k_steps / (loop_ms / 1e3)
+    loop_value = global_batch * k_steps / (loop_ms / 1e3)
     s_idx += w_steps + k_steps
     loop.release()
 
     # ---- roofline of the paged decode kernel: one launch per layer, events on its stream
     last = s_idx - 1
     ctx_last = torch.from_numpy(ctx[min(last, total_steps - 1)]).to(dev)
-    q = torch.randn(BATCH, cfg.num_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(batch, cfg.num_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
     out = torch.empty_like(q)
     mcl = cols * BLOCK_SIZE
 
@@ -459,7 +483,7 @@ def run_ours(args):
     launch_ms = _events_time(decode_layer, 3 * len(caches))
     ctx_sum = int(ctx[min(last, total_steps - 1)].astype(np.int64).sum())
     kv_bytes = ctx_sum * cfg.num_kv_heads * cfg.head_dim * 2 * 2
-    qo_bytes = BATCH * cfg.num_heads * cfg.head_dim * 2 * 2
+    qo_bytes = batch * cfg.num_heads * cfg.head_dim * 2 * 2
     alg_bytes = kv_bytes + qo_bytes
     achieved = alg_bytes / (launch_ms / 1e3) / 1e9
     peak, peak_kind = load_peaks()
@@ -471,24 +495,42 @@ def run_ours(args):
             traffic = ratio * alg_bytes
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 5:
+        # bounded: 64 of the 512 sequences, their layer time scaled by the context sum
+        sub = lens0[:BATCH]
+        r = cpu_attention_sample(args.seed, args.cpu_seconds, lens=sub)
+        t_full = r["t_layer"] * float(lens0.sum()) / float(sub.sum())
+        cpu = {"value": batch / (cfg.num_layers * t_full), "unit": "tok/s", "cores": r["threads"],
+               "kind": "port",
+               "sample": (f"{r['reps']} x one decode-attention layer over {len(sub)} of the {batch} "
+                          f"config-5 sequences (f32 C/OpenMP oracle), layer time scaled by the context "
+                          f"sum to all {batch} and to 28 layers per token step; GEMMs excluded; {cpu_info()}")}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_attention_sample(args.seed, args.cpu_seconds)
         cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
-               "sample": (f"{r['reps']} x one decode-attention layer ({BATCH} seqs, ctx U[{CTX_LO},{CTX_HI}], "
+               "sample": (f"{r['reps']} x one decode-attention layer ({batch} seqs, ctx U[{CTX_LO},{CTX_HI}], "
                           f"f32 C/OpenMP oracle), scaled to 28 layers per token step; GEMMs excluded; "
                           f"{cpu_info()}")}
+    kv_step_gb = float(lens0.sum()) * cfg.num_kv_heads * cfg.head_dim * 2 * 2 * cfg.num_layers / 1e9
+    if args.config == 5:
+        workload = ("config5: qwen3-asr-1.7B decode step, 28 layers, 512 sequences sharded over "
+                    f"{world} GPU(s) by KV bytes ({batch} on rank 0), ctx log-U[64,4096], block_size 16")
+        model_name = "Qwen3-ASR-1.7B text decoder (random init)"
+    else:
+        workload = "config2: qwen3-asr-0.6B decode step, 28 layers, B=64 per GPU, ctx U[200,1500], block_size 16"
+        model_name = "Qwen3-ASR-0.6B text decoder (random init)"
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": k_steps,
             "warmup": w_steps, "ms_per_step": dev_ms / k_steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if args.config == 5 else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded contexts, random-init weights, N(0,1) cache)",
-            "config": {"workload": "config2: qwen3-asr-0.6B decode step, 28 layers, B=64 per GPU, "
-                                   "ctx U[200,1500], block_size 16",
-                       "model": "Qwen3-ASR-0.6B text decoder (random init)", "global_batch": BATCH * world,
+            "config": {"workload": workload, "model": model_name, "global_batch": global_batch,
                        "seq_len": int(lens0.mean()), "parallelism": f"dp{world} (request-sharded)",
-                       "graph_cols": cols, "l2": "inputs larger than L2 (per step ~6.2 GB KV + 1.2 GB weights)"},
+                       "graph_cols": cols,
+                       "l2": (f"inputs larger than L2 (per step {kv_step_gb:.1f} GB KV + "
+                              f"{model.weight_bytes() / 1e9:.1f} GB weights on rank 0)")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "kernel": "paged_decode_mma_kernel",
                          "peak_source": peak_kind, "launch_us": launch_ms * 1e3,
