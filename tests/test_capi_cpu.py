@@ -77,6 +77,59 @@ def test_decode_rejects_bad_arguments_and_sizes_workspace():
     assert call(B=0) == _lib.OK
 
 
+def _prefill_args(**kw):
+    a = dict(B=4, T=64, maxq=16, Hq=16, Hkv=8, D=128, bs=16, nb=40, cols=8, softcap=1.0,
+             stride=16 * 128, dt=_lib.BF16)
+    a.update(kw)
+    return a
+
+
+def test_prefill_rejects_bad_arguments_before_any_cuda_call():
+    f = _lib.lib().vasr_pa_paged_attention_varlen_prefill
+    p = ctypes.c_void_p(256)
+
+    def call(**kw):
+        a = _prefill_args(**kw)
+        ptr = kw.get("ptr", p)
+        return f(ptr, p, p, p, p, p, p, a["B"], a["T"], a["maxq"], a["Hq"], a["Hkv"], a["D"],
+                 a["bs"], a["nb"], a["cols"], 0.088, a["softcap"], a["stride"], a["dt"], None)
+
+    assert call(bs=12) == _lib.EINVAL_BLOCKSIZE
+    assert call(dt=9) == _lib.EINVAL_DTYPE
+    assert call(Hkv=6) == _lib.EINVAL_SHAPE            # Hq % Hkv != 0
+    assert call(stride=100) == _lib.EINVAL_SHAPE       # token stride shorter than a token
+    assert call(softcap=0.0) == _lib.EINVAL_SHAPE
+    assert call(ptr=None) == _lib.EINVAL_POINTER
+    assert call(ptr=ctypes.c_void_p(258)) == _lib.EINVAL_ALIGN
+    assert call(B=0) == _lib.OK and call(T=0) == _lib.OK   # empty batches launch nothing
+
+
+def test_fp8_prefill_sizes_its_scratch_and_rejects_bad_arguments():
+    lib = _lib.lib()
+    ws = lib.vasr_pa_paged_attention_varlen_prefill_fp8_workspace_size
+    # 16-bit K and V copies of every (sequence, column) page plus the remapped table
+    pages = 4 * 8 * 8 * 128 * 16 * 2
+    assert ws(4, 8, 128, 16, 8) >= 2 * pages + 4 * 8 * 4
+    assert ws(0, 8, 128, 16, 8) == 0 and ws(4, 8, 128, 16, 0) == 0
+    f = lib.vasr_pa_paged_attention_varlen_prefill_fp8
+    p = ctypes.c_void_p(256)
+    need = ws(4, 8, 128, 16, 8)
+
+    def call(scale_ptr=p, ws_ptr=p, ws_bytes=need, **kw):
+        a = _prefill_args(**kw)
+        return f(p, p, p, p, p, p, p, a["B"], a["T"], a["maxq"], a["Hq"], a["Hkv"], a["D"], a["bs"],
+                 a["nb"], a["cols"], 0.088, a["softcap"], a["stride"], a["dt"], scale_ptr, p, ws_ptr,
+                 ws_bytes, None)
+
+    assert call(dt=_lib.FP8_E4M3) == _lib.EINVAL_DTYPE   # dtype names the query / output type
+    assert call(dt=_lib.F32) == _lib.EINVAL_DTYPE
+    assert call(scale_ptr=None) == _lib.EINVAL_POINTER   # fp8 pages need both scales
+    assert call(ws_ptr=None) == _lib.EINVAL_WORKSPACE
+    assert call(ws_bytes=need - 1) == _lib.EINVAL_WORKSPACE
+    assert call(D=64, stride=16 * 64) == _lib.ENOT_SUPPORTED
+    assert call(B=0) == _lib.OK
+
+
 def test_block_ops_reject_bad_arguments():
     lib = _lib.lib()
     arr = (ctypes.c_void_p * 2)(16, 32)
