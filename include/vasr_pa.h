@@ -146,6 +146,33 @@ int32_t vasr_pa_paged_attention(void *out, const void *query,
                                 vasr_pa_stream_t stream);
 
 /*
+ * vasr_pa_paged_attention issued right behind this step's KV append on the
+ * same stream (vasr_pa_fused_qk_norm_rope_append or vasr_pa_reshape_and_cache,
+ * the pair at thinker_text.rs:1101-1139), as a programmatic dependent launch:
+ * its CTAs start while the append still runs and stream every page before
+ * each sequence's last one, then wait for the append to complete before
+ * reading q, the last page or writing anything. Same arguments, results
+ * and errors as vasr_pa_paged_attention. Contract: the kernel immediately
+ * before it on the stream writes nothing this call reads except q and
+ * tokens in each sequence's last page (as a decode append does), and was
+ * itself launched in ordinary stream order. Other dtypes and GQA groups than
+ * the 16-bit GQA-2 kernel launch as vasr_pa_paged_attention does.
+ */
+int32_t vasr_pa_paged_attention_after_append(void *out, const void *query,
+                                             const void *key_cache, const void *value_cache,
+                                             const uint32_t *block_tables,
+                                             const uint32_t *context_lens, int32_t num_seqs,
+                                             int32_t num_heads, int32_t num_kv_heads,
+                                             int32_t head_dim, int32_t block_size,
+                                             int64_t num_blocks,
+                                             int32_t max_num_blocks_per_seq,
+                                             int32_t max_context_len, float scale,
+                                             float softcapping, int64_t q_seq_stride,
+                                             int32_t dtype, void *workspace,
+                                             size_t workspace_bytes,
+                                             vasr_pa_stream_t stream);
+
+/*
  * Decode attention for callers that cannot allocate device memory.
  * No counterpart in the reference: it is an addition of this library.
  *

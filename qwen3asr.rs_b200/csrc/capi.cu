@@ -171,14 +171,15 @@ size_t vasr_pa_paged_attention_workspace_size(int32_t num_seqs, int32_t num_head
       .total;
 }
 
-int32_t vasr_pa_paged_attention(void *out, const void *query, const void *key_cache,
-                                const void *value_cache, const uint32_t *block_tables,
-                                const uint32_t *context_lens, int32_t num_seqs, int32_t num_heads,
-                                int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
-                                int64_t num_blocks, int32_t max_num_blocks_per_seq,
-                                int32_t max_context_len, float scale, float softcapping,
-                                int64_t q_seq_stride, int32_t dtype, void *workspace,
-                                size_t workspace_bytes, vasr_pa_stream_t stream) {
+namespace {
+int32_t paged_attention_impl(void *out, const void *query, const void *key_cache,
+                             const void *value_cache, const uint32_t *block_tables,
+                             const uint32_t *context_lens, int32_t num_seqs, int32_t num_heads,
+                             int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                             int64_t num_blocks, int32_t max_num_blocks_per_seq,
+                             int32_t max_context_len, float scale, float softcapping,
+                             int64_t q_seq_stride, int32_t dtype, void *workspace,
+                             size_t workspace_bytes, vasr_pa_stream_t stream, int overlap_append) {
   const int g = check_geometry(dtype, num_kv_heads, head_dim, block_size, num_blocks);
   if (g != VASR_PA_OK) return g;
   if (num_seqs < 0 || num_heads <= 0 || num_heads % num_kv_heads != 0 ||
@@ -199,7 +200,36 @@ int32_t vasr_pa_paged_attention(void *out, const void *query, const void *key_ca
                num_heads, num_kv_heads, head_dim, block_size, num_blocks, max_num_blocks_per_seq,
                max_context_len > 0 ? max_context_len : 1, scale, softcapping, q_seq_stride, dtype,
                workspace, workspace_bytes};
+  a.overlap_append = overlap_append;
   return vasr::launch_decode(a, to_stream(stream));
+}
+}  // namespace
+
+int32_t vasr_pa_paged_attention(void *out, const void *query, const void *key_cache,
+                                const void *value_cache, const uint32_t *block_tables,
+                                const uint32_t *context_lens, int32_t num_seqs, int32_t num_heads,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                int64_t num_blocks, int32_t max_num_blocks_per_seq,
+                                int32_t max_context_len, float scale, float softcapping,
+                                int64_t q_seq_stride, int32_t dtype, void *workspace,
+                                size_t workspace_bytes, vasr_pa_stream_t stream) {
+  return paged_attention_impl(out, query, key_cache, value_cache, block_tables, context_lens,
+                              num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                              max_num_blocks_per_seq, max_context_len, scale, softcapping,
+                              q_seq_stride, dtype, workspace, workspace_bytes, stream, 0);
+}
+
+int32_t vasr_pa_paged_attention_after_append(
+    void *out, const void *query, const void *key_cache, const void *value_cache,
+    const uint32_t *block_tables, const uint32_t *context_lens, int32_t num_seqs,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int64_t num_blocks, int32_t max_num_blocks_per_seq, int32_t max_context_len, float scale,
+    float softcapping, int64_t q_seq_stride, int32_t dtype, void *workspace,
+    size_t workspace_bytes, vasr_pa_stream_t stream) {
+  return paged_attention_impl(out, query, key_cache, value_cache, block_tables, context_lens,
+                              num_seqs, num_heads, num_kv_heads, head_dim, block_size, num_blocks,
+                              max_num_blocks_per_seq, max_context_len, scale, softcapping,
+                              q_seq_stride, dtype, workspace, workspace_bytes, stream, 1);
 }
 
 int32_t vasr_pa_gather_kv_cache(void *key_out, void *value_out, const void *key_cache,

@@ -108,6 +108,16 @@ __device__ __forceinline__ void unpack_chunk<__nv_fp8_e4m3>(const uint4 &u, floa
 }
 
 // ------------------------------------------------------- shared-memory I/O
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while the kernel before it on the stream still
+// runs; pdl_wait() returns once that kernel has completed and its memory
+// operations are visible (at once when the launch was an ordinary one).
+// pdl_launch_dependents() lets such a dependent start before this grid ends.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

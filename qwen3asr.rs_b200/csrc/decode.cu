@@ -21,6 +21,10 @@
 #ifndef VASR_DECODE_MMA
 #define VASR_DECODE_MMA 1
 #endif
+// honour DecodeArgs::overlap_append with a programmatic dependent launch
+#ifndef VASR_DECODE_PDL
+#define VASR_DECODE_PDL 1
+#endif
 
 namespace vasr {
 
@@ -124,6 +128,19 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
     static std::atomic<uint64_t> attr_done{0};
     if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
     dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+    if (VASR_DECODE_PDL && a.overlap_append) {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = grid;
+      cfg.blockDim = dim3(C::kThreads);
+      cfg.dynamicSmemBytes = C::kSmemBytes;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+    }
     kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }

@@ -108,26 +108,6 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
   const int spec_col = split * p.pages_per_split + tid;
   if (tid < p.pages_per_split && spec_col < p.cols)
     spec_id = __ldg(p.block_tables + (int64_t)b * p.cols + spec_col);
-  // query fragments (A operand, rows = heads): lanes 0-7 hold rows 0 / 1
-  uint32_t qa[kKS][2];
-  {
-    const T *qp = reinterpret_cast<const T *>(p.q) + (int64_t)b * p.q_seq_stride +
-                  (int64_t)(kvh * G + (grp & 1)) * D;
-#pragma unroll
-    for (int ks = 0; ks < kKS; ++ks) {
-      if constexpr (kFp8) {  // dims 4 tig .. 4 tig + 3 of the k-step, as f16 pairs
-        qa[ks][0] = qa[ks][1] = 0u;
-        if (grp < G) {
-          const T *q4 = qp + ks * 16 + tig * 4;
-          qa[ks][0] = dec_pack2<__half>(Elem<T>::to_f32(q4[0]), Elem<T>::to_f32(q4[1]));
-          qa[ks][1] = dec_pack2<__half>(Elem<T>::to_f32(q4[2]), Elem<T>::to_f32(q4[3]));
-        }
-      } else {
-        qa[ks][0] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + tig * 2)) : 0u;
-        qa[ks][1] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + 8 + tig * 2)) : 0u;
-      }
-    }
-  }
   int ctx = (int)p.context_lens[b];
   const int cap_tables = p.cols * BS;
   const int cap_splits = p.max_splits * P;
@@ -137,6 +117,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
   }
   T *out = reinterpret_cast<T *>(p.out) + ((int64_t)b * p.num_heads + (int64_t)kvh * G) * D;
   if (ctx <= 0) {
+    pdl_wait();  // no global write before the preceding kernel has completed
     if (split == 0)
       for (int e = tid; e < G * D; e += C::kThreads) out[e] = Elem<T>::from_f32(0.f);
     return;
@@ -180,8 +161,41 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
       bulk_g2s(s_base + C::kOffV + (s * C::kSP + i) * C::kPB, vc + off, C::kPB, bar);
     }
   };
+  // Under a programmatic launch behind this step's KV append (which writes
+  // q and each sequence's newest token only), everything read so far and
+  // every page before the sequence's last one is already final: those stages
+  // stream in while the append still runs. The stage holding the last page,
+  // q, and every global write (bar the error word's atomic OR) wait for the
+  // append to complete.
+  const int last_in_split = seq_pages - 1 - page_begin;
+  const int late_unit = (last_in_split >= 0 && last_in_split < n_pages) ? last_in_split / C::kSP : -1;
   if (lane == 0)
-    for (int u = warp; u < min(C::kNST, n_units); u += C::kWarps) issue_unit(u);
+    for (int u = warp; u < min(C::kNST, n_units); u += C::kWarps)
+      if (u != late_unit) issue_unit(u);
+  pdl_wait();
+  if (lane == 0 && late_unit >= 0 && late_unit < C::kNST && late_unit % C::kWarps == warp)
+    issue_unit(late_unit);
+
+  // query fragments (A operand, rows = heads): lanes 0-7 hold rows 0 / 1
+  uint32_t qa[kKS][2];
+  {
+    const T *qp = reinterpret_cast<const T *>(p.q) + (int64_t)b * p.q_seq_stride +
+                  (int64_t)(kvh * G + (grp & 1)) * D;
+#pragma unroll
+    for (int ks = 0; ks < kKS; ++ks) {
+      if constexpr (kFp8) {  // dims 4 tig .. 4 tig + 3 of the k-step, as f16 pairs
+        qa[ks][0] = qa[ks][1] = 0u;
+        if (grp < G) {
+          const T *q4 = qp + ks * 16 + tig * 4;
+          qa[ks][0] = dec_pack2<__half>(Elem<T>::to_f32(q4[0]), Elem<T>::to_f32(q4[1]));
+          qa[ks][1] = dec_pack2<__half>(Elem<T>::to_f32(q4[2]), Elem<T>::to_f32(q4[3]));
+        }
+      } else {
+        qa[ks][0] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + tig * 2)) : 0u;
+        qa[ks][1] = grp < G ? __ldg(reinterpret_cast<const uint32_t *>(qp + ks * 16 + 8 + tig * 2)) : 0u;
+      }
+    }
+  }
 
   // fp8 pages hold K / k_scale and V / v_scale
   const float k_mul = p.k_scale ? p.scale * __ldg(p.k_scale) : p.scale;

@@ -69,6 +69,9 @@ constexpr int kWarpsPerCta = 8;
 template <typename T, int BS>
 __global__ void __launch_bounds__(32 * kWarpsPerCta) fused_qk_norm_rope_append_kernel(
     const FusedRopeParams p) {
+  // A decode launched behind this kernel as a programmatic dependent may
+  // start now: it reads nothing this kernel writes before it waits.
+  pdl_launch_dependents();
   constexpr int D = 128;
   constexpr int kX = Elem<T>::kX;
   const int tasks = p.num_heads + 2 * p.num_kv_heads;

@@ -54,6 +54,9 @@ struct DecodeArgs {
   int cache_dtype = -1;            // -1: same as dtype; VASR_PA_FP8_E4M3: scaled fp8 pages
   const float *k_scale = nullptr;  // fp8: device scalars, real K = stored K * k_scale
   const float *v_scale = nullptr;
+  // Launch as a programmatic dependent of the preceding kernel on the stream
+  // (the KV append of this step); honoured by the GQA-2 tensor-core kernel.
+  int overlap_append = 0;
 };
 
 struct GatherArgs {

@@ -56,6 +56,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32,
          _i32, _i32, _i64, _i32, _i32, _f32, _f32, _i64, _i32, _c_void_p, _size, _c_void_p],
     ),
+    "vasr_pa_paged_attention_after_append": (
+        _i32,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i32,
+         _i32, _i32, _i64, _i32, _i32, _f32, _f32, _i64, _i32, _c_void_p, _size, _c_void_p],
+    ),
     "vasr_pa_gather_kv_cache": (
         _i32,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, _i64,

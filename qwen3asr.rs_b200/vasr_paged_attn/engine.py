@@ -148,8 +148,10 @@ class RandomQwen3Decoder:
                 q = self._rope(q, cos, sin)
                 k = self._rope(k, cos, sin)
                 pa.reshape_and_cache(k, v, None, None, kc, vc, slot_mapping)
+            # fused: the append kernel is the one just issued, so the decode
+            # starts streaming older pages while it finishes
             attn = pa.paged_attention(q, None, None, kc, vc, block_tables, context_lens, None,
-                                      max_context_len, scale, 1.0, None)
+                                      max_context_len, scale, 1.0, None, after_append=fused)
             x = x + attn.view(b, hq * d) @ l["w_o"].t()
             h = F.rms_norm(x, (cfg.hidden_size,), l["post_norm"], cfg.rms_norm_eps)
             gu = h @ l["w_gate_up"].t()

@@ -167,8 +167,15 @@ def paged_attention(q: torch.Tensor, k_scale: Optional[torch.Tensor], v_scale: O
                     key_cache: torch.Tensor, value_cache: torch.Tensor, block_tables: torch.Tensor,
                     context_lens: torch.Tensor, alibi: Optional[torch.Tensor], max_context_len: int,
                     softmax_scale: float, softcapping: float = 1.0,
-                    sinks: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Single-token decode attention over the pages; returns ``[B, Hq, D]`` in q's dtype."""
+                    sinks: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                    after_append: bool = False) -> torch.Tensor:
+    """Single-token decode attention over the pages; returns ``[B, Hq, D]`` in q's dtype.
+
+    ``after_append=True`` (16-bit pages) launches it as a programmatic
+    dependent of the kernel just issued on the current stream, which must be
+    this step's KV append (``reshape_and_cache`` or the fused q/k norm + RoPE +
+    append): the pages before each sequence's last one stream in while the
+    append finishes (vasr_pa_paged_attention_after_append)."""
     if alibi is not None or sinks is not None:
         raise _lib.VasrPaError(_lib.ENOT_SUPPORTED, "alibi / attention sinks are not used by Qwen3-ASR")
     dev = _require_cuda(q, key_cache, value_cache, block_tables, context_lens)
@@ -200,7 +207,8 @@ def paged_attention(q: torch.Tensor, k_scale: Optional[torch.Tensor], v_scale: O
             ws.numel(), _stream(dev))
         _lib.check(st, "paged_attention (fp8 cache)")
         return out
-    st = _lib.lib().vasr_pa_paged_attention(
+    entry = _lib.lib().vasr_pa_paged_attention_after_append if after_append else _lib.lib().vasr_pa_paged_attention
+    st = entry(
         out.data_ptr(), q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), b, hq, hkv, d, bs, nb,
         int(block_tables.shape[1]), int(max_context_len), float(softmax_scale), float(softcapping),

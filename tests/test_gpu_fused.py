@@ -100,3 +100,86 @@ def test_fused_step_matches_unfused_step(cuda_device):
         assert ulp_close(bits(wa), bits(wb))
         assert (ka.view(torch.int16) != kb.view(torch.int16)).sum().item() == \
             (wa.view(torch.int16) != wb.view(torch.int16)).sum().item()
+
+
+def _after_append_case(dev, layers=4, b=64, bs=16, seed=5):
+    hq, hkv, d = 16, 8, 128
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(200, 1501, size=b)  # tokens already cached; the step appends one more
+    blocks = (lens + 1 + bs - 1) // bs
+    cols = int(blocks.max())
+    nb = int(blocks.sum()) + 1
+    perm = rng.permutation(np.arange(1, nb))
+    tables = np.zeros((b, cols), np.int32)
+    off = 0
+    for i, n in enumerate(blocks):
+        tables[i, :n] = perm[off:off + n]
+        off += n
+    slots = tables[np.arange(b), lens // bs].astype(np.int64) * bs + lens % bs
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    caches = []
+    for _ in range(layers):
+        kc = torch.randn(nb, hkv, d // 8, bs, 8, generator=gen, device=dev).to(torch.bfloat16)
+        vc = torch.randn(nb, hkv, d, bs, generator=gen, device=dev).to(torch.bfloat16)
+        # the new token's slot holds stale data far from what the append writes:
+        # a decode that read it before the append completed would be far off
+        pg = torch.from_numpy(slots // bs).to(dev)
+        of = torch.from_numpy(slots % bs).to(dev)
+        kc[pg, :, :, of, :] = 40.0
+        vc[pg, :, :, of] = -40.0
+        caches.append((kc, vc))
+    qkv = [torch.randn(b, (hq + 2 * hkv) * d, generator=gen, device=dev).to(torch.bfloat16)
+           for _ in range(layers)]
+    norm_w = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    cfg = DecoderConfig(num_layers=1, vocab_size=16, max_positions=4096)
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+    ang = torch.outer(torch.arange(4096, dtype=torch.float64), inv)
+    cos, sin = torch.cos(ang).float().to(dev), torch.sin(ang).float().to(dev)
+    meta = dict(pos=torch.from_numpy(lens).to(dev), slots=torch.from_numpy(slots).to(dev),
+                ctx=torch.from_numpy((lens + 1).astype(np.int32)).to(dev),
+                tables=torch.from_numpy(tables).to(dev), mcl=cols * bs, hq=hq)
+    return caches, qkv, norm_w, cos, sin, meta
+
+
+def _append_then_decode(caches, qkv, norm_w, cos, sin, m, after_append):
+    outs = []
+    for (kc, vc), x in zip(caches, qkv):
+        q = fused.qk_norm_rope_append(x, norm_w, norm_w, 1e-6, cos, sin, m["pos"], kc, vc, m["slots"], m["hq"])
+        outs.append(pa.paged_attention(q, None, None, kc, vc, m["tables"], m["ctx"], None, m["mcl"],
+                                       128 ** -0.5, 1.0, None, after_append=after_append))
+    return outs
+
+
+def test_decode_after_append_equals_plain_decode(cuda_device):
+    """The programmatic-dependent decode behind the append gives the plain call's bits,
+    eagerly and in a CUDA graph of append -> decode pairs, although the new token's
+    slot held stale data until the append wrote it."""
+    dev = cuda_device
+    caches, qkv, w, cos, sin, m = _after_append_case(dev)
+    ref_caches = [(k.clone(), v.clone()) for k, v in caches]
+    graph_caches = [(k.clone(), v.clone()) for k, v in caches]
+    want = _append_then_decode(ref_caches, qkv, w, cos, sin, m, after_append=False)
+    got = _append_then_decode(caches, qkv, w, cos, sin, m, after_append=True)
+    torch.cuda.synchronize()
+    for a, b in zip(got, want):
+        assert torch.equal(a, b)
+    for (ka, va), (kb, vb) in zip(caches, ref_caches):
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+    # the stale values are gone from the outputs: |out| stays at the N(0,1) V scale
+    assert max(float(o.float().abs().max()) for o in got) < 8.0
+
+    s = torch.cuda.Stream(device=dev)
+    need = pa.paged_attention_workspace_bytes(64, 16, 8, 128, 16, m["mcl"], torch.bfloat16)
+    pa.reserve_paged_attention_workspace(dev, need, s)  # one workspace per stream, before capture
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            outs = _append_then_decode(graph_caches, qkv, w, cos, sin, m, after_append=True)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):  # the append rewrites the same slot with the same values
+        g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(outs, want):
+        assert torch.equal(a, b)
+    del g
