@@ -184,8 +184,11 @@ int launch_append_t(const AppendArgs &a, cudaStream_t stream) {
 // ========================================================== gather_kv_cache
 // Reference semantics: mistralrs_paged_attn::gather_kv_cache as called at
 // thinker_text.rs:190-198 / :1344-1352: packed [sum kv, Hkv, D] K and V.
-// One CTA per (page, sequence): K chunks are copied as 16-byte vectors;
-// V pages [D][BS] are transposed through shared memory.
+// One CTA per (page, sequence, kv head). Every thread first issues all of
+// its 16-byte loads (K chunks into registers, V chunks too), so a CTA keeps
+// its whole page pair in flight; K chunks are stored as they are (a K chunk
+// is 16 bytes of one token's row), V rows [D][BS] are transposed through
+// shared memory into 16-byte vectors of one token's row.
 struct GatherParams {
   unsigned char *k_out;
   unsigned char *v_out;
@@ -198,53 +201,98 @@ struct GatherParams {
   int num_kv_heads;
 };
 
-template <typename T, int BS, int D>
-__global__ void __launch_bounds__(256) gather_kernel(const GatherParams p) {
-  constexpr int kX = Elem<T>::kX;
-  constexpr int kCH = D / kX;
-  constexpr int kES = (int)sizeof(T);
-  constexpr int kRowWords = BS * kES / 4 + 1;  // padded V row, in 32-bit words
-  extern __shared__ __align__(16) uint32_t vsm[];
-  const int page = blockIdx.x;
-  const int b = blockIdx.y;
+// threads per CTA for a page of `chunks` 16-byte chunks: about 4 chunks each
+constexpr int gather_threads(int chunks) {
+  return chunks / 4 < 32 ? 32 : (chunks / 4 > 256 ? 256 : chunks / 4);
+}
+
+// Locates (page, sequence, kv head) of this CTA; false when the page lies
+// past the sequence. Block ids past the pool read block 0 and are flagged.
+__device__ __forceinline__ bool gather_page(const GatherParams &p, int BS, int &n, int64_t &tok0,
+                                            uint32_t &blk) {
+  const int page = blockIdx.x, b = blockIdx.y;
   const int64_t start = p.cu[b];
   const int64_t len = (int64_t)p.cu[b + 1] - start;
-  if ((int64_t)page * BS >= len) return;
-  const int n = (int)min((int64_t)BS, len - (int64_t)page * BS);
-  uint32_t blk = p.block_tables[(int64_t)b * p.cols + page];
+  if ((int64_t)page * BS >= len) return false;
+  n = (int)min((int64_t)BS, len - (int64_t)page * BS);
+  tok0 = start + (int64_t)page * BS;
+  blk = p.block_tables[(int64_t)b * p.cols + page];
   if ((int64_t)blk >= p.num_blocks) {
     if (threadIdx.x == 0) raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
     blk = 0;
   }
-  const int H = p.num_kv_heads;
-  const int64_t tok0 = start + (int64_t)page * BS;
-  const int64_t page_bytes = (int64_t)D * BS * kES;
-  // K
-  for (int i = threadIdx.x; i < n * H * kCH; i += blockDim.x) {
-    const int c = i % kCH;
-    const int h = (i / kCH) % H;
-    const int t = i / (kCH * H);
-    const unsigned char *src = p.k_cache + ((int64_t)blk * H + h) * page_bytes + ((int64_t)c * BS + t) * 16;
-    unsigned char *dst = p.k_out + ((tok0 + t) * H + h) * (int64_t)D * kES + c * 16;
-    *reinterpret_cast<uint4 *>(dst) = __ldg(reinterpret_cast<const uint4 *>(src));
+  return true;
+}
+
+// V page chunk e (16 bytes at byte e * 16 of the [D][row_bytes] page) into
+// shared rows padded to row_bytes + 4 bytes (one 32-bit word each).
+template <int kRowBytes>
+__device__ __forceinline__ void stage_v_chunk(unsigned char *vsm, int e, const uint4 &v) {
+  constexpr int kPad = kRowBytes + 4;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int off = e * 16 + 4 * i;
+    *reinterpret_cast<uint32_t *>(vsm + (off / kRowBytes) * kPad + off % kRowBytes) = w[i];
   }
-  // V, one head at a time through shared memory
-  for (int h = 0; h < H; ++h) {
-    const uint32_t *src = reinterpret_cast<const uint32_t *>(p.v_cache + ((int64_t)blk * H + h) * page_bytes);
-    for (int w = threadIdx.x; w < D * BS * kES / 4; w += blockDim.x) {
-      const int d = w / (BS * kES / 4);
-      const int r = w - d * (BS * kES / 4);
-      vsm[d * kRowWords + r] = __ldg(src + w);
+}
+
+template <typename T, int BS, int D>
+__global__ void __launch_bounds__(gather_threads(D * BS * (int)sizeof(T) / 16))
+    gather_kernel(const GatherParams p) {
+  constexpr int kES = (int)sizeof(T);
+  constexpr int kVE = 16 / kES;                 // elements per 16-byte vector
+  constexpr int kChunks = D * BS * kES / 16;    // 16-byte chunks of one head's K (or V) page
+  constexpr int kThreads = gather_threads(kChunks);
+  constexpr int kPer = kChunks / kThreads;
+  static_assert(kChunks % kThreads == 0, "whole chunks per thread");
+  constexpr int kRowBytes = BS * kES;           // one V row: one dim over the page's tokens
+  constexpr int kPad = kRowBytes + 4;
+  __shared__ __align__(16) unsigned char vsm[D * kPad];
+  int n;
+  int64_t tok0;
+  uint32_t blk;
+  if (!gather_page(p, BS, n, tok0, blk)) return;
+  const int h = blockIdx.z, H = p.num_kv_heads;
+  const int64_t page = ((int64_t)blk * H + h) * (D * BS * kES);
+  const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_cache + page);
+  const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_cache + page);
+  uint4 kr[kPer], vr[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kThreads;  // K chunk e: dims (e / BS) * kVE.., token e % BS
+    if (e % BS < n) kr[i] = __ldg(ks + e);
+    vr[i] = __ldg(vs + e);
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) stage_v_chunk<kRowBytes>(vsm, threadIdx.x + i * kThreads, vr[i]);
+  const int64_t row = (int64_t)D * kES;  // bytes of one (token, head) output row
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kThreads;
+    const int t = e % BS;
+    if (t < n)
+      *reinterpret_cast<uint4 *>(p.k_out + ((tok0 + t) * H + h) * row + (e / BS) * 16) = kr[i];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int o = threadIdx.x + i * kThreads;  // output vector: token o % BS, dims (o / BS) * kVE..
+    const int t = o % BS, d0 = (o / BS) * kVE;
+    if (t >= n) continue;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (kES == 4) {
+        w[j] = *reinterpret_cast<const uint32_t *>(vsm + (d0 + j) * kPad + t * 4);
+      } else {
+        const uint32_t lo = *reinterpret_cast<const uint16_t *>(vsm + (d0 + 2 * j) * kPad + t * 2);
+        const uint32_t hi = *reinterpret_cast<const uint16_t *>(vsm + (d0 + 2 * j + 1) * kPad + t * 2);
+        w[j] = lo | (hi << 16);
+      }
     }
-    __syncthreads();
-    const unsigned char *vb = reinterpret_cast<const unsigned char *>(vsm);
-    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
-      const int d = i % D;
-      const int t = i / D;
-      const T v = *reinterpret_cast<const T *>(vb + d * kRowWords * 4 + t * kES);
-      reinterpret_cast<T *>(p.v_out)[((tok0 + t) * H + h) * (int64_t)D + d] = v;
-    }
-    __syncthreads();
+    *reinterpret_cast<uint4 *>(p.v_out + ((tok0 + t) * H + h) * row + d0 * kES) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -260,18 +308,19 @@ int launch_gather_t(const GatherArgs &a, cudaStream_t stream) {
   p.num_blocks = a.num_blocks;
   p.cols = a.max_num_blocks_per_seq;
   p.num_kv_heads = a.num_kv_heads;
-  const int smem = D * (BS * (int)sizeof(T) / 4 + 1) * 4;
-  dim3 grid((unsigned)a.max_num_blocks_per_seq, (unsigned)a.num_seqs);
-  gather_kernel<T, BS, D><<<grid, 256, smem, stream>>>(p);
+  if (a.num_kv_heads > 65535) return VASR_PA_EINVAL_SHAPE;
+  dim3 grid((unsigned)a.max_num_blocks_per_seq, (unsigned)a.num_seqs, (unsigned)a.num_kv_heads);
+  gather_kernel<T, BS, D><<<grid, gather_threads(D * BS * (int)sizeof(T) / 16), 0, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
 // ================================================ gather_kv_cache, fp8 pages
 // The fp8 form of the same gather: the call site passes k_scale / v_scale
 // and the model dtype as out_dtype, and the packed rows hold
-// float(stored byte) * scale rounded to that dtype. One CTA per (page,
-// sequence); K chunks of 16 bytes become 16 outputs, V pages [D][BS] are
-// transposed through shared memory.
+// float(stored byte) * scale rounded to that dtype. Same decomposition as
+// gather_kernel: one CTA per (page, sequence, kv head), all loads first; a
+// 16-byte K chunk (16 dims of one token) becomes 16 outputs, V rows [D][BS]
+// are transposed through shared memory.
 struct GatherFp8Params {
   GatherParams g;
   const float *k_scale;
@@ -299,56 +348,69 @@ __device__ __forceinline__ void store16_scaled(TO *dst, const float (&f)[16], fl
 }
 
 template <typename TO, int BS, int D>
-__global__ void __launch_bounds__(256) gather_fp8_kernel(const GatherFp8Params q) {
+__global__ void __launch_bounds__(gather_threads(2 * D * BS / 16))
+    gather_fp8_kernel(const GatherFp8Params q) {
   const GatherParams &p = q.g;
-  constexpr int kCH = D / 16;            // 16-byte chunks of a K row
-  constexpr int kRowWords = BS / 4 + 1;  // padded V row (BS bytes), in 32-bit words
-  extern __shared__ __align__(16) uint32_t vsm[];
-  const int page = blockIdx.x;
-  const int b = blockIdx.y;
-  const int64_t start = p.cu[b];
-  const int64_t len = (int64_t)p.cu[b + 1] - start;
-  if ((int64_t)page * BS >= len) return;
-  const int n = (int)min((int64_t)BS, len - (int64_t)page * BS);
-  uint32_t blk = p.block_tables[(int64_t)b * p.cols + page];
-  if ((int64_t)blk >= p.num_blocks) {
-    if (threadIdx.x == 0) raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
-    blk = 0;
+  constexpr int kChunks = D * BS / 16;           // 16-byte chunks of one head's K (or V) page
+  constexpr int kThreads = gather_threads(2 * kChunks);
+  constexpr int kPer = kChunks / kThreads < 1 ? 1 : kChunks / kThreads;
+  constexpr int kVE = 16 / (int)sizeof(TO);      // outputs per 16-byte vector
+  constexpr int kOut = D * BS / kVE;             // output V vectors of the page
+  constexpr int kOutPer = kOut / kThreads;
+  static_assert(kChunks % kThreads == 0 || kChunks < kThreads, "whole chunks per thread");
+  static_assert(kOut % kThreads == 0, "whole output vectors per thread");
+  constexpr int kPad = BS + 4;
+  __shared__ __align__(16) unsigned char vsm[D * kPad];
+  int n;
+  int64_t tok0;
+  uint32_t blk;
+  if (!gather_page(p, BS, n, tok0, blk)) return;
+  const int h = blockIdx.z, H = p.num_kv_heads;
+  const int64_t page = ((int64_t)blk * H + h) * (D * BS);
+  const uint4 *ks = reinterpret_cast<const uint4 *>(p.k_cache + page);
+  const uint4 *vs = reinterpret_cast<const uint4 *>(p.v_cache + page);
+  uint4 kr[kPer], vr[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kThreads;  // K chunk e: dims (e / BS) * 16.., token e % BS
+    if (e < kChunks) {
+      if (e % BS < n) kr[i] = __ldg(ks + e);
+      vr[i] = __ldg(vs + e);
+    }
   }
-  const float ks = __ldg(q.k_scale), vs = __ldg(q.v_scale);
-  const int H = p.num_kv_heads;
-  const int64_t tok0 = start + (int64_t)page * BS;
-  const int64_t page_bytes = (int64_t)D * BS;
+  const float kscale = __ldg(q.k_scale), vscale = __ldg(q.v_scale);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kThreads;
+    if (e < kChunks) stage_v_chunk<BS>(vsm, e, vr[i]);
+  }
   TO *k_out = reinterpret_cast<TO *>(p.k_out);
   TO *v_out = reinterpret_cast<TO *>(p.v_out);
-  // K
-  for (int i = threadIdx.x; i < n * H * kCH; i += blockDim.x) {
-    const int c = i % kCH;
-    const int h = (i / kCH) % H;
-    const int t = i / (kCH * H);
-    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(
-        p.k_cache + ((int64_t)blk * H + h) * page_bytes + ((int64_t)c * BS + t) * 16));
-    float f[16];
-    unpack16_fp8(raw, f);
-    store16_scaled<TO>(k_out + ((tok0 + t) * H + h) * (int64_t)D + c * 16, f, ks);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kThreads;
+    const int t = e % BS;
+    if (e < kChunks && t < n) {
+      float f[16];
+      unpack16_fp8(kr[i], f);
+      store16_scaled<TO>(k_out + ((tok0 + t) * H + h) * (int64_t)D + (e / BS) * 16, f, kscale);
+    }
   }
-  // V, one head at a time through shared memory
-  for (int h = 0; h < H; ++h) {
-    const uint32_t *src = reinterpret_cast<const uint32_t *>(p.v_cache + ((int64_t)blk * H + h) * page_bytes);
-    for (int w = threadIdx.x; w < D * BS / 4; w += blockDim.x) {
-      const int d = w / (BS / 4);
-      vsm[d * kRowWords + (w - d * (BS / 4))] = __ldg(src + w);
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kOutPer; ++i) {
+    const int o = threadIdx.x + i * kThreads;  // output vector: token o % BS, dims (o / BS) * kVE..
+    const int t = o % BS, d0 = (o / BS) * kVE;
+    if (t >= n) continue;
+    alignas(16) TO vals[kVE];
+#pragma unroll
+    for (int j = 0; j < kVE; ++j) {
+      __nv_fp8_e4m3 b8;
+      b8.__x = vsm[(d0 + j) * kPad + t];
+      vals[j] = Elem<TO>::from_f32(static_cast<float>(b8) * vscale);
     }
-    __syncthreads();
-    const unsigned char *vb = reinterpret_cast<const unsigned char *>(vsm);
-    for (int i = threadIdx.x; i < n * D; i += blockDim.x) {
-      const int d = i % D;
-      const int t = i / D;
-      __nv_fp8_e4m3 e;
-      e.__x = vb[d * kRowWords * 4 + t];
-      v_out[((tok0 + t) * H + h) * (int64_t)D + d] = Elem<TO>::from_f32(static_cast<float>(e) * vs);
-    }
-    __syncthreads();
+    *reinterpret_cast<uint4 *>(v_out + ((tok0 + t) * H + h) * (int64_t)D + d0) =
+        *reinterpret_cast<const uint4 *>(vals);
   }
 }
 
@@ -366,9 +428,9 @@ int launch_gather_fp8_t(const GatherArgs &a, cudaStream_t stream) {
   q.g.num_kv_heads = a.num_kv_heads;
   q.k_scale = a.k_scale;
   q.v_scale = a.v_scale;
-  const int smem = D * (BS / 4 + 1) * 4;
-  dim3 grid((unsigned)a.max_num_blocks_per_seq, (unsigned)a.num_seqs);
-  gather_fp8_kernel<TO, BS, D><<<grid, 256, smem, stream>>>(q);
+  if (a.num_kv_heads > 65535) return VASR_PA_EINVAL_SHAPE;
+  dim3 grid((unsigned)a.max_num_blocks_per_seq, (unsigned)a.num_seqs, (unsigned)a.num_kv_heads);
+  gather_fp8_kernel<TO, BS, D><<<grid, gather_threads(2 * D * BS / 16), 0, stream>>>(q);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 

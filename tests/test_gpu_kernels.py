@@ -10,8 +10,8 @@ import pytest
 import torch
 
 import paged_ref as ref
-from cases import (CONFIG1_CACHED, appended, config1_case, loguniform_lens, make_decode_case, oracle_decode,
-                   uniform_lens)
+from cases import (CONFIG1_CACHED, appended, config1_case, disjoint_block_tables, loguniform_lens,
+                   make_decode_case, oracle_decode, uniform_lens)
 from vasr_paged_attn import _lib
 from vasr_paged_attn import mistralrs_paged_attn as pa
 
@@ -327,6 +327,28 @@ def test_gather_kv_cache_bitexact(cuda_device, dtype):
     k, v = pa.gather_kv_cache(t["kc"], t["vc"], None, None, t["bt"],
                               torch.from_numpy(cu.astype(np.int32)).to(cuda_device))
     kr, vr = ref.gather_kv_cache(case.key_cache, case.value_cache, case.block_tables, cu, 8, 128, 16)
+    assert np.array_equal(to_bits(k), kr) and np.array_equal(to_bits(v), vr)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("bs,d", [(8, 128), (32, 128), (16, 64), (32, 256)])
+def test_gather_kv_cache_page_sizes_bitexact(cuda_device, dtype, bs, d):
+    """Every page size and head dim the gather serves, with partial last pages."""
+    rng = np.random.default_rng(bs * 1000 + d)
+    hkv = 4
+    lens = np.array([1, bs - 1, bs, bs + 1, 3 * bs + 5], np.int64)
+    blocks = [-(-int(n) // bs) for n in lens]
+    nb = sum(blocks) + 2
+    tables = disjoint_block_tables(rng, blocks, nb)
+    word = np.uint32 if dtype == "f32" else np.uint16
+    x = 16 // np.dtype(word).itemsize
+    kc = rng.integers(0, np.iinfo(word).max, size=(nb, hkv, d // x, bs, x), dtype=word)
+    vc = rng.integers(0, np.iinfo(word).max, size=(nb, hkv, d, bs), dtype=word)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    k, v = pa.gather_kv_cache(to_dev(kc, dtype, cuda_device), to_dev(vc, dtype, cuda_device), None, None,
+                              torch.from_numpy(tables.astype(np.int32)).to(cuda_device),
+                              torch.from_numpy(cu.astype(np.int32)).to(cuda_device))
+    kr, vr = ref.gather_kv_cache(kc, vc, np.ascontiguousarray(tables), cu, hkv, d, bs)
     assert np.array_equal(to_bits(k), kr) and np.array_equal(to_bits(v), vr)
 
 
