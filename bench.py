@@ -299,7 +299,9 @@ def run_ours(args):
     batch = len(lens0)
     model = eng.RandomQwen3Decoder(cfg, dev, torch.bfloat16, seed=args.seed)
     k_steps, w_steps = args.steps, max(3, args.warmup)
-    total_steps = 3 * (w_steps + k_steps) + 2  # device-resident, e2e and device-loop runs
+    # the device-resident, e2e and device-loop runs each replay steps 0 .. W + K - 1
+    # (same positions, same contexts), so their rates compare like for like
+    total_steps = w_steps + k_steps + 2
     need_tok = lens0 + total_steps
     blocks = np.array([-(-int(n) // BLOCK_SIZE) for n in need_tok])
     nb = int(blocks.sum()) + 1
@@ -420,6 +422,7 @@ def run_ours(args):
         build(s + 1, sets[(s + 1) % 2])  # overlaps the GPU step
         stream.synchronize()
 
+    s_idx = 0
     build(s_idx, sets[s_idx % 2])
     for _ in range(w_steps):
         e2e_step(s_idx)
@@ -442,7 +445,7 @@ def run_ours(args):
     # ---- device decode loop: prepare -> forward -> argmax replayed with no host round trip
     from vasr_paged_attn import decode_loop as dloop
     loop_state = dloop.DecodeLoopState(
-        [int(x) + s_idx for x in lens0], [0] * batch, [cfg.vocab_size],  # EOS id outside the vocab:
+        [int(x) for x in lens0], [0] * batch, [cfg.vocab_size],  # EOS id outside the vocab:
         torch.from_numpy(tables).to(dev), blocks.tolist(), BLOCK_SIZE, nb,  # every row stays active
         cfg.vocab_size, device=dev)
     loop = eng.DecodeLoopGraph(model, caches, loop_state, BLOCK_SIZE)
@@ -464,11 +467,10 @@ def run_ours(args):
     barrier()
     fin, gen_counts, _ = loop_state.read_back()
     loop_value = global_batch * k_steps / (loop_ms / 1e3)
-    s_idx += w_steps + k_steps
     loop.release()
 
     # ---- roofline of the paged decode kernel: one launch per layer, events on its stream
-    last = s_idx - 1
+    last = w_steps + k_steps - 1  # contexts of the last timed step
     ctx_last = torch.from_numpy(ctx[min(last, total_steps - 1)]).to(dev)
     q = torch.randn(batch, cfg.num_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
     out = torch.empty_like(q)

@@ -440,8 +440,10 @@ int launch_gather_fp8_t(const GatherArgs &a, cudaStream_t stream) {
 // b * cols + i of the pool, holding the page's K and V as T(byte * scale) in
 // the 16-bit page layouts (K [D/8][BS][8], V [D][BS]); the remapped table is
 // written too. One CTA per (table entry, kv head).
+constexpr int kDequantThreads = 128;
+
 template <typename TO, int BS, int D>
-__global__ void __launch_bounds__(128) dequant_pages_kernel(
+__global__ void __launch_bounds__(kDequantThreads) dequant_pages_kernel(
     const unsigned char *k_cache, const unsigned char *v_cache, const uint32_t *block_tables,
     const uint32_t *context_lens, int cols, int num_kv_heads, int64_t num_blocks,
     const float *k_scale, const float *v_scale, TO *k_out, TO *v_out, uint32_t *table_out) {
@@ -458,46 +460,51 @@ __global__ void __launch_bounds__(128) dequant_pages_kernel(
   const float ks = __ldg(k_scale), vs = __ldg(v_scale);
   const int64_t src_page = ((int64_t)blk * num_kv_heads + h) * D * BS;  // bytes
   const int64_t dst_page = (dst * num_kv_heads + h) * D * BS;           // elements
-  // K: fp8 chunk c (16 dims) of token t -> 16-bit chunks 2c, 2c + 1 of token t
-  for (int e = threadIdx.x; e < (D / 16) * BS; e += blockDim.x) {
-    const int c = e / BS, t = e % BS;
-    float f[16];
-    unpack16_fp8(__ldg(reinterpret_cast<const uint4 *>(k_cache + src_page + (int64_t)e * 16)), f);
+  // K chunk e = fp8 dims 16c.. of token t (c = e / BS, t = e % BS) -> 16-bit
+  // chunks 2c, 2c + 1 of token t; V chunk e = 16 bytes of the [D][BS] rows ->
+  // 16 elements at the same place. Both loads of every chunk a thread owns
+  // are issued before any store.
+  constexpr int kChunks = D * BS / 16;  // per page, for K and for V alike
+  constexpr int kPer = (kChunks + kDequantThreads - 1) / kDequantThreads;
+  uint4 kr[kPer], vr[kPer];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t w[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const TO lo = Elem<TO>::from_f32(f[8 * half + 2 * j] * ks);
-        const TO hi = Elem<TO>::from_f32(f[8 * half + 2 * j + 1] * ks);
-        w[j] = (uint32_t)(*reinterpret_cast<const uint16_t *>(&lo)) |
-               ((uint32_t)(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
-      }
-      *reinterpret_cast<uint4 *>(k_out + dst_page + ((int64_t)(2 * c + half) * BS + t) * 8) =
-          make_uint4(w[0], w[1], w[2], w[3]);
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kDequantThreads;
+    if (e < kChunks) {
+      kr[i] = __ldg(reinterpret_cast<const uint4 *>(k_cache + src_page + (int64_t)e * 16));
+      vr[i] = __ldg(reinterpret_cast<const uint4 *>(v_cache + src_page + (int64_t)e * 16));
     }
   }
-  // V: same [D][BS] order, 16 bytes -> 16 elements
-  for (int e = threadIdx.x; e < D * BS / 16; e += blockDim.x) {
-    float f[16];
-    unpack16_fp8(__ldg(reinterpret_cast<const uint4 *>(v_cache + src_page + (int64_t)e * 16)), f);
-    uint32_t w[8];
+  auto pack = [](const float *f, float scale) {
+    uint32_t w[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const TO lo = Elem<TO>::from_f32(f[2 * j] * vs), hi = Elem<TO>::from_f32(f[2 * j + 1] * vs);
+    for (int j = 0; j < 4; ++j) {
+      const TO lo = Elem<TO>::from_f32(f[2 * j] * scale), hi = Elem<TO>::from_f32(f[2 * j + 1] * scale);
       w[j] = (uint32_t)(*reinterpret_cast<const uint16_t *>(&lo)) |
              ((uint32_t)(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
     }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  };
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = threadIdx.x + i * kDequantThreads;
+    if (e >= kChunks) continue;
+    const int c = e / BS, t = e % BS;
+    float f[16];
+    unpack16_fp8(kr[i], f);
+    *reinterpret_cast<uint4 *>(k_out + dst_page + ((int64_t)(2 * c) * BS + t) * 8) = pack(f, ks);
+    *reinterpret_cast<uint4 *>(k_out + dst_page + ((int64_t)(2 * c + 1) * BS + t) * 8) = pack(f + 8, ks);
+    unpack16_fp8(vr[i], f);
     uint4 *d4 = reinterpret_cast<uint4 *>(v_out + dst_page + (int64_t)e * 16);
-    d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    d4[0] = pack(f, vs);
+    d4[1] = pack(f + 8, vs);
   }
 }
 
 template <typename TO, int BS>
 int launch_dequant_t(const DequantArgs &a, cudaStream_t s) {
   dim3 grid((unsigned)a.cols, (unsigned)a.num_seqs, (unsigned)a.num_kv_heads);
-  dequant_pages_kernel<TO, BS, 128><<<grid, 128, 0, s>>>(
+  dequant_pages_kernel<TO, BS, 128><<<grid, kDequantThreads, 0, s>>>(
       static_cast<const unsigned char *>(a.key_cache), static_cast<const unsigned char *>(a.value_cache),
       a.block_tables, a.context_lens, a.cols, a.num_kv_heads, a.num_blocks, a.k_scale, a.v_scale,
       static_cast<TO *>(a.key_out), static_cast<TO *>(a.value_out), a.table_out);
