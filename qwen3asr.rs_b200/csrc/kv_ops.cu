@@ -29,7 +29,6 @@ namespace {
 constexpr int kAppendThreads = 256;
 constexpr int kAppendMaxTokens = 16;
 constexpr int kAppendRowBytes = 2048;                 // bytes of heads per tile row
-constexpr int kAppendRowPitch = kAppendRowBytes + 16;  // +16 B: conflict-free columns
 
 struct AppendParams {
   const unsigned char *key;
@@ -604,6 +603,7 @@ struct AppendFp8Params {
   int num_kv_heads;
   int tile_tokens;
   int heads_per_tile;
+  int row_pitch;  // bytes of one staged token row (one byte per element) + 16
 };
 
 // 16 source elements at src (16-byte aligned) -> 16 E4M3 bytes of x / scale.
@@ -634,9 +634,10 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
   constexpr int kTPS = BS < 16 ? BS : 16;     // tokens per vector V store
   constexpr int kES = (int)sizeof(T);
   extern __shared__ __align__(16) unsigned char sm[];
+  const int pitch = p.row_pitch;
   unsigned char *kt = sm;
-  unsigned char *vt = sm + kAppendMaxTokens * kAppendRowPitch;
-  int64_t *s_slot = reinterpret_cast<int64_t *>(vt + kAppendMaxTokens * kAppendRowPitch);
+  unsigned char *vt = sm + p.tile_tokens * pitch;
+  int64_t *s_slot = reinterpret_cast<int64_t *>(vt + p.tile_tokens * pitch);
   int *s_run_start = reinterpret_cast<int *>(s_slot + kAppendMaxTokens);
   int *s_run_len = s_run_start + kAppendMaxTokens;
   int *s_nruns = s_run_len + kAppendMaxTokens;
@@ -664,9 +665,9 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
     const int tt = i / row_chunks;
     const int r = i - tt * row_chunks;
     const int64_t col = ((int64_t)h0 * D + (int64_t)r * 16) * kES;
-    *reinterpret_cast<uint4 *>(kt + tt * kAppendRowPitch + r * 16) =
+    *reinterpret_cast<uint4 *>(kt + tt * pitch + r * 16) =
         quantize16<T>(p.key + (t0 + tt) * p.k_stride_bytes + col, ks);
-    *reinterpret_cast<uint4 *>(vt + tt * kAppendRowPitch + r * 16) =
+    *reinterpret_cast<uint4 *>(vt + tt * pitch + r * 16) =
         quantize16<T>(p.value + (t0 + tt) * p.v_stride_bytes + col, vs);
   }
   __syncthreads();
@@ -702,7 +703,7 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
     const int off = (int)(s - blk * BS);
     const int64_t dst = ((((blk * p.num_kv_heads + h0 + hc) * kCH + c) * BS) + off) * 16;
     *reinterpret_cast<uint4 *>(p.k_cache + dst) =
-        *reinterpret_cast<const uint4 *>(kt + tt * kAppendRowPitch + r * 16);
+        *reinterpret_cast<const uint4 *>(kt + tt * pitch + r * 16);
   }
   __syncthreads();
   // V: (head, dim, run) with run fastest
@@ -718,21 +719,21 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
     const int64_t s = s_slot[tt0];
     const int64_t blk = s / BS;
     const int off = (int)(s - blk * BS);
-    const unsigned char *src = vt + tt0 * kAppendRowPitch + hc * D + d;
+    const unsigned char *src = vt + tt0 * pitch + hc * D + d;
     unsigned char *dst = p.v_cache + ((blk * p.num_kv_heads + h0 + hc) * D + d) * BS + off;
     if (len == kTPS && (off % kTPS) == 0) {
       uint32_t w[kTPS / 4];
 #pragma unroll
       for (int q = 0; q < kTPS / 4; ++q)
-        w[q] = (uint32_t)src[(4 * q) * kAppendRowPitch] | ((uint32_t)src[(4 * q + 1) * kAppendRowPitch] << 8) |
-               ((uint32_t)src[(4 * q + 2) * kAppendRowPitch] << 16) |
-               ((uint32_t)src[(4 * q + 3) * kAppendRowPitch] << 24);
+        w[q] = (uint32_t)src[(4 * q) * pitch] | ((uint32_t)src[(4 * q + 1) * pitch] << 8) |
+               ((uint32_t)src[(4 * q + 2) * pitch] << 16) |
+               ((uint32_t)src[(4 * q + 3) * pitch] << 24);
       if constexpr (kTPS == 16)
         *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
       else
         *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
     } else {
-      for (int e = 0; e < len; ++e) dst[e] = src[e * kAppendRowPitch];
+      for (int e = 0; e < len; ++e) dst[e] = src[e * pitch];
     }
   }
 }
@@ -793,10 +794,13 @@ int launch_append_fp8_t(const AppendArgs &a, cudaStream_t stream) {
   const int tt = a.num_tokens >= 4096 ? 16 : 8;  // prefill-sized: 8 / 16-token tiles
   p.tile_tokens = tt;
   p.heads_per_tile = kAppendRowBytes / D;  // one byte per staged element
-  const int smem = 2 * kAppendMaxTokens * kAppendRowPitch + kAppendMaxTokens * 8 +
-                   (2 * kAppendMaxTokens + 1) * 4;
+  // staged rows hold the tile's heads only; shared memory sized to the tile
+  p.row_pitch = (a.num_kv_heads < p.heads_per_tile ? a.num_kv_heads : p.heads_per_tile) * D + 16;
+  constexpr int kTail = kAppendMaxTokens * 8 + (2 * kAppendMaxTokens + 1) * 4;
+  const int smem = 2 * tt * p.row_pitch + kTail;
+  constexpr int kSmemMax = 2 * kAppendMaxTokens * (kAppendRowBytes + 16) + kTail;
   static std::atomic<uint64_t> attr_done{0};
-  if (!ensure_smem_attr(kv_append_fp8_kernel<T, BS, D>, smem, attr_done)) return VASR_PA_ELAUNCH;
+  if (!ensure_smem_attr(kv_append_fp8_kernel<T, BS, D>, kSmemMax, attr_done)) return VASR_PA_ELAUNCH;
   const int64_t tiles = (a.num_tokens + tt - 1) / tt;
   if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
   dim3 grid((unsigned)tiles, (unsigned)((a.num_kv_heads + p.heads_per_tile - 1) / p.heads_per_tile));
