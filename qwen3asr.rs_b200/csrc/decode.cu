@@ -17,6 +17,14 @@
 #ifndef VASR_G2_MINB
 #define VASR_G2_MINB 3
 #endif
+// Launch shape of the tensor-core kernel over fp8 pages (stages per CTA,
+// resident CTAs per SM)
+#ifndef VASR_G2_NST_FP8
+#define VASR_G2_NST_FP8 8
+#endif
+#ifndef VASR_G2_MINB_FP8
+#define VASR_G2_MINB_FP8 4
+#endif
 // GQA-2 bf16 / f16 pages: tensor-core score and P.V tiles (decode_mma.cuh)
 #ifndef VASR_DECODE_MMA
 #define VASR_DECODE_MMA 1
@@ -115,7 +123,13 @@ template <typename T, int BS, int D, typename TC = T>
 int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
   constexpr int kStageBytes = 2 * ((16 > BS) ? 16 / BS : 1) * D * BS * (int)sizeof(TC);
   // same bytes in flight per CTA for any page size: twice the stages for 4 KB stages
-  constexpr int kNST = kStageBytes <= 4096 ? 2 * VASR_G2_NST : kStageBytes <= 8192 ? VASR_G2_NST : 4;
+  constexpr bool kFp8Pages = std::is_same<TC, __nv_fp8_e4m3>::value;
+  // fp8: the tuned stage count for 4 KB stages, half of it (a multiple of the
+  // 4 warps) for the 8 KB stages of 32-token pages
+  constexpr int kNST = kFp8Pages ? (kStageBytes <= 4096 ? VASR_G2_NST_FP8
+                                    : ((VASR_G2_NST_FP8 / 2) / 4 * 4 < 4 ? 4 : (VASR_G2_NST_FP8 / 2) / 4 * 4))
+                       : kStageBytes <= 4096 ? 2 * VASR_G2_NST : kStageBytes <= 8192 ? VASR_G2_NST : 4;
+  constexpr int kMinB = kFp8Pages ? VASR_G2_MINB_FP8 : VASR_G2_MINB;
   using C = DecodeG2Cfg<TC, BS, D, kNST>;
   DecodeWorkspace w;
   const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
@@ -124,7 +138,7 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
   constexpr bool kMma = VASR_DECODE_MMA && !std::is_same<T, float>::value &&
                         (std::is_same<T, TC>::value || BS >= 16);
   if constexpr (kMma) {
-    auto kern = paged_decode_mma_kernel<T, BS, D, kNST, VASR_G2_MINB, TC>;
+    auto kern = paged_decode_mma_kernel<T, BS, D, kNST, kMinB, TC>;
     static std::atomic<uint64_t> attr_done{0};
     if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
     dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
@@ -144,7 +158,7 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
     kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
-  auto kern = paged_decode_g2_kernel<T, BS, D, kNST, VASR_G2_MINB, TC>;
+  auto kern = paged_decode_g2_kernel<T, BS, D, kNST, kMinB, TC>;
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
   dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
