@@ -11,8 +11,9 @@
  *  - Plain pointers and sizes only. Every tensor pointer is a device address
  *    (or, for swap, a device-accessible pinned host address) that the caller
  *    owns. No entry point allocates, frees or synchronises; all work is
- *    enqueued on `stream` (NULL = legacy default stream), so every call is
- *    safe inside CUDA stream capture.
+ *    enqueued on `stream` (NULL = legacy default stream). Every call except
+ *    vasr_pa_paged_attention_noalloc (see its own notes) is safe inside CUDA
+ *    stream capture.
  *  - Cache layout is the vLLM layout the reference allocates in
  *    vasr-paged-attn/src/paged_kv_cache.rs:285-294:
  *        key_cache   [num_blocks, num_kv_heads, head_dim / x, block_size, x]
