@@ -623,6 +623,13 @@ def run_kernel_bench(args):
             out.append((kc, vc))
         return out
 
+    l2_bytes = 126 * 2**20
+
+    def sets_for(bytes_per_set, cap=16):
+        """Independent input sets the timed launches cycle through: together at least
+        4x the 126 MB L2, so no launch finds the previous launches' data in L2."""
+        return max(1, min(cap, -(-4 * l2_bytes // max(1, int(bytes_per_set)))))
+
     def tables_for(lens, nb, cols=None):
         blocks = [-(-int(n) // bs) for n in lens]
         perm = rng.permutation(np.arange(1, nb))
@@ -704,25 +711,34 @@ def run_kernel_bench(args):
     elif k == "append":
         for name, ntok, per_seq in (("config2_decode", 64, 1), ("config3_chunk", 32 * 256, 256)):
             nb = ntok // per_seq * (-(-per_seq // bs)) + 16 + 1
-            kc, vc = pool(nb, 1)[0]
-            kv = torch.randn(ntok, hkv, d, device=dev).to(torch.bfloat16)
+            nset = sets_for(2 * ntok * hkv * d * 2 + nb * hkv * d * bs * 2 * 2)
+            pools = pool(nb, nset)
+            ks = [torch.randn(ntok, hkv, d, device=dev).to(torch.bfloat16) for _ in range(nset)]
+            vs = [torch.randn(ntok, hkv, d, device=dev).to(torch.bfloat16) for _ in range(nset)]
             nseq = ntok // per_seq
             t = tables_for([per_seq] * nseq, nb)
             pos = np.arange(per_seq)
             slots = np.concatenate([t[i, pos // bs].astype(np.int64) * bs + pos % bs for i in range(nseq)])
             sl = torch.from_numpy(slots).to(dev)
-            ms = _events_time(lambda i: pa.reshape_and_cache(kv, kv, None, None, kc, vc, sl), args.iters)
+            ms = _events_time(lambda i: pa.reshape_and_cache(ks[i % nset], vs[i % nset], None, None,
+                                                             pools[i % nset][0], pools[i % nset][1], sl), args.iters)
             alg = ntok * hkv * d * 2 * 2 * 2
             lines.append({"kernel": "kv_append", "config": name, "tokens": ntok, "us": ms * 1e3,
-                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
+                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak,
+                          "input_sets_cycled": nset})
             # the same tokens into fp8 (E4M3) pages: bf16 read, one byte per element written
-            kc8 = torch.zeros(nb, hkv, d // 16, bs, 16, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
-            vc8 = torch.zeros(nb, hkv, d, bs, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+            del pools
+            p8 = [(torch.zeros(nb, hkv, d // 16, bs, 16, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn),
+                   torch.zeros(nb, hkv, d, bs, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn))
+                  for _ in range(nset)]
             sk = torch.tensor([0.05], device=dev)
-            ms = _events_time(lambda i: pa.reshape_and_cache(kv, kv, sk, sk, kc8, vc8, sl), args.iters)
+            ms = _events_time(lambda i: pa.reshape_and_cache(ks[i % nset], vs[i % nset], sk, sk, p8[i % nset][0],
+                                                             p8[i % nset][1], sl), args.iters)
             alg = ntok * hkv * d * 2 * (2 + 1)
             lines.append({"kernel": "kv_append_fp8", "config": name, "tokens": ntok, "us": ms * 1e3,
-                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
+                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak,
+                          "input_sets_cycled": nset})
+            del p8, ks, vs
     elif k == "gather":
         # gather_kv_cache of config 3's full prompts (32 x U[100, 800] tokens) from bf16 and fp8 pages
         from vasr_paged_attn.workloads import config3_rounds
@@ -733,32 +749,39 @@ def run_kernel_bench(args):
         t = torch.from_numpy(tables_for(lens, nb)).to(dev)
         cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).to(dev)
         total = int(lens.sum())
-        kc, vc = pool(nb, 1)[0]
-        ms = _events_time(lambda i: pa.gather_kv_cache(kc, vc, None, None, t, cu, None, total), args.iters)
+        nset = sets_for(nb * hkv * d * bs * 2 * 2 + total * hkv * d * 2 * 2)
+        pools = pool(nb, nset)
+        ms = _events_time(lambda i: pa.gather_kv_cache(pools[i % nset][0], pools[i % nset][1], None, None, t, cu,
+                                                       None, total), args.iters)
         alg = total * hkv * d * 2 * 2 * 2
         lines.append({"kernel": "gather_kv_cache", "config": "config3 prompts, bf16 pages", "tokens": total,
                       "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
-                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
-        kc8 = (torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn)
-        vc8 = (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)
+                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "input_sets_cycled": nset})
+        del pools
+        nset = sets_for(nb * hkv * d * bs * 2 + total * hkv * d * 2 * 2)
+        p8 = [((torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn),
+               (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)) for _ in range(nset)]
         sk = torch.tensor([0.125], device=dev)
-        ms = _events_time(lambda i: pa.gather_kv_cache(kc8, vc8, sk, sk, t, cu, torch.bfloat16, total),
-                          args.iters)
+        ms = _events_time(lambda i: pa.gather_kv_cache(p8[i % nset][0], p8[i % nset][1], sk, sk, t, cu,
+                                                       torch.bfloat16, total), args.iters)
         alg = total * hkv * d * 2 * (1 + 2)
         lines.append({"kernel": "gather_kv_cache_fp8", "config": "config3 prompts, fp8 pages -> bf16",
                       "tokens": total, "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
-                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak})
+                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "input_sets_cycled": nset})
     elif k in ("prefill", "prefill_fp8"):
         from vasr_paged_attn.workloads import config3_rounds
 
         lens, rounds = config3_rounds(args.seed)
         nb = sum(-(-int(n) // bs) for n in lens) + 1
-        kc, vc = pool(nb, 1)[0]
+        # page pools (one per layer) and query sets cycled so that the launches' inputs exceed L2
+        nset = sets_for(nb * hkv * d * bs * 2 * 2 + 2 * 32 * 256 * hq * d * 2, cap=8)
         sk = sv = None
         if k == "prefill_fp8":  # the same pages in E4M3 with per-tensor scales
-            kc = (torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn)
-            vc = (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)
+            pools = [((torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn),
+                      (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)) for _ in range(nset)]
             sk = sv = torch.tensor([0.125], device=dev)
+        else:
+            pools = pool(nb, nset)
         t_all = tables_for(lens, nb)
         total_flops, total_ms = 0.0, 0.0
         for r in rounds:
@@ -766,12 +789,13 @@ def run_kernel_bench(args):
             chunk = np.array([n for (_, _, n) in r])
             ctx = np.array([s + n for (_, s, n) in r])
             cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
-            q = torch.randn(int(chunk.sum()), hq, d, device=dev).to(torch.bfloat16)
+            qs = [torch.randn(int(chunk.sum()), hq, d, device=dev).to(torch.bfloat16) for _ in range(nset)]
             bt = torch.from_numpy(t_all[idx]).to(dev)
             dctx = torch.from_numpy(ctx.astype(np.int32)).to(dev)
             dcu = torch.from_numpy(cu).to(dev)
             mq = int(chunk.max())
-            ms = _events_time(lambda i: pa.paged_attention_varlen_prefill(q, kc, vc, bt, dctx, dcu, sk, sv,
+            ms = _events_time(lambda i: pa.paged_attention_varlen_prefill(qs[i % nset], pools[i % nset][0],
+                                                                          pools[i % nset][1], bt, dctx, dcu, sk, sv,
                                                                           d ** -0.5, 1.0, mq), args.iters)
             vis = sum(sum(int(s) + j + 1 for j in range(int(n))) for (_, s, n) in r)
             total_flops += 4.0 * d * hq * vis
@@ -782,6 +806,7 @@ def run_kernel_bench(args):
         lines.append({"kernel": "paged_prefill_varlen" + ("_fp8" if k == "prefill_fp8" else ""),
                       "config": "config3 (one layer, all chunk rounds)",
                       "rounds": len(rounds), "us_per_layer": total_ms * 1e3, "flops_per_layer": total_flops,
+                      "input_sets_cycled": nset,
                       "TFLOP/s": tflops, "frac_of_bf16_peak": tflops / tpeak,
                       "tflops_28_layers": total_flops * 28 / 1e12})
     elif k == "copy":
