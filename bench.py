@@ -1,37 +1,43 @@
 #!/usr/bin/env python
-"""Benchmark of the paged KV-cache decode path on B200.
+"""Benchmark of the paged KV-cache decode path on B200 (BASELINE.json config 5 by default).
 
-One *step* = one full 28-layer decode step of a Qwen3-ASR-0.6B-shaped decoder
-(random-init bf16 weights) for 64 sequences with seeded context lengths
-~U[200, 1500]: per layer one ``reshape_and_cache`` + one ``paged_attention``
-through the sm_100a kernels, the rest (GEMMs, norms, RoPE, lm_head, argmax)
-through torch; the step is a captured CUDA graph replayed per token, as in
-the reference (vasr-paged-attn/src/cuda_graph.rs).
+One *step* = one full 28-layer decode step of a random-init bf16 Qwen3-ASR
+text decoder: per layer one fused q/k RMSNorm + RoPE + KV append and one
+``paged_attention`` through the sm_100a kernels, the rest (GEMMs, norms,
+lm_head, argmax) through torch; the step is a captured CUDA graph replayed
+per token, as in the reference (vasr-paged-attn/src/cuda_graph.rs).
+
+Default workload = config 5: the 1.7B-shaped decoder (hidden 2048, MLP 6144)
+and 512 sequences with contexts ~log-U[64, 4096], split over the ranks by
+expected KV bytes (strong scaling: the 512 sequences are the whole job at
+every N, one process per GPU, no collective on the hot path).
 
   value      tokens/s over all ranks, metadata already resident in HBM
              (per step: device-side copy of that step's metadata into the
-             graph buffers + replay).
+             graph buffers + replay); device time, max over ranks.
   e2e        tokens/s through the engine's host-facing call: per step the
              host builds the step metadata, copies it from pinned memory,
              replays, and reads the next token ids back (synchronising);
              the host builds step s + 1's metadata (double-buffered pinned
              memory) while the GPU runs step s.
-  roofline   the paged decode kernel alone: algorithmic KV bytes per launch
-             / CUDA-event launch time vs the measured HBM copy bandwidth.
+  roofline   the paged decode kernel alone at the workload's shapes (rank 0):
+             algorithmic KV bytes per launch / CUDA-event launch time vs the
+             measured HBM copy bandwidth.
+  ranks      per rank: sequences, context tokens, decode-kernel us and GB/s
+             per launch, step ms and the share of the step outside the paged
+             decode kernel (the per-replica fixed cost: weights and glue).
   device_loop  tokens/s of the device-side decode loop: step prepare (token
              feedback, EOS state, metadata) + the 28 layers + greedy argmax
              captured as one graph and replayed back to back.
+  config2    the same step for config 2 (0.6B decoder, 64 sequences per GPU,
+             weak scaling) with its decode-kernel roofline.
+  prefill / append / decode_fp8 / copy_blocks / swap_blocks / gather_kv_cache
+             (one GPU only) each kernel on its BASELINE config, timed with
+             CUDA events over a captured graph of launches whose inputs
+             together exceed L2: us, achieved, peak, frac.
 
-Multi-GPU (torchrun): request-level data parallelism, each rank holds its own
-decoder replica and page pool and decodes its own 64 sequences (weak
-scaling, no collective on the hot path; one all-reduce of the elapsed time
-outside the timed region).
-
-``--config 5`` runs the same step for benchmark config 5 instead: a
-Qwen3-ASR-1.7B-shaped decoder (hidden 2048, MLP 6144) and 512 sequences with
-contexts ~log-U[64, 4096], split over the ranks by expected KV bytes (strong
-scaling: the 512 sequences are the whole job at every N), 64 timed steps.
-
+``--config 2`` makes config 2 the headline workload instead.
+``--kernel NAME`` prints only that kernel microbenchmark.
 ``--impl reference`` times the reference's CPU attention path (the C
 restatement in oracle/, all host threads) on the same contexts.
 """
@@ -56,30 +62,32 @@ METRIC = "decode tok/s & paged-attn KV-read GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 BATCH = 64
 CTX_LO, CTX_HI = 200, 1500
 BLOCK_SIZE = 16
+KERNELS = ["decode", "decode5", "decode_fp8", "append", "gather", "prefill", "prefill_fp8",
+           "copy", "swap", "config1"]
 
 
-def parse_args():
+def parse_args(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=None,
-                   help="timed steps (default 100 for config 2, 64 for config 5)")
+                   help="timed steps (default 64 for config 5, 100 for config 2)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the bounded cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the config-2 step and the per-kernel microbenchmarks of the JSON line")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--config", type=int, choices=[2, 5], default=2,
-                   help="decode-step workload: 2 = 0.6B decoder, 64 sequences per GPU (weak scaling); "
-                        "5 = 1.7B decoder, 512 sequences sharded over the GPUs (strong scaling)")
-    p.add_argument("--kernel", default=None,
-                   choices=["decode", "decode5", "decode_fp8", "append", "gather", "prefill", "prefill_fp8",
-                            "copy", "swap", "config1"],
+    p.add_argument("--config", type=int, choices=[2, 5], default=5,
+                   help="decode-step workload: 5 = 1.7B decoder, 512 sequences sharded over the GPUs "
+                        "(strong scaling); 2 = 0.6B decoder, 64 sequences per GPU (weak scaling)")
+    p.add_argument("--kernel", default=None, choices=KERNELS,
                    help="microbenchmark one kernel on its BASELINE config instead of the decode step")
     p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
     p.add_argument("--layers", type=int, default=28,
                    help="distinct per-layer caches cycled through by --kernel decode/copy")
-    args = p.parse_args()
+    args = p.parse_args(argv)
     if args.steps is None:
         args.steps = 64 if args.config == 5 else 100
     return args
@@ -94,18 +102,30 @@ def dist_env():
 
 
 def context_lens(seed: int, rank: int):
+    """Config 2: 64 contexts ~U[200, 1500] per rank."""
     import numpy as np
 
     rng = np.random.default_rng(seed + 1000 * rank)
     return rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int64)
 
 
-def load_peaks():
+def _peaks_file():
     f = REPO / "MEASURED_PEAKS.json"
-    if f.exists():
-        d = json.loads(f.read_text())
+    return json.loads(f.read_text()) if f.exists() else None
+
+
+def load_peaks():
+    d = _peaks_file()
+    if d:
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def load_tensor_peak():
+    d = _peaks_file()
+    if d:
+        return float(d["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback (burst)"
 
 
 class ClockSampler:
@@ -250,7 +270,6 @@ def run_reference(args):
     ks = max(1, min(k, 3))
     if args.config == 5:
         # 64 of the 512 sequences per step, the step time scaled by the context sum
-        sys.path.insert(0, str(REPO / "qwen3asr.rs_b200"))
         from vasr_paged_attn.workloads import config5_context_lens
         lens_all = config5_context_lens(args.seed)
         sub = lens_all[:BATCH]
@@ -284,24 +303,55 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args):
+# ------------------------------------------------------- decode-step bench
+class Ranks:
+    """Barrier and max-over-ranks of the one-process-per-GPU job (identity at N = 1)."""
+
+    def __init__(self, world, dev):
+        self.world, self.dev = world, dev
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, row):
+        """Every rank's row of floats (all ranks call this at the same point)."""
+        if self.world == 1:
+            return [list(row)]
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor(row, dtype=torch.float64, device=self.dev)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        dist.all_gather(out, t)
+        return [o.cpu().tolist() for o in out]
+
+
+def decode_step_bench(which: int, args, dev, rank: int, world: int, ranks: Ranks, windows: list,
+                      steps: int, full: bool = True):
+    """Time the captured 28-layer decode step of config ``which`` (2 or 5) on this rank's
+    sequences. Every rank runs the same collective calls in the same order.
+
+    Returns a dict of whole-job rates (device-resident ``value``; with ``full``
+    also ``e2e`` and ``device_loop``), the decode kernel's launch time at this
+    rank's shapes and every rank's row of per-rank figures."""
     import numpy as np
     import torch
-    import torch.distributed as dist
 
     from vasr_paged_attn import engine as eng
+    from vasr_paged_attn import host
     from vasr_paged_attn import mistralrs_paged_attn as pa
 
-    rank, world, local = dist_env()
-    if not torch.cuda.is_available():
-        raise SystemExit("bench.py needs a CUDA device for --impl ours")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
-
-    if args.config == 5:
-        # 1.7B decoder; the 512 sequences are split over the ranks by expected KV bytes
+    if which == 5:
         from vasr_paged_attn.sharding import lpt_shard
         from vasr_paged_attn.workloads import config5_context_lens
         cfg = eng.DecoderConfig.qwen3_asr_1_7b()
@@ -314,7 +364,7 @@ def run_ours(args):
         global_batch = BATCH * world
     batch = len(lens0)
     model = eng.RandomQwen3Decoder(cfg, dev, torch.bfloat16, seed=args.seed)
-    k_steps, w_steps = args.steps, max(3, args.warmup)
+    k_steps, w_steps = steps, max(3, args.warmup)
     # the device-resident, e2e and device-loop runs each replay steps 0 .. W + K - 1
     # (same positions, same contexts), so their rates compare like for like
     total_steps = w_steps + k_steps + 2
@@ -324,7 +374,6 @@ def run_ours(args):
     rng = np.random.default_rng(args.seed + 7 + rank)
     perm = rng.permutation(np.arange(1, nb))
     raw_cols = int(blocks.max())
-    from vasr_paged_attn import host
     cols = host.bucket_block_table_cols(raw_cols, BLOCK_SIZE)
     tables = np.zeros((batch, cols), np.int32)
     off = 0
@@ -360,29 +409,14 @@ def run_ours(args):
             graph.block_tables.copy_(d_tables)
         graph.replay()
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     s_idx = 0
     for _ in range(w_steps):
         device_step(s_idx)
         s_idx += 1
     torch.cuda.synchronize()
-    barrier()
-    clocks = ClockSampler(local)
-    clocks.start()
-    clocks.wait_first()
-    windows = []  # host wall-clock spans of the timed regions, for the clock samples
+    ranks.barrier()
     torch.cuda.synchronize()
-    barrier()
+    ranks.barrier()
     w0 = time.time()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed_steps")  # lets ncu --nvtx-include select the timed launches
@@ -393,101 +427,109 @@ def run_ours(args):
     e1.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-    barrier()
-    dev_ms = max_over_ranks(e0.elapsed_time(e1))
+    ranks.barrier()
+    local_ms = e0.elapsed_time(e1)
+    dev_ms = ranks.max(local_ms)
     windows.append((w0, time.time()))
-    value = global_batch * k_steps / (dev_ms / 1e3)
+    res = {"cfg": cfg, "model": model, "lens": lens0, "cols": cols, "global_batch": global_batch,
+           "batch": batch, "k_steps": k_steps, "w_steps": w_steps, "dev_ms": dev_ms,
+           "value": global_batch * k_steps / (dev_ms / 1e3)}
 
-    # ---- e2e: host-built metadata, pinned H2D, replay, D2H of next ids. The
-    # pinned metadata is double-buffered so that the host builds step s + 1
-    # while the GPU runs step s; every step still copies its inputs H2D, reads
-    # its next ids D2H and synchronises before the next step starts.
-    meta_cache = host.metadata_cache(nb, cfg.num_kv_heads, cfg.head_dim, BLOCK_SIZE, "bf16")
+    if full:
+        # ---- e2e: host-built metadata, pinned H2D, replay, D2H of next ids. The
+        # pinned metadata is double-buffered so that the host builds step s + 1
+        # while the GPU runs step s; every step still copies its inputs H2D, reads
+        # its next ids D2H and synchronises before the next step starts.
+        meta_cache = host.metadata_cache(nb, cfg.num_kv_heads, cfg.head_dim, BLOCK_SIZE, "bf16")
 
-    def pinned_set():
-        return {"ids": torch.zeros(batch, dtype=torch.int64).pin_memory(),
-                "pos": torch.zeros(batch, dtype=torch.int64).pin_memory(),
-                "slots": torch.zeros(batch, dtype=torch.int64).pin_memory(),
-                "ctx": torch.zeros(batch, dtype=torch.int32).pin_memory(),
-                "tables": torch.zeros(batch, cols, dtype=torch.int32).pin_memory()}
+        def pinned_set():
+            return {"ids": torch.zeros(batch, dtype=torch.int64).pin_memory(),
+                    "pos": torch.zeros(batch, dtype=torch.int64).pin_memory(),
+                    "slots": torch.zeros(batch, dtype=torch.int64).pin_memory(),
+                    "ctx": torch.zeros(batch, dtype=torch.int32).pin_memory(),
+                    "tables": torch.zeros(batch, cols, dtype=torch.int32).pin_memory()}
 
-    sets = [pinned_set(), pinned_set()]
-    h_next = torch.zeros(batch, dtype=torch.int64).pin_memory()
-    prompt_lens = [int(x) for x in lens0]
-    table_rows = [list(map(int, r[:n])) for r, n in zip(tables, blocks)]
-    stream = torch.cuda.current_stream()
+        sets = [pinned_set(), pinned_set()]
+        h_next = torch.zeros(batch, dtype=torch.int64).pin_memory()
+        prompt_lens = [int(x) for x in lens0]
+        table_rows = [list(map(int, r[:n])) for r, n in zip(tables, blocks)]
+        stream = torch.cuda.current_stream()
 
-    def build(s, st):
-        # host metadata through the C++ mirror of decode_metadata_for_batch_step
-        meta = meta_cache.decode_metadata_for_batch_step(table_rows, prompt_lens, s, True)
-        st["slots"].numpy()[:] = meta.slot_mapping
-        st["ctx"].numpy()[:] = meta.context_lens
-        st["pos"].numpy()[:] = np.asarray(meta.context_lens, dtype=np.int64) - 1
-        st["tables"].numpy().reshape(-1)[:] = meta.block_tables_flat
+        def build(s, st):
+            # host metadata through the C++ mirror of decode_metadata_for_batch_step
+            meta = meta_cache.decode_metadata_for_batch_step(table_rows, prompt_lens, s, True)
+            st["slots"].numpy()[:] = meta.slot_mapping
+            st["ctx"].numpy()[:] = meta.context_lens
+            st["pos"].numpy()[:] = np.asarray(meta.context_lens, dtype=np.int64) - 1
+            st["tables"].numpy().reshape(-1)[:] = meta.block_tables_flat
 
-    def e2e_step(s):
-        st = sets[s % 2]
-        st["ids"].copy_(h_next)  # the previous step's tokens, read back by the host
-        graph.input_ids.copy_(st["ids"], non_blocking=True)
-        graph.positions.copy_(st["pos"], non_blocking=True)
-        graph.slot_mapping.copy_(st["slots"], non_blocking=True)
-        graph.context_lens.copy_(st["ctx"], non_blocking=True)
-        graph.block_tables.copy_(st["tables"], non_blocking=True)
-        graph.replay()
-        h_next.copy_(graph.next_ids, non_blocking=True)
-        build(s + 1, sets[(s + 1) % 2])  # overlaps the GPU step
-        stream.synchronize()
+        def e2e_step(s):
+            st = sets[s % 2]
+            st["ids"].copy_(h_next)  # the previous step's tokens, read back by the host
+            graph.input_ids.copy_(st["ids"], non_blocking=True)
+            graph.positions.copy_(st["pos"], non_blocking=True)
+            graph.slot_mapping.copy_(st["slots"], non_blocking=True)
+            graph.context_lens.copy_(st["ctx"], non_blocking=True)
+            graph.block_tables.copy_(st["tables"], non_blocking=True)
+            graph.replay()
+            h_next.copy_(graph.next_ids, non_blocking=True)
+            build(s + 1, sets[(s + 1) % 2])  # overlaps the GPU step
+            stream.synchronize()
 
-    s_idx = 0
-    build(s_idx, sets[s_idx % 2])
-    for _ in range(w_steps):
-        e2e_step(s_idx)
-        s_idx += 1
-    torch.cuda.synchronize()
-    barrier()
-    t0 = time.perf_counter()
-    w0 = time.time()
-    for _ in range(k_steps):
-        e2e_step(s_idx)
-        s_idx += 1
-    torch.cuda.synchronize()
-    windows.append((w0, time.time()))
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    barrier()
-    e2e_value = global_batch * k_steps / e2e_s
-    h2d = sum(t.numel() * t.element_size() for t in sets[0].values())
-    d2h = h_next.numel() * 8
+        s_idx = 0
+        build(s_idx, sets[s_idx % 2])
+        for _ in range(w_steps):
+            e2e_step(s_idx)
+            s_idx += 1
+        torch.cuda.synchronize()
+        ranks.barrier()
+        t0 = time.perf_counter()
+        w0 = time.time()
+        for _ in range(k_steps):
+            e2e_step(s_idx)
+            s_idx += 1
+        torch.cuda.synchronize()
+        windows.append((w0, time.time()))
+        e2e_s = ranks.max(time.perf_counter() - t0)
+        ranks.barrier()
+        res["e2e"] = {"value": global_batch * k_steps / e2e_s, "unit": "tok/s",
+                      "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in sets[0].values()),
+                      "d2h_bytes_per_step": h_next.numel() * 8}
 
-    # ---- device decode loop: prepare -> forward -> argmax replayed with no host round trip
-    from vasr_paged_attn import decode_loop as dloop
-    loop_state = dloop.DecodeLoopState(
-        [int(x) for x in lens0], [0] * batch, [cfg.vocab_size],  # EOS id outside the vocab:
-        torch.from_numpy(tables).to(dev), blocks.tolist(), BLOCK_SIZE, nb,  # every row stays active
-        cfg.vocab_size, device=dev)
-    loop = eng.DecodeLoopGraph(model, caches, loop_state, BLOCK_SIZE)
-    loop.capture()
-    for _ in range(w_steps):
-        loop.replay()
-    torch.cuda.synchronize()
-    barrier()
-    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0 = time.time()
-    l0.record()
-    for _ in range(k_steps):
-        loop.replay()
-    l1.record()
-    torch.cuda.synchronize()
-    windows.append((w0, time.time()))
-    clk = clocks.stop(windows)
-    loop_ms = max_over_ranks(l0.elapsed_time(l1))
-    barrier()
-    fin, gen_counts, _ = loop_state.read_back()
-    loop_value = global_batch * k_steps / (loop_ms / 1e3)
-    loop.release()
+        # ---- device decode loop: prepare -> forward -> argmax replayed with no host round trip
+        from vasr_paged_attn import decode_loop as dloop
+        loop_state = dloop.DecodeLoopState(
+            [int(x) for x in lens0], [0] * batch, [cfg.vocab_size],  # EOS id outside the vocab:
+            torch.from_numpy(tables).to(dev), blocks.tolist(), BLOCK_SIZE, nb,  # every row stays active
+            cfg.vocab_size, device=dev)
+        loop = eng.DecodeLoopGraph(model, caches, loop_state, BLOCK_SIZE)
+        loop.capture()
+        for _ in range(w_steps):
+            loop.replay()
+        torch.cuda.synchronize()
+        ranks.barrier()
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.time()
+        l0.record()
+        for _ in range(k_steps):
+            loop.replay()
+        l1.record()
+        torch.cuda.synchronize()
+        windows.append((w0, time.time()))
+        loop_ms = ranks.max(l0.elapsed_time(l1))
+        ranks.barrier()
+        fin, gen_counts, _ = loop_state.read_back()
+        loop.release()
+        res["device_loop"] = {
+            "value": global_batch * k_steps / (loop_ms / 1e3), "unit": "tok/s", "ms_per_step": loop_ms / k_steps,
+            "note": "decode_step_prepare + 28 layers + greedy_argmax captured as one graph and replayed "
+                    "back to back: next ids, EOS state and metadata stay on the device (no per-step host "
+                    "round trip)",
+            "rows_active_at_end": int((~fin).sum()), "tokens_generated": int(gen_counts.sum())}
 
-    # ---- roofline of the paged decode kernel: one launch per layer, events on its stream
-    last = w_steps + k_steps - 1  # contexts of the last timed step
-    ctx_last = torch.from_numpy(ctx[min(last, total_steps - 1)]).to(dev)
+    # ---- the paged decode kernel alone: one launch per layer, events on its stream
+    last = min(w_steps + k_steps - 1, total_steps - 1)  # contexts of the last timed step
+    ctx_last = torch.from_numpy(ctx[last]).to(dev)
     q = torch.randn(batch, cfg.num_heads, cfg.head_dim, device=dev, dtype=torch.bfloat16)
     out = torch.empty_like(q)
     mcl = cols * BLOCK_SIZE
@@ -499,73 +541,132 @@ def run_ours(args):
 
     # back-to-back launches over the 28 layer caches (as inside the step), one graph replay
     launch_ms = _events_time(decode_layer, 3 * len(caches))
-    ctx_sum = int(ctx[min(last, total_steps - 1)].astype(np.int64).sum())
+    ctx_sum = int(ctx[last].astype(np.int64).sum())
     kv_bytes = ctx_sum * cfg.num_kv_heads * cfg.head_dim * 2 * 2
     qo_bytes = batch * cfg.num_heads * cfg.head_dim * 2 * 2
     alg_bytes = kv_bytes + qo_bytes
-    achieved = alg_bytes / (launch_ms / 1e3) / 1e9
-    peak, peak_kind = load_peaks()
+    step_us = local_ms / k_steps * 1e3
+    res.update(launch_ms=launch_ms, alg_bytes=alg_bytes)
+    rows = ranks.gather([rank, batch, ctx_sum, launch_ms * 1e3, alg_bytes / (launch_ms / 1e3) / 1e9,
+                         step_us / 1e3, 1.0 - cfg.num_layers * launch_ms * 1e3 / step_us])
+    res["ranks"] = [{"rank": int(r[0]), "seqs": int(r[1]), "ctx_tokens": int(r[2]),
+                     "decode_us_per_launch": round(r[3], 2), "decode_GBps": round(r[4], 1),
+                     "step_ms": round(r[5], 4), "non_paged_share_of_step": round(r[6], 4)} for r in rows]
+    res["kv_step_gb"] = float(lens0.sum()) * cfg.num_kv_heads * cfg.head_dim * 2 * 2 * cfg.num_layers / 1e9
+    graph.release()
+    del graph, caches
+    return res
+
+
+def _roofline(res, peak, peak_kind):
+    achieved = res["alg_bytes"] / (res["launch_ms"] / 1e3) / 1e9
     traffic = None
     tf = REPO / "profiles" / "paged_decode_traffic.json"
     if tf.exists():
         ratio = json.loads(tf.read_text()).get("dram_bytes_per_algorithmic_byte")
         if ratio:
-            traffic = ratio * alg_bytes
+            traffic = ratio * res["alg_bytes"]
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "kernel": "paged_decode_mma_kernel", "peak_source": peak_kind,
+            "launch_us": res["launch_ms"] * 1e3, "algorithmic_bytes_per_launch": res["alg_bytes"]}
+
+
+def run_ours(args):
+    import numpy as np  # noqa: F401
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device for --impl ours")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        # NCCL's communicator lines (rank count per communicator) stay in the log
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    ranks = Ranks(world, dev)
+    peak, peak_kind = load_peaks()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    clocks.wait_first()
+    windows = []  # host wall-clock spans of the timed regions, for the clock samples
+    main = decode_step_bench(args.config, args, dev, rank, world, ranks, windows, args.steps, full=True)
+    cfg, lens0 = main["cfg"], main["lens"]
+    weight_gb = main.pop("model").weight_bytes() / 1e9
+    torch.cuda.empty_cache()
+
+    extras = {}
+    if args.config == 5 and not args.no_extras:
+        c2 = decode_step_bench(2, args, dev, rank, world, ranks, windows, 100, full=False)
+        extras["config2"] = {
+            "value": c2["value"], "unit": "tok/s", "ms_per_step": c2["dev_ms"] / c2["k_steps"],
+            "scaling": "weak", "global_batch": c2["global_batch"],
+            "workload": "config2: qwen3-asr-0.6B decode step, 28 layers, B=64 per GPU, ctx U[200,1500]",
+            "roofline": _roofline(c2, peak, peak_kind), "ranks": c2["ranks"]}
+        del c2
+        torch.cuda.empty_cache()
+    clk = clocks.stop(windows)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 5:
-        # bounded: 64 of the 512 sequences, their layer time scaled by the context sum
-        sub = lens0[:BATCH]
-        r = cpu_attention_sample(args.seed, args.cpu_seconds, lens=sub)
-        t_full = r["t_layer"] * float(lens0.sum()) / float(sub.sum())
-        cpu = {"value": batch / (cfg.num_layers * t_full), "unit": "tok/s", "cores": r["threads"],
-               "kind": "port",
-               "sample": (f"{r['reps']} x one decode-attention layer over {len(sub)} of the {batch} "
-                          f"config-5 sequences (f32 C/OpenMP oracle), layer time scaled by the context "
-                          f"sum to all {batch} and to 28 layers per token step; GEMMs excluded; {cpu_info()}")}
-    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_attention_sample(args.seed, args.cpu_seconds)
-        cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
-               "sample": (f"{r['reps']} x one decode-attention layer ({batch} seqs, ctx U[{CTX_LO},{CTX_HI}], "
-                          f"f32 C/OpenMP oracle), scaled to 28 layers per token step; GEMMs excluded; "
-                          f"{cpu_info()}")}
-    kv_step_gb = float(lens0.sum()) * cfg.num_kv_heads * cfg.head_dim * 2 * 2 * cfg.num_layers / 1e9
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if args.config == 5:
+            # bounded: 64 of the 512 sequences, their layer time scaled by the context sum
+            sub = lens0[:BATCH]
+            r = cpu_attention_sample(args.seed, args.cpu_seconds, lens=sub)
+            t_full = r["t_layer"] * float(lens0.sum()) / float(sub.sum())
+            cpu = {"value": len(lens0) / (cfg.num_layers * t_full), "unit": "tok/s", "cores": r["threads"],
+                   "kind": "port",
+                   "sample": (f"{r['reps']} x one decode-attention layer over {len(sub)} of the {len(lens0)} "
+                              f"config-5 sequences (f32 C/OpenMP oracle), layer time scaled by the context "
+                              f"sum to all {len(lens0)} and to 28 layers per token step; GEMMs excluded; "
+                              f"{cpu_info()}")}
+        else:
+            r = cpu_attention_sample(args.seed, args.cpu_seconds)
+            cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
+                   "sample": (f"{r['reps']} x one decode-attention layer ({len(lens0)} seqs, "
+                              f"ctx U[{CTX_LO},{CTX_HI}], f32 C/OpenMP oracle), scaled to 28 layers per "
+                              f"token step; GEMMs excluded; {cpu_info()}")}
+
+    if world == 1 and not args.no_extras:
+        # each kernel on its own BASELINE config (one GPU; inputs cycled beyond L2)
+        for name, kern in (("prefill", "prefill"), ("append", "append"), ("decode_fp8", "decode_fp8"),
+                           ("copy_blocks", "copy"), ("swap_blocks", "swap"), ("gather_kv_cache", "gather")):
+            lines = KERNEL_BENCH[kern](args, torch.device("cuda", local))
+            extras[name] = lines[0] if len(lines) == 1 else {ln["config"]: ln for ln in lines}
+            torch.cuda.empty_cache()
+
     if args.config == 5:
         workload = ("config5: qwen3-asr-1.7B decode step, 28 layers, 512 sequences sharded over "
-                    f"{world} GPU(s) by KV bytes ({batch} on rank 0), ctx log-U[64,4096], block_size 16")
+                    f"{world} GPU(s) by KV bytes ({len(lens0)} on rank 0), ctx log-U[64,4096], block_size 16")
         model_name = "Qwen3-ASR-1.7B text decoder (random init)"
     else:
         workload = "config2: qwen3-asr-0.6B decode step, 28 layers, B=64 per GPU, ctx U[200,1500], block_size 16"
         model_name = "Qwen3-ASR-0.6B text decoder (random init)"
-
     if rank == 0:
+        k_steps = main["k_steps"]
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": k_steps,
-            "warmup": w_steps, "ms_per_step": dev_ms / k_steps, "higher_is_better": True,
+            "metric": METRIC, "value": main["value"], "unit": "tok/s", "n_gpus": world, "steps": k_steps,
+            "warmup": main["w_steps"], "ms_per_step": main["dev_ms"] / k_steps, "higher_is_better": True,
             "scaling": "strong" if args.config == 5 else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded contexts, random-init weights, N(0,1) cache)",
-            "config": {"workload": workload, "model": model_name, "global_batch": global_batch,
+            "config": {"workload": workload, "model": model_name, "global_batch": main["global_batch"],
                        "seq_len": int(lens0.mean()), "parallelism": f"dp{world} (request-sharded)",
-                       "graph_cols": cols,
-                       "l2": (f"inputs larger than L2 (per step {kv_step_gb:.1f} GB KV + "
-                              f"{model.weight_bytes() / 1e9:.1f} GB weights on rank 0)")},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "kernel": "paged_decode_mma_kernel",
-                         "peak_source": peak_kind, "launch_us": launch_ms * 1e3,
-                         "algorithmic_bytes_per_launch": alg_bytes},
+                       "graph_cols": main["cols"],
+                       "l2": (f"inputs larger than L2 (per step {main['kv_step_gb']:.1f} GB KV + "
+                              f"{weight_gb:.1f} GB weights on rank 0)")},
+            "roofline": _roofline(main, peak, peak_kind),
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+            "e2e": main["e2e"],
             "gpu_launches": 2 * cfg.num_layers * k_steps,
-            "device_loop": {"value": loop_value, "unit": "tok/s", "ms_per_step": loop_ms / k_steps,
-                            "note": "decode_step_prepare + 28 layers + greedy_argmax captured as one "
-                                    "graph and replayed back to back: next ids, EOS state and metadata "
-                                    "stay on the device (no per-step host round trip)",
-                            "rows_active_at_end": int((~fin).sum()), "tokens_generated": int(gen_counts.sum())},
+            "ranks": main["ranks"],
+            "device_loop": main["device_loop"],
             "clocks": clk,
         }
+        line.update(extras)
         print(json.dumps(line), flush=True)
-    graph.release()
     if world > 1:
         dist.destroy_process_group()
 
@@ -600,254 +701,319 @@ def _events_time(fn, iters):
     return ms
 
 
-def run_kernel_bench(args):
-    """One JSON line per kernel: device time per launch and the roofline fraction."""
+HQ, HKV, D = 16, 8, 128
+L2_BYTES = 126 * 2**20
+
+
+def _sets_for(bytes_per_set, cap=16):
+    """Independent input sets the timed launches cycle through: together at least
+    4x the 126 MB L2, so no launch finds the previous launches' data in L2."""
+    return max(1, min(cap, -(-4 * L2_BYTES // max(1, int(bytes_per_set)))))
+
+
+def _pool(dev, nb, layers, dtype):
+    import torch
+
+    x = 16 // torch.empty((), dtype=dtype).element_size()
+    return [(torch.randn(nb, HKV, D // x, BLOCK_SIZE, x, device=dev).to(dtype),
+             torch.randn(nb, HKV, D, BLOCK_SIZE, device=dev).to(dtype)) for _ in range(layers)]
+
+
+def _tables(rng, lens, nb, cols=None):
+    import numpy as np
+
+    blocks = [-(-int(n) // BLOCK_SIZE) for n in lens]
+    perm = rng.permutation(np.arange(1, nb))
+    t = np.zeros((len(lens), cols or max(blocks)), np.int32)
+    off = 0
+    for i, n in enumerate(blocks):
+        t[i, :n] = perm[off:off + n]
+        off += n
+    return t
+
+
+def _hbm_line(kernel, config, ms, alg, **extra):
+    peak, kind = load_peaks()
+    gbs = alg / ms / 1e6
+    d = {"kernel": kernel, "config": config, "us": ms * 1e3, "bytes": alg, "achieved": gbs, "unit": "GB/s",
+         "peak": peak, "frac": gbs / peak, "peak_source": kind}
+    d.update(extra)
+    return d
+
+
+def kb_decode(args, dev, which="decode"):
     import numpy as np
     import torch
 
     from vasr_paged_attn import mistralrs_paged_attn as pa
 
+    rng = np.random.default_rng(args.seed)
+    dtype = torch.float32 if which == "config1" else torch.bfloat16
+    if which == "config1":
+        lens = np.array([138, 513, 1024, 2049])
+        nb, layers = 512, 1
+    elif which == "decode5":  # config 5 attention shapes: 512 sequences, ctx ~log-U[64, 4096]
+        from vasr_paged_attn.workloads import config5_context_lens
+
+        lens = config5_context_lens(args.seed)
+        nb = sum(-(-int(n) // BLOCK_SIZE) for n in lens) + 1
+        layers = min(args.layers, 4)  # 4 x 2 GB pools: well above L2
+    else:
+        lens = context_lens(args.seed, 0)
+        nb = sum(-(-int(n) // BLOCK_SIZE) for n in lens) + 1
+        layers = args.layers
+    caches = _pool(dev, nb, layers, dtype)
+    t = torch.from_numpy(_tables(rng, lens, nb)).to(dev)
+    ctx = torch.from_numpy(lens.astype(np.int32)).to(dev)
+    q = torch.randn(len(lens), HQ, D, device=dev).to(dtype)
+    mcl = int(lens.max())
+    out = torch.empty_like(q)
+    es = q.element_size()
+
+    def launch(i):
+        kc, vc = caches[i % layers]
+        pa.paged_attention(q, None, None, kc, vc, t, ctx, None, mcl, D ** -0.5, 1.0, None, out=out)
+
+    ms = _events_time(launch, args.iters)
+    alg = int(lens.sum()) * HKV * D * 2 * es + q.numel() * es * 2
+    lines = [_hbm_line("paged_decode", {"config1": "config1", "decode5": "config5"}.get(which, "config2"),
+                       ms, alg, layers_cycled=layers)]
+    if which == "config1":
+        kn = torch.randn(4, HKV, D, device=dev)
+        sl = torch.from_numpy((t[:, 0].cpu().numpy().astype(np.int64) * BLOCK_SIZE)).to(dev)
+        ms = _events_time(lambda i: pa.reshape_and_cache(kn, kn, None, None, caches[0][0], caches[0][1], sl),
+                          args.iters)
+        lines.append(_hbm_line("kv_append", "config1", ms, 4 * HKV * D * 4 * 2 * 2))
+    return lines
+
+
+def kb_decode_fp8(args, dev):
+    """Config 2 shapes over fp8 (E4M3) pages with per-tensor scales (half the KV bytes)."""
+    import numpy as np
+    import torch
+
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+
+    rng = np.random.default_rng(args.seed)
+    lens = context_lens(args.seed, 0)
+    nb = sum(-(-int(n) // BLOCK_SIZE) for n in lens) + 1
+    layers = args.layers
+    caches = [((torch.randn(nb, HKV, D // 16, BLOCK_SIZE, 16, device=dev) * 8).to(torch.float8_e4m3fn),
+               (torch.randn(nb, HKV, D, BLOCK_SIZE, device=dev) * 8).to(torch.float8_e4m3fn))
+              for _ in range(layers)]
+    sk = torch.tensor([0.125], device=dev)
+    sv = torch.tensor([0.125], device=dev)
+    t = torch.from_numpy(_tables(rng, lens, nb)).to(dev)
+    ctx = torch.from_numpy(lens.astype(np.int32)).to(dev)
+    q = torch.randn(len(lens), HQ, D, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+
+    def launch(i):
+        kc, vc = caches[i % layers]
+        pa.paged_attention(q, sk, sv, kc, vc, t, ctx, None, int(lens.max()), D ** -0.5, 1.0, None, out=out)
+
+    ms = _events_time(launch, args.iters)
+    alg = int(lens.sum()) * HKV * D * 2 + q.numel() * 2 * 2
+    return [_hbm_line("paged_decode_fp8", "config2 shapes, fp8 E4M3 pages", ms, alg, layers_cycled=layers)]
+
+
+def kb_append(args, dev):
+    import numpy as np
+    import torch
+
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+
+    rng = np.random.default_rng(args.seed)
+    lines = []
+    for name, ntok, per_seq in (("config3_chunk", 32 * 256, 256), ("config2_decode", 64, 1)):
+        nb = ntok // per_seq * (-(-per_seq // BLOCK_SIZE)) + 16 + 1
+        nset = _sets_for(2 * ntok * HKV * D * 2 + nb * HKV * D * BLOCK_SIZE * 2 * 2)
+        pools = _pool(dev, nb, nset, torch.bfloat16)
+        ks = [torch.randn(ntok, HKV, D, device=dev).to(torch.bfloat16) for _ in range(nset)]
+        vs = [torch.randn(ntok, HKV, D, device=dev).to(torch.bfloat16) for _ in range(nset)]
+        nseq = ntok // per_seq
+        t = _tables(rng, [per_seq] * nseq, nb)
+        pos = np.arange(per_seq)
+        slots = np.concatenate([t[i, pos // BLOCK_SIZE].astype(np.int64) * BLOCK_SIZE + pos % BLOCK_SIZE
+                                for i in range(nseq)])
+        sl = torch.from_numpy(slots).to(dev)
+        ms = _events_time(lambda i: pa.reshape_and_cache(ks[i % nset], vs[i % nset], None, None,
+                                                         pools[i % nset][0], pools[i % nset][1], sl), args.iters)
+        lines.append(_hbm_line("kv_append", name, ms, ntok * HKV * D * 2 * 2 * 2, tokens=ntok,
+                               input_sets_cycled=nset))
+        # the same tokens into fp8 (E4M3) pages: bf16 read, one byte per element written
+        del pools
+        p8 = [(torch.zeros(nb, HKV, D // 16, BLOCK_SIZE, 16, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn),
+               torch.zeros(nb, HKV, D, BLOCK_SIZE, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn))
+              for _ in range(nset)]
+        sk = torch.tensor([0.05], device=dev)
+        ms = _events_time(lambda i: pa.reshape_and_cache(ks[i % nset], vs[i % nset], sk, sk, p8[i % nset][0],
+                                                         p8[i % nset][1], sl), args.iters)
+        lines.append(_hbm_line("kv_append_fp8", name, ms, ntok * HKV * D * 2 * (2 + 1), tokens=ntok,
+                               input_sets_cycled=nset))
+        del p8, ks, vs
+    for ln in lines:
+        ln["config"] = ln["config"] + ("_fp8" if ln["kernel"] == "kv_append_fp8" else "")
+    return lines
+
+
+def kb_gather(args, dev):
+    """gather_kv_cache of config 3's full prompts (32 x U[100, 800] tokens) from bf16 and fp8 pages."""
+    import numpy as np
+    import torch
+
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+    from vasr_paged_attn.workloads import config3_rounds
+
+    rng = np.random.default_rng(args.seed)
+    lens, _ = config3_rounds(args.seed)
+    lens = np.asarray(lens, np.int64)
+    nb = sum(-(-int(n) // BLOCK_SIZE) for n in lens) + 1
+    t = torch.from_numpy(_tables(rng, lens, nb)).to(dev)
+    cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).to(dev)
+    total = int(lens.sum())
+    nset = _sets_for(nb * HKV * D * BLOCK_SIZE * 2 * 2 + total * HKV * D * 2 * 2)
+    pools = _pool(dev, nb, nset, torch.bfloat16)
+    ms = _events_time(lambda i: pa.gather_kv_cache(pools[i % nset][0], pools[i % nset][1], None, None, t, cu,
+                                                   None, total), args.iters)
+    lines = [_hbm_line("gather_kv_cache", "config3 prompts, bf16 pages", ms, total * HKV * D * 2 * 2 * 2,
+                       tokens=total, input_sets_cycled=nset)]
+    del pools
+    nset = _sets_for(nb * HKV * D * BLOCK_SIZE * 2 + total * HKV * D * 2 * 2)
+    p8 = [((torch.randn(nb, HKV, D // 16, BLOCK_SIZE, 16, device=dev) * 8).to(torch.float8_e4m3fn),
+           (torch.randn(nb, HKV, D, BLOCK_SIZE, device=dev) * 8).to(torch.float8_e4m3fn)) for _ in range(nset)]
+    sk = torch.tensor([0.125], device=dev)
+    ms = _events_time(lambda i: pa.gather_kv_cache(p8[i % nset][0], p8[i % nset][1], sk, sk, t, cu,
+                                                   torch.bfloat16, total), args.iters)
+    lines.append(_hbm_line("gather_kv_cache_fp8", "config3 prompts, fp8 pages -> bf16", ms,
+                           total * HKV * D * 2 * (1 + 2), tokens=total, input_sets_cycled=nset))
+    return lines
+
+
+def kb_prefill(args, dev, fp8=False):
+    import numpy as np
+    import torch
+
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+    from vasr_paged_attn.workloads import config3_rounds
+
+    rng = np.random.default_rng(args.seed)
+    lens, rounds = config3_rounds(args.seed)
+    nb = sum(-(-int(n) // BLOCK_SIZE) for n in lens) + 1
+    # page pools (one per layer) and query sets cycled so that the launches' inputs exceed L2
+    nset = _sets_for(nb * HKV * D * BLOCK_SIZE * 2 * 2 + 2 * 32 * 256 * HQ * D * 2, cap=8)
+    sk = sv = None
+    if fp8:  # the same pages in E4M3 with per-tensor scales
+        pools = [((torch.randn(nb, HKV, D // 16, BLOCK_SIZE, 16, device=dev) * 8).to(torch.float8_e4m3fn),
+                  (torch.randn(nb, HKV, D, BLOCK_SIZE, device=dev) * 8).to(torch.float8_e4m3fn))
+                 for _ in range(nset)]
+        sk = sv = torch.tensor([0.125], device=dev)
+    else:
+        pools = _pool(dev, nb, nset, torch.bfloat16)
+    t_all = _tables(rng, lens, nb)
+    total_flops, total_ms = 0.0, 0.0
+    for r in rounds:
+        idx = [i for (i, _, _) in r]
+        chunk = np.array([n for (_, _, n) in r])
+        ctx = np.array([s + n for (_, s, n) in r])
+        cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+        qs = [torch.randn(int(chunk.sum()), HQ, D, device=dev).to(torch.bfloat16) for _ in range(nset)]
+        bt = torch.from_numpy(t_all[idx]).to(dev)
+        dctx = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+        dcu = torch.from_numpy(cu).to(dev)
+        mq = int(chunk.max())
+        ms = _events_time(lambda i: pa.paged_attention_varlen_prefill(qs[i % nset], pools[i % nset][0],
+                                                                      pools[i % nset][1], bt, dctx, dcu, sk, sv,
+                                                                      D ** -0.5, 1.0, mq), args.iters)
+        vis = sum(sum(int(s) + j + 1 for j in range(int(n))) for (_, s, n) in r)
+        total_flops += 4.0 * D * HQ * vis
+        total_ms += ms
+    tflops = total_flops / (total_ms / 1e3) / 1e12
+    tpeak, tkind = load_tensor_peak()
+    return [{"kernel": "paged_prefill_varlen" + ("_fp8" if fp8 else ""),
+             "config": "config3 (one layer, all chunk rounds)", "rounds": len(rounds),
+             "us": total_ms * 1e3, "flops": total_flops, "achieved": tflops, "unit": "TFLOP/s",
+             "peak": tpeak, "frac": tflops / tpeak, "peak_source": tkind, "input_sets_cycled": nset,
+             "tflop_28_layers": total_flops * 28 / 1e12}]
+
+
+def kb_copy(args, dev):
+    """Config 4 copy_blocks: 4096 seeded src -> dst pairs over 200k-block pools, as many layers as fit."""
+    import numpy as np
+    import torch
+
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+
+    rng = np.random.default_rng(args.seed)
+    free, _ = torch.cuda.mem_get_info()
+    nb = 200_000
+    per_layer = nb * HKV * D * BLOCK_SIZE * 2 * 2
+    layers = max(1, min(args.layers, int(free * 0.8 // per_layer)))
+    caches = [(torch.empty(nb, HKV, D // 8, BLOCK_SIZE, 8, dtype=torch.bfloat16, device=dev),
+               torch.empty(nb, HKV, D, BLOCK_SIZE, dtype=torch.bfloat16, device=dev)) for _ in range(layers)]
+    perm = rng.permutation(nb)
+    pairs = torch.from_numpy(np.stack([perm[:4096], perm[4096:8192]], 1).astype(np.int64)).to(dev)
+    ms = _events_time(lambda i: pa.copy_blocks([c[0] for c in caches], [c[1] for c in caches], pairs),
+                      args.iters)
+    alg = 4096 * layers * 2 * (HKV * D * BLOCK_SIZE * 2) * 2
+    return [_hbm_line("copy_blocks", "config4", ms, alg, layers_allocated=layers,
+                      ms_28_layers_extrapolated=ms * 28 / layers)]
+
+
+def kb_swap(args, dev):
+    """1024 blocks of one layer cache device <-> pinned host, against pinned cudaMemcpyAsync of the
+    same bytes (the host link is the roofline)."""
+    import numpy as np
+    import torch
+
+    from vasr_paged_attn import mistralrs_paged_attn as pa
+
+    rng = np.random.default_rng(args.seed)
+    nb_dev, nb_host = 8192, 2048
+    dcache = torch.randn(nb_dev, HKV, D, BLOCK_SIZE, device=dev).to(torch.bfloat16)
+    hcache = torch.empty(nb_host, HKV, D, BLOCK_SIZE, dtype=torch.bfloat16).pin_memory()
+    src = rng.permutation(nb_dev)[:1024]
+    dst = rng.permutation(nb_host)[:1024]
+    out_map = torch.from_numpy(np.stack([src, dst], 1).astype(np.int64)).to(dev)
+    in_map = torch.from_numpy(np.stack([dst, src], 1).astype(np.int64)).to(dev)
+    blk = HKV * D * BLOCK_SIZE * 2
+    ms_out = _events_time(lambda i: pa.swap_blocks(dcache, hcache, out_map), args.iters)
+    ms_in = _events_time(lambda i: pa.swap_blocks(hcache, dcache, in_map), args.iters)
+    big = torch.empty(1024 * blk // 2, dtype=torch.bfloat16, device=dev)
+    hbig = torch.empty_like(big, device="cpu").pin_memory()
+    ms_d2h = _events_time(lambda i: hbig.copy_(big, non_blocking=True), args.iters)
+    ms_h2d = _events_time(lambda i: big.copy_(hbig, non_blocking=True), args.iters)
+    n = 1024 * blk
+    d2h, h2d = n / ms_out / 1e6, n / ms_in / 1e6
+    pd2h, ph2d = n / ms_d2h / 1e6, n / ms_h2d / 1e6
+    return [{"kernel": "swap_blocks", "config": "config4 (1024 blocks of one layer cache)", "bytes": n,
+             "us_d2h": ms_out * 1e3, "us_h2d": ms_in * 1e3, "achieved": min(d2h, h2d), "unit": "GB/s",
+             "peak": min(pd2h, ph2d), "frac": min(d2h / pd2h, h2d / ph2d),
+             "peak_source": "pinned cudaMemcpyAsync of the same bytes, measured in this run",
+             "d2h_GB/s": d2h, "h2d_GB/s": h2d, "pinned_copy_d2h_GB/s": pd2h, "pinned_copy_h2d_GB/s": ph2d}]
+
+
+KERNEL_BENCH = {
+    "decode": lambda a, d: kb_decode(a, d, "decode"),
+    "decode5": lambda a, d: kb_decode(a, d, "decode5"),
+    "config1": lambda a, d: kb_decode(a, d, "config1"),
+    "decode_fp8": kb_decode_fp8,
+    "append": kb_append,
+    "gather": kb_gather,
+    "prefill": lambda a, d: kb_prefill(a, d, fp8=False),
+    "prefill_fp8": lambda a, d: kb_prefill(a, d, fp8=True),
+    "copy": kb_copy,
+    "swap": kb_swap,
+}
+
+
+def run_kernel_bench(args):
+    """One JSON line per kernel: device time per launch and the roofline fraction."""
+    import torch
+
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    peak, peak_kind = load_peaks()
-    rng = np.random.default_rng(args.seed)
-    hq, hkv, d, bs = 16, 8, 128, BLOCK_SIZE
-    lines = []
-
-    def pool(nb, layers, dtype=torch.bfloat16):
-        x = 16 // torch.empty((), dtype=dtype).element_size()
-        out = []
-        for _ in range(layers):
-            kc = torch.randn(nb, hkv, d // x, bs, x, device=dev).to(dtype)
-            vc = torch.randn(nb, hkv, d, bs, device=dev).to(dtype)
-            out.append((kc, vc))
-        return out
-
-    l2_bytes = 126 * 2**20
-
-    def sets_for(bytes_per_set, cap=16):
-        """Independent input sets the timed launches cycle through: together at least
-        4x the 126 MB L2, so no launch finds the previous launches' data in L2."""
-        return max(1, min(cap, -(-4 * l2_bytes // max(1, int(bytes_per_set)))))
-
-    def tables_for(lens, nb, cols=None):
-        blocks = [-(-int(n) // bs) for n in lens]
-        perm = rng.permutation(np.arange(1, nb))
-        t = np.zeros((len(lens), cols or max(blocks)), np.int32)
-        off = 0
-        for i, n in enumerate(blocks):
-            t[i, :n] = perm[off:off + n]
-            off += n
-        return t
-
-    k = args.kernel
-    if k in ("decode", "config1", "decode5"):
-        dtype = torch.float32 if k == "config1" else torch.bfloat16
-        if k == "config1":
-            lens = np.array([138, 513, 1024, 2049])
-            nb, layers = 512, 1
-        elif k == "decode5":  # config 5 attention shapes: 512 sequences, ctx ~log-U[64, 4096]
-            from vasr_paged_attn.workloads import config5_context_lens
-
-            lens = config5_context_lens(args.seed)
-            nb = sum(-(-int(n) // bs) for n in lens) + 1
-            layers = min(args.layers, 4)  # 4 x 2 GB pools: well above L2
-        else:
-            lens = context_lens(args.seed, 0)
-            nb = sum(-(-int(n) // bs) for n in lens) + 1
-            layers = args.layers
-        caches = pool(nb, layers, dtype)
-        t = torch.from_numpy(tables_for(lens, nb)).to(dev)
-        ctx = torch.from_numpy(lens.astype(np.int32)).to(dev)
-        q = torch.randn(len(lens), hq, d, device=dev).to(dtype)
-        mcl = int(lens.max())
-        out = torch.empty_like(q)
-        es = q.element_size()
-
-        def launch(i):
-            kc, vc = caches[i % layers]
-            pa.paged_attention(q, None, None, kc, vc, t, ctx, None, mcl, d ** -0.5, 1.0, None, out=out)
-
-        ms = _events_time(launch, args.iters)
-        alg = int(lens.sum()) * hkv * d * 2 * es + q.numel() * es * 2
-        lines.append({"kernel": "paged_decode", "config": {"config1": "config1", "decode5": "config5"}.get(k, "config2"),
-                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
-                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "layers_cycled": layers})
-        if k == "config1":
-            kn = torch.randn(4, hkv, d, device=dev)
-            sl = torch.from_numpy((t[:, 0].cpu().numpy().astype(np.int64) * bs)).to(dev)
-            ms = _events_time(lambda i: pa.reshape_and_cache(kn, kn, None, None, caches[0][0], caches[0][1], sl),
-                              args.iters)
-            alg = 4 * hkv * d * 4 * 2 * 2
-            lines.append({"kernel": "kv_append", "config": "config1", "us": ms * 1e3, "bytes": alg,
-                          "GB/s": alg / ms / 1e6})
-    elif k == "decode_fp8":
-        # config 2 shapes over fp8 (E4M3) pages with per-tensor scales (half the KV bytes)
-        lens = context_lens(args.seed, 0)
-        nb = sum(-(-int(n) // bs) for n in lens) + 1
-        layers = args.layers
-        caches = []
-        for _ in range(layers):
-            kc = (torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn)
-            vc = (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)
-            caches.append((kc, vc))
-        sk = torch.tensor([0.125], device=dev)
-        sv = torch.tensor([0.125], device=dev)
-        t = torch.from_numpy(tables_for(lens, nb)).to(dev)
-        ctx = torch.from_numpy(lens.astype(np.int32)).to(dev)
-        q = torch.randn(len(lens), hq, d, device=dev).to(torch.bfloat16)
-        out = torch.empty_like(q)
-
-        def launch(i):
-            kc, vc = caches[i % layers]
-            pa.paged_attention(q, sk, sv, kc, vc, t, ctx, None, int(lens.max()), d ** -0.5, 1.0, None,
-                               out=out)
-
-        ms = _events_time(launch, args.iters)
-        alg = int(lens.sum()) * hkv * d * 2 + q.numel() * 2 * 2
-        lines.append({"kernel": "paged_decode_fp8", "config": "config2 shapes, fp8 E4M3 pages",
-                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
-                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "layers_cycled": layers})
-    elif k == "append":
-        for name, ntok, per_seq in (("config2_decode", 64, 1), ("config3_chunk", 32 * 256, 256)):
-            nb = ntok // per_seq * (-(-per_seq // bs)) + 16 + 1
-            nset = sets_for(2 * ntok * hkv * d * 2 + nb * hkv * d * bs * 2 * 2)
-            pools = pool(nb, nset)
-            ks = [torch.randn(ntok, hkv, d, device=dev).to(torch.bfloat16) for _ in range(nset)]
-            vs = [torch.randn(ntok, hkv, d, device=dev).to(torch.bfloat16) for _ in range(nset)]
-            nseq = ntok // per_seq
-            t = tables_for([per_seq] * nseq, nb)
-            pos = np.arange(per_seq)
-            slots = np.concatenate([t[i, pos // bs].astype(np.int64) * bs + pos % bs for i in range(nseq)])
-            sl = torch.from_numpy(slots).to(dev)
-            ms = _events_time(lambda i: pa.reshape_and_cache(ks[i % nset], vs[i % nset], None, None,
-                                                             pools[i % nset][0], pools[i % nset][1], sl), args.iters)
-            alg = ntok * hkv * d * 2 * 2 * 2
-            lines.append({"kernel": "kv_append", "config": name, "tokens": ntok, "us": ms * 1e3,
-                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak,
-                          "input_sets_cycled": nset})
-            # the same tokens into fp8 (E4M3) pages: bf16 read, one byte per element written
-            del pools
-            p8 = [(torch.zeros(nb, hkv, d // 16, bs, 16, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn),
-                   torch.zeros(nb, hkv, d, bs, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn))
-                  for _ in range(nset)]
-            sk = torch.tensor([0.05], device=dev)
-            ms = _events_time(lambda i: pa.reshape_and_cache(ks[i % nset], vs[i % nset], sk, sk, p8[i % nset][0],
-                                                             p8[i % nset][1], sl), args.iters)
-            alg = ntok * hkv * d * 2 * (2 + 1)
-            lines.append({"kernel": "kv_append_fp8", "config": name, "tokens": ntok, "us": ms * 1e3,
-                          "bytes": alg, "GB/s": alg / ms / 1e6, "frac_of_" + peak_kind: alg / ms / 1e6 / peak,
-                          "input_sets_cycled": nset})
-            del p8, ks, vs
-    elif k == "gather":
-        # gather_kv_cache of config 3's full prompts (32 x U[100, 800] tokens) from bf16 and fp8 pages
-        from vasr_paged_attn.workloads import config3_rounds
-
-        lens, _ = config3_rounds(args.seed)
-        lens = np.asarray(lens, np.int64)
-        nb = sum(-(-int(n) // bs) for n in lens) + 1
-        t = torch.from_numpy(tables_for(lens, nb)).to(dev)
-        cu = torch.from_numpy(np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)).to(dev)
-        total = int(lens.sum())
-        nset = sets_for(nb * hkv * d * bs * 2 * 2 + total * hkv * d * 2 * 2)
-        pools = pool(nb, nset)
-        ms = _events_time(lambda i: pa.gather_kv_cache(pools[i % nset][0], pools[i % nset][1], None, None, t, cu,
-                                                       None, total), args.iters)
-        alg = total * hkv * d * 2 * 2 * 2
-        lines.append({"kernel": "gather_kv_cache", "config": "config3 prompts, bf16 pages", "tokens": total,
-                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
-                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "input_sets_cycled": nset})
-        del pools
-        nset = sets_for(nb * hkv * d * bs * 2 + total * hkv * d * 2 * 2)
-        p8 = [((torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn),
-               (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)) for _ in range(nset)]
-        sk = torch.tensor([0.125], device=dev)
-        ms = _events_time(lambda i: pa.gather_kv_cache(p8[i % nset][0], p8[i % nset][1], sk, sk, t, cu,
-                                                       torch.bfloat16, total), args.iters)
-        alg = total * hkv * d * 2 * (1 + 2)
-        lines.append({"kernel": "gather_kv_cache_fp8", "config": "config3 prompts, fp8 pages -> bf16",
-                      "tokens": total, "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
-                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak, "input_sets_cycled": nset})
-    elif k in ("prefill", "prefill_fp8"):
-        from vasr_paged_attn.workloads import config3_rounds
-
-        lens, rounds = config3_rounds(args.seed)
-        nb = sum(-(-int(n) // bs) for n in lens) + 1
-        # page pools (one per layer) and query sets cycled so that the launches' inputs exceed L2
-        nset = sets_for(nb * hkv * d * bs * 2 * 2 + 2 * 32 * 256 * hq * d * 2, cap=8)
-        sk = sv = None
-        if k == "prefill_fp8":  # the same pages in E4M3 with per-tensor scales
-            pools = [((torch.randn(nb, hkv, d // 16, bs, 16, device=dev) * 8).to(torch.float8_e4m3fn),
-                      (torch.randn(nb, hkv, d, bs, device=dev) * 8).to(torch.float8_e4m3fn)) for _ in range(nset)]
-            sk = sv = torch.tensor([0.125], device=dev)
-        else:
-            pools = pool(nb, nset)
-        t_all = tables_for(lens, nb)
-        total_flops, total_ms = 0.0, 0.0
-        for r in rounds:
-            idx = [i for (i, _, _) in r]
-            chunk = np.array([n for (_, _, n) in r])
-            ctx = np.array([s + n for (_, s, n) in r])
-            cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
-            qs = [torch.randn(int(chunk.sum()), hq, d, device=dev).to(torch.bfloat16) for _ in range(nset)]
-            bt = torch.from_numpy(t_all[idx]).to(dev)
-            dctx = torch.from_numpy(ctx.astype(np.int32)).to(dev)
-            dcu = torch.from_numpy(cu).to(dev)
-            mq = int(chunk.max())
-            ms = _events_time(lambda i: pa.paged_attention_varlen_prefill(qs[i % nset], pools[i % nset][0],
-                                                                          pools[i % nset][1], bt, dctx, dcu, sk, sv,
-                                                                          d ** -0.5, 1.0, mq), args.iters)
-            vis = sum(sum(int(s) + j + 1 for j in range(int(n))) for (_, s, n) in r)
-            total_flops += 4.0 * d * hq * vis
-            total_ms += ms
-        tflops = total_flops / (total_ms / 1e3) / 1e12
-        mp = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) if (REPO / "MEASURED_PEAKS.json").exists() else {}
-        tpeak = float(mp.get("bf16_tflops", 1590.0))
-        lines.append({"kernel": "paged_prefill_varlen" + ("_fp8" if k == "prefill_fp8" else ""),
-                      "config": "config3 (one layer, all chunk rounds)",
-                      "rounds": len(rounds), "us_per_layer": total_ms * 1e3, "flops_per_layer": total_flops,
-                      "input_sets_cycled": nset,
-                      "TFLOP/s": tflops, "frac_of_bf16_peak": tflops / tpeak,
-                      "tflops_28_layers": total_flops * 28 / 1e12})
-    elif k == "copy":
-        free, _ = torch.cuda.mem_get_info()
-        per_layer = 200_000 * hkv * d * bs * 2 * 2
-        layers = max(1, min(args.layers, int(free * 0.8 // per_layer)))
-        nb = 200_000
-        caches = []
-        for _ in range(layers):
-            caches.append((torch.empty(nb, hkv, d // 8, bs, 8, dtype=torch.bfloat16, device=dev),
-                           torch.empty(nb, hkv, d, bs, dtype=torch.bfloat16, device=dev)))
-        perm = rng.permutation(nb)
-        pairs = torch.from_numpy(np.stack([perm[:4096], perm[4096:8192]], 1).astype(np.int64)).to(dev)
-        ms = _events_time(lambda i: pa.copy_blocks([c[0] for c in caches], [c[1] for c in caches], pairs),
-                          args.iters)
-        alg = 4096 * layers * 2 * (hkv * d * bs * 2) * 2
-        lines.append({"kernel": "copy_blocks", "config": "config4", "layers_allocated": layers,
-                      "us": ms * 1e3, "bytes": alg, "GB/s": alg / ms / 1e6,
-                      "frac_of_" + peak_kind: alg / ms / 1e6 / peak,
-                      "ms_28_layers_extrapolated": ms * 28 / layers})
-    elif k == "swap":
-        nb_dev, nb_host = 8192, 2048
-        dcache = torch.randn(nb_dev, hkv, d, bs, device=dev).to(torch.bfloat16)
-        hcache = torch.empty(nb_host, hkv, d, bs, dtype=torch.bfloat16).pin_memory()
-        src = rng.permutation(nb_dev)[:1024]
-        dst = rng.permutation(nb_host)[:1024]
-        out_map = torch.from_numpy(np.stack([src, dst], 1).astype(np.int64)).to(dev)
-        in_map = torch.from_numpy(np.stack([dst, src], 1).astype(np.int64)).to(dev)
-        blk = hkv * d * bs * 2
-        ms_out = _events_time(lambda i: pa.swap_blocks(dcache, hcache, out_map), args.iters)
-        ms_in = _events_time(lambda i: pa.swap_blocks(hcache, dcache, in_map), args.iters)
-        big = torch.empty(1024 * blk // 2, dtype=torch.bfloat16, device=dev)
-        hbig = torch.empty_like(big, device="cpu").pin_memory()
-        ms_d2h = _events_time(lambda i: hbig.copy_(big, non_blocking=True), args.iters)
-        ms_h2d = _events_time(lambda i: big.copy_(hbig, non_blocking=True), args.iters)
-        n = 1024 * blk
-        lines.append({"kernel": "swap_blocks", "config": "config4 (1024 blocks of one layer cache)",
-                      "d2h_GB/s": n / ms_out / 1e6, "h2d_GB/s": n / ms_in / 1e6,
-                      "pinned_copy_d2h_GB/s": n / ms_d2h / 1e6, "pinned_copy_h2d_GB/s": n / ms_h2d / 1e6,
-                      "bytes": n})
-    for ln in lines:
+    for ln in KERNEL_BENCH[args.kernel](args, dev):
         print(json.dumps(ln), flush=True)
 
 

@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(128, 2) paged_decode_kernel(const DecodeParams
   const float scale_l2 = p.scale;
   const bool use_softcap = (p.softcap != 1.0f) && (p.softcap > 0.f);
   bool aborted = false;
+  int u_abort = 0;
 
   float *p_w = p_s + warp * G * C::kST;
 
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(128, 2) paged_decode_kernel(const DecodeParams
     const uint32_t bar = s_base + C::kOffBar + s * 8;
     if (!mbar_wait_bounded(bar, (uint32_t)((u / C::kNST) & 1))) {
       aborted = true;
+      u_abort = u;
       break;
     }
     const int unit_tok0 = tok_begin + u * C::kST;
@@ -323,6 +325,12 @@ __global__ void __launch_bounds__(128, 2) paged_decode_kernel(const DecodeParams
       fence_proxy_async_smem();
       issue_unit(nu);
     }
+  }
+
+  // stages of this warp still in flight land before the CTA retires
+  if (aborted) {
+    for (int v = u_abort; v < min(u_abort + C::kNST, n_units); v += C::kWarps)
+      mbar_wait_bounded(s_base + C::kOffBar + (v % C::kNST) * 8, (uint32_t)((v / C::kNST) & 1));
   }
 
   // ---- warp-level finalisation

@@ -58,6 +58,22 @@ struct DecodeG2Cfg {
   static_assert(D % (4 * kRPP) == 0, "head_dim not covered by PV lanes");
 };
 
+// A warp whose wait on unit u_abort gave up issues no further stage. Its own
+// copies still in flight are those of units u_abort, u_abort + kWarps, ...
+// up to kNST units ahead (a warp refills only the stages it consumes, kNST
+// units ahead); they must land before the CTA retires, since the hardware
+// hands this shared memory to the next CTA. Each is waited for once more,
+// again bounded; a copy that does not arrive within that second limit is the
+// one case left that can outlive the CTA (recorded in the device error word).
+template <typename C>
+__device__ __forceinline__ void decode_drain_warp_stages(uint32_t s_base, int u_abort, int n_units,
+                                                         uint32_t ubase) {
+  for (int v = u_abort; v < min(u_abort + C::kNST, n_units); v += C::kWarps) {
+    const uint32_t uu = ubase + (uint32_t)v;
+    mbar_wait_bounded(s_base + C::kOffBar + (uu % C::kNST) * 8, (uu / C::kNST) & 1u);
+  }
+}
+
 // One work item: (split, kv head, sequence). `ubase` = stage-ring units this
 // CTA consumed before (the ring's barriers keep counting across items);
 // returns the units consumed here. The barriers are initialised by the caller.
@@ -187,6 +203,7 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
   float l_part = 0.f;
   const bool use_softcap = (p.softcap != 1.0f) && (p.softcap > 0.f);
   bool aborted = false;
+  int u_abort = 0;
   float *p_w = p_s + warp * G * C::kST;
 
   for (int u = warp; u < n_units; u += C::kWarps) {
@@ -194,6 +211,7 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
     const uint32_t bar = s_base + C::kOffBar + s * 8;
     if (!mbar_wait_bounded(bar, (uint32_t)(((ubase + u) / C::kNST) & 1))) {
       aborted = true;
+      u_abort = u;
       break;
     }
     const int unit_tok0 = tok_begin + u * C::kST;
@@ -331,6 +349,8 @@ __device__ __forceinline__ uint32_t decode_g2_item(const DecodeParams &p, unsign
       issue_unit(nu);
     }
   }
+
+  if (aborted) decode_drain_warp_stages<C>(s_base, u_abort, n_units, ubase);
 
   // ---- warp finalisation: l of head g lives in lanes with qb0 == g
   float l_g = l_part;

@@ -207,11 +207,13 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
   for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_used = -INFINITY, l_part = 0.f;  // row grp (lanes 0-7 meaningful)
   bool aborted = false;
+  int u_abort = 0;
 
   for (int u = warp; u < n_units; u += C::kWarps) {
     const int s = u % C::kNST;
     if (!mbar_wait_bounded(s_base + C::kOffBar + s * 8, (uint32_t)((u / C::kNST) & 1))) {
       aborted = true;
+      u_abort = u;
       break;
     }
     const int n_valid = min(C::kST, tok_end - (tok_begin + u * C::kST));
@@ -338,6 +340,8 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
       issue_unit(nu);
     }
   }
+
+  if (aborted) decode_drain_warp_stages<C>(s_base, u_abort, n_units, 0);
 
   // ---- warp results -> shared memory (rows 0 and 1 live in lanes 0-7)
   float l_row = l_part;

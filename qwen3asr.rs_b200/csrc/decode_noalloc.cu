@@ -31,16 +31,24 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 std::mutex g_scratch_mu;
 void *g_scratch_ptr[64] = {};
 
-// Device address of the scratch on the current device, resolved once per
-// device with that device current.
-int32_t scratch_on_current_device(void **out) {
+// Device address of the scratch on the current device. Outside stream
+// capture every call looks it up again with that device current, so a module
+// that the runtime reloaded (after cudaDeviceReset, for instance) is found at
+// its new address; while `stream` is capturing, the address an earlier call
+// resolved on this device is used, and the lookup runs only if there is none.
+int32_t scratch_on_current_device(cudaStream_t stream, void **out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     cudaGetLastError();
     return VASR_PA_EDEVICE;
   }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return VASR_PA_ELAUNCH;
+  }
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  if (cs == cudaStreamCaptureStatusNone || g_scratch_ptr[dev] == nullptr) {
     void *p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -80,11 +88,12 @@ int32_t vasr_pa_paged_attention_noalloc(void *out, const void *query, const void
   }
   if (need > kNoAllocScratchBytes) return VASR_PA_ESCRATCH_LIMIT;
   void *scratch = nullptr;
-  const int32_t st = scratch_on_current_device(&scratch);
+  const int32_t st = scratch_on_current_device(reinterpret_cast<cudaStream_t>(stream), &scratch);
   if (st != VASR_PA_OK) return st;
   // The split-K arrival counters (the first num_seqs * num_kv_heads words of
-  // the workspace layout) must start at zero; the scratch keeps whatever the
-  // previous call left, so clear them on the stream first.
+  // the workspace layout) must start at zero. A completed decode launch leaves
+  // the counters it used at zero; this clear guards against a previous launch
+  // that stopped early (a bounded wait that gave up) and left some behind.
   const size_t counter_bytes = (size_t)num_seqs * (size_t)num_kv_heads * sizeof(uint32_t);
   if (cudaMemsetAsync(scratch, 0, counter_bytes, reinterpret_cast<cudaStream_t>(stream)) !=
       cudaSuccess) {

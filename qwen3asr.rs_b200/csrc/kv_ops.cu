@@ -182,8 +182,9 @@ int launch_append_t(const AppendArgs &a, cudaStream_t stream) {
   constexpr int kSmemMax = 2 * kAppendMaxTokens * (kAppendRowBytes + D * (int)sizeof(T) + 16) + kTail;
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(kv_append_kernel<T, BS, D>, kSmemMax, attr_done)) return VASR_PA_ELAUNCH;
-  dim3 grid((unsigned)((a.num_tokens + tt - 1) / tt),
-            (unsigned)((a.num_kv_heads + p.heads_per_tile - 1) / p.heads_per_tile));
+  const int64_t tiles = (a.num_tokens + tt - 1) / tt;
+  if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+  dim3 grid((unsigned)tiles, (unsigned)((a.num_kv_heads + p.heads_per_tile - 1) / p.heads_per_tile));
   kv_append_kernel<T, BS, D><<<grid, kAppendThreads, smem, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }

@@ -20,8 +20,6 @@
 // the kernel under 128 registers (2 CTAs = 16 warps per SM). Warps whose
 // rows the causal mask hides from a whole half-tile skip it.
 // f32: CUDA-core kernel, one CTA per (query row, kv head), online softmax.
-#include <cstdlib>
-#include <cstring>
 
 #include "common.cuh"
 #include "launch.h"
@@ -236,7 +234,7 @@ __global__ void __launch_bounds__(256, 2) prefill_tc_kernel(const PrefillParams 
 
   for (int kt = 0; kt < n_kt; ++kt) {
     const int s = kt % C::kNST;
-    mbar_wait_bounded(s_base + C::kOffBar + s * 8, (uint32_t)((kt / C::kNST) & 1));
+    const bool landed = mbar_wait_bounded(s_base + C::kOffBar + s * 8, (uint32_t)((kt / C::kNST) & 1));
     const int key0 = kt * C::kBK;
     const uint32_t sk = s_base + C::kOffK + s * C::kTileBytes;
     const uint32_t sv = s_base + C::kOffV + s * C::kTileBytes;
@@ -346,7 +344,16 @@ __global__ void __launch_bounds__(256, 2) prefill_tc_kernel(const PrefillParams 
         }
       }
     }
-    __syncthreads();  // every warp is done with stage s
+    // every warp is done with stage s; if any thread's wait gave up, issue
+    // nothing more: the tiles still in flight (kt .. kt + kNST - 1) land
+    // before the CTA retires (waited for once more, bounded), and the rows
+    // stay unwritten (the device error word carries the timeout)
+    if (!__syncthreads_and(landed)) {
+      if (warp == 0)
+        for (int t = kt; t < min(kt + C::kNST, n_kt); ++t)
+          mbar_wait_bounded(s_base + C::kOffBar + (t % C::kNST) * 8, (uint32_t)((t / C::kNST) & 1));
+      return;
+    }
     if (tid == 0 && kt + C::kNST < n_kt) {
       fence_proxy_async_smem();
       issue_tile(kt + C::kNST);
@@ -495,15 +502,12 @@ int tc_dispatch(const PrefillArgs &a, const PrefillParams &p, cudaStream_t s) {
   }
 }
 
-// The tcgen05 kernel (prefill_umma.cu) serves the shapes it supports unless
-// VASR_PREFILL_KERNEL=mma selects this file's mma.sync kernel (A/B timing).
-bool umma_enabled() {
-  static const bool on = [] {
-    const char *e = std::getenv("VASR_PREFILL_KERNEL");
-    return !(e && std::strcmp(e, "mma") == 0);
-  }();
-  return on;
-}
+// The tcgen05 kernel (prefill_umma.cu) serves the shapes it supports; an
+// A/B build compiled with -DVASR_PREFILL_MMA_ONLY=1 sends every 16-bit call
+// to this file's mma.sync kernel instead. The library reads no environment.
+#ifndef VASR_PREFILL_MMA_ONLY
+#define VASR_PREFILL_MMA_ONLY 0
+#endif
 
 template <int BS>
 int scalar_launch(const PrefillArgs &a, const PrefillParams &p, cudaStream_t s) {
@@ -538,7 +542,7 @@ int launch_prefill(const PrefillArgs &a, cudaStream_t s) {
   p.tiles = 1;
   p.scale = a.scale;
   p.softcap = a.softcapping;
-  if ((a.dtype == VASR_PA_BF16 || a.dtype == VASR_PA_F16) && umma_enabled()) {
+  if ((a.dtype == VASR_PA_BF16 || a.dtype == VASR_PA_F16) && !VASR_PREFILL_MMA_ONLY) {
     const int r = launch_prefill_umma(a, s);
     if (r != VASR_PA_ENOT_SUPPORTED) return r;
   }

@@ -34,11 +34,14 @@
 // Softmax keeps a per-row running max that only moves when a tile's max
 // exceeds it by more than 2^8, so O in TMEM is rescaled rarely (exact in
 // real arithmetic: numerator and denominator use the same offset).
-// Every mbarrier wait is bounded (VASR_PA_DERR_WAIT_TIMEOUT) and the kernel
-// always frees its tensor memory before returning.
+// Every mbarrier wait is bounded (VASR_PA_DERR_WAIT_TIMEOUT). A warp whose
+// wait gives up issues no further copy or MMA; the load warp then waits
+// (bounded) for the last copy issued on each stage and the MMA warp for its
+// last commit, so that no copy lands in shared memory and no MMA writes
+// tensor memory after the CTA has let them go; the kernel always frees its
+// tensor memory before returning.
 #include <cuda.h>
 
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -407,29 +410,40 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (n_kt > 1) load_k(1);
     load_v(0);
     if (n_kt > 1) load_v(1);
+    int k_issued = min(n_kt, 2), v_issued = min(n_kt, 2);
     __syncthreads();
     // The tensor core completes Q K^T 0, Q K^T 1, P V 0, Q K^T 2, P V 1, ...
-    // in this order; the loads wait for those events in the same order.
+    // in this order; the loads wait for those events in the same order. Once
+    // a wait gives up, nothing more is issued: a stage whose previous copy or
+    // reader has not finished must not receive another.
     bool dead = false;
-    for (int j = 2; j < min(n_kt, 4); ++j) {
+    for (int j = 2; j < min(n_kt, 4) && !dead; ++j) {
       wait_phase(B(kBarEmptyK + (j & 1)), ((j >> 1) - 1) & 1, dead);
+      if (dead) break;
       load_k(j);
+      k_issued = j + 1;
     }
-    for (int j = 2; j < n_kt; ++j) {
+    for (int j = 2; j < n_kt && !dead; ++j) {
       wait_phase(B(kBarEmptyV + (j & 1)), ((j >> 1) - 1) & 1, dead);
+      if (dead) break;
       load_v(j);
+      v_issued = j + 1;
       if (j + 2 < n_kt) {
         wait_phase(B(kBarEmptyK + (j & 1)), (((j + 2) >> 1) - 1) & 1, dead);
+        if (dead) break;
         load_k(j + 2);
+        k_issued = j + 3;
       }
     }
     // copies still in flight must land before the CTA's shared memory goes
-    // away (in a healthy run every one of them was already waited for)
+    // away: the last phase issued on each stage (in a healthy run every one
+    // of them was already waited for); waited for once more, bounded
     dead = false;
-    for (int j = max(0, n_kt - kStages); j < n_kt; ++j) {
+    for (int j = max(0, k_issued - kStages); j < k_issued; ++j)
       wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
+    dead = false;
+    for (int j = max(0, v_issued - kStages); j < v_issued; ++j)
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
-    }
     __syncthreads();
     return;
   }
@@ -447,8 +461,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // Order on the tensor core: Q K^T 0, Q K^T 1, then per tile j: P V j,
     // Q K^T j + 2. Backpressure from the tensor core stalls only this warp.
     const uint32_t idesc_s = idesc_f16<T>(kNT), idesc_o = idesc_f16<T>(kD);
+    // last commit issued (barrier index, phase parity): once it arrives every
+    // MMA this warp issued has completed
+    int last_bar = -1;
+    uint32_t last_par = 0;
     auto issue_s = [&](int j) {  // S(j & 1) = Q K_j^T
       wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
+      if (dead) return;
       tc_fence_after();
       {
         const uint32_t sk = sbase + kOffK + (j & 1) * kKVTile;
@@ -458,14 +477,17 @@ __global__ void __launch_bounds__(kThreads, 2)
                    sdesc(sbase + kOffQ + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32, 16, 1024, 2),
                    sdesc(sk + ks * 2 * (kNT * 16), kNT * 16, 128, 0), idesc_s, ks > 0);
         umma_commit(B(kBarSFull + (j & 1)));  // = kBarEmptyK
+        last_bar = kBarSFull + (j & 1);
+        last_par = (j >> 1) & 1;
       }
       __syncwarp();
     };
     wait_phase(B(kBarQ), 0, dead);
-    issue_s(0);
-    if (n_kt > 1) issue_s(1);
-    for (int j = 0; j < n_kt; ++j) {
+    if (!dead) issue_s(0);
+    if (n_kt > 1 && !dead) issue_s(1);
+    for (int j = 0; j < n_kt && !dead; ++j) {
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
+      if (dead) break;
       if (j == n_kt - 1 && (kv_end % kBS) != 0) {
         // V of tokens >= kv_end in the last page holds other data (possibly
         // non-finite); zero it so that P = 0 there contributes exactly 0.
@@ -477,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       // P of tile j (a ring of two: the softmax warps may run one tile ahead)
       wait_phase(B(kBarPFull + (j & 1)), (j >> 1) & 1, dead);
+      if (dead) break;
       tc_fence_after();
       {
         const int np = min(kPagesPerTile, n_pages - j * kPagesPerTile);
@@ -485,6 +508,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           umma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * kNT + pg * (kBS / 2),
                       sdesc(sv + pg * kPageBytes, 16, 256, 6), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
         umma_commit(B(kBarPvDone + (j & 1)));  // = kBarEmptyV
+        last_bar = kBarPvDone + (j & 1);
+        last_par = (j >> 1) & 1;
       }
       __syncwarp();
       if (j + 2 < n_kt) {
@@ -492,11 +517,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         // does not order a later MMA's D writes after an earlier MMA's TMEM A
         // reads, so P V j must have completed first.
         wait_phase(B(kBarPvDone + (j & 1)), (j >> 1) & 1, dead);
+        if (dead) break;
         tc_fence_after();
         issue_s(j + 2);
       }
     }
-    // the last P V commit (waited for by the epilogue) covers every MMA issued here
+    // In a healthy run the last P V commit (waited for by the epilogue)
+    // covers every MMA issued here. After a wait gave up, nothing more was
+    // issued, and this warp waits (bounded) for its last commit so that no
+    // MMA still writes tensor memory when it is freed.
+    if (dead && last_bar >= 0) {
+      bool d2 = false;
+      wait_phase(B(last_bar), last_par, d2);
+    }
     tc_fence_before();
     __syncthreads();
     return;

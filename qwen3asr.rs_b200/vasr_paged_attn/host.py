@@ -13,7 +13,6 @@ from __future__ import annotations
 import importlib
 import sys
 from pathlib import Path
-from types import SimpleNamespace
 
 _LIB_DIR = Path(__file__).resolve().parent.parent / "lib"
 if str(_LIB_DIR) not in sys.path:
@@ -46,23 +45,3 @@ def metadata_cache(num_blocks: int, num_kv_heads: int, head_dim: int, block_size
     """A geometry-only PagedKvCache (no pages) for building host metadata of a pool."""
     return PagedKvCache.from_external([0], [0], num_blocks, num_kv_heads, head_dim, block_size, dtype)
 
-
-def golden_api() -> SimpleNamespace:
-    """Adapter used by tests/test_oracle_golden.py (same shape as the oracle adapter)."""
-    return SimpleNamespace(
-        name="host",
-        new=lambda l, h, d, bs, mt, dt: PagedKvCache.new(l, h, d, bs, mt, dt),
-        new_batched=lambda l, h, d, bs, b, mt, dt: PagedKvCache.new_batched(l, h, d, bs, b, mt, dt),
-        new_pool=lambda l, h, d, bs, nb, dt: PagedKvCache.new_pool(l, h, d, bs, nb, dt),
-        BlockManager=PagedBlockManager,
-        bytes_per_paged_block=bytes_per_paged_block,
-        blocks_for_byte_budget=blocks_for_byte_budget,
-        cuda_graph_batch_bucket=cuda_graph_batch_bucket,
-        cuda_graph_batch_buckets=cuda_graph_batch_buckets,
-        bucket_block_table_cols=bucket_block_table_cols,
-        pad_decode_batch_to_max=pad_decode_batch_to_max,
-        can_admit=can_admit_with_projected_kv,
-        allocatable_block_capacity=PagedBlockManager.allocatable_block_capacity,
-        graph_key=DecodeGraphRegistry,
-        Error=VasrHostError,
-    )

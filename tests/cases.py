@@ -16,11 +16,25 @@ from vasr_paged_attn.workloads import config3_rounds, loguniform_lens, uniform_l
 
 F32_SENTINEL = np.uint32(0x7FC0DEAD)  # a quiet NaN
 BF16_SENTINEL = np.uint16(0x7FC1)     # a quiet NaN
+F16_SENTINEL = np.uint16(0x7E5A)      # a quiet NaN
+
+
+def sentinel_for(dtype: str):
+    return {"f32": F32_SENTINEL, "bf16": BF16_SENTINEL, "f16": F16_SENTINEL}[dtype]
+
+
+def bits_to_f32(bits: np.ndarray, dtype: str) -> np.ndarray:
+    """Raw element bits (u32 for f32, u16 for bf16 / f16) -> f32 values."""
+    if dtype == "f32":
+        return bits.view(np.float32)
+    if dtype == "f16":
+        return np.ascontiguousarray(bits).view(np.float16).astype(np.float32)
+    return ref.bf16_bits_to_f32(bits)
 
 
 @dataclass
 class PagedCase:
-    dtype: str            # "f32" or "bf16"
+    dtype: str            # "f32", "bf16" or "f16"
     num_heads: int
     num_kv_heads: int
     head_dim: int
@@ -40,14 +54,14 @@ class PagedCase:
         return np.uint32 if self.dtype == "f32" else np.uint16
 
     def as_f32(self, bits: np.ndarray) -> np.ndarray:
-        if self.dtype == "f32":
-            return bits.view(np.float32)
-        return ref.bf16_bits_to_f32(bits)
+        return bits_to_f32(bits, self.dtype)
 
 
 def _to_bits(x: np.ndarray, dtype: str) -> np.ndarray:
     if dtype == "f32":
         return np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    if dtype == "f16":
+        return np.ascontiguousarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
     return ref.f32_to_bf16_bits(x)
 
 
@@ -76,7 +90,7 @@ def make_decode_case(seed: int, cached_lens, dtype="f32", num_heads=16, num_kv_h
     lens_blocks = [int(-(-c // block_size)) for c in ctx]
     tables = disjoint_block_tables(rng, lens_blocks, num_blocks, cols)
     x = 16 // (4 if dtype == "f32" else 2)
-    sentinel = F32_SENTINEL if dtype == "f32" else BF16_SENTINEL
+    sentinel = sentinel_for(dtype)
     kc = np.full((num_blocks, num_kv_heads, head_dim // x, block_size, x), sentinel)
     vc = np.full((num_blocks, num_kv_heads, head_dim, block_size), sentinel)
     # cached tokens, written with the oracle's scatter
@@ -129,10 +143,6 @@ def config1_case() -> PagedCase:
     return make_decode_case(0, CONFIG1_CACHED, dtype="f32", num_blocks=512)
 
 
-
-
-
-
 @dataclass
 class PrefillCase:
     dtype: str
@@ -148,7 +158,7 @@ class PrefillCase:
     q: np.ndarray                 # raw bits [sum chunk, Hq, D]
 
     def as_f32(self, bits):
-        return bits.view(np.float32) if self.dtype == "f32" else ref.bf16_bits_to_f32(bits)
+        return bits_to_f32(bits, self.dtype)
 
 
 def make_prefill_case(seed, cached, chunk, dtype="bf16", num_heads=16, num_kv_heads=8, head_dim=128,
@@ -164,7 +174,7 @@ def make_prefill_case(seed, cached, chunk, dtype="bf16", num_heads=16, num_kv_he
         num_blocks = sum(lens_blocks) + 8
     tables = disjoint_block_tables(rng, lens_blocks, num_blocks, cols)
     x = 16 // (4 if dtype == "f32" else 2)
-    sentinel = F32_SENTINEL if dtype == "f32" else BF16_SENTINEL
+    sentinel = sentinel_for(dtype)
     kc = np.full((num_blocks, num_kv_heads, head_dim // x, block_size, x), sentinel)
     vc = np.full((num_blocks, num_kv_heads, head_dim, block_size), sentinel)
     for i, n in enumerate(ctx):

@@ -131,7 +131,7 @@ def test_decode_step_prepare_slots_match_reference_metadata(cuda_device):
     """Without EOS the prepared metadata equals decode_metadata_for_batch_step of the host mirror."""
     from vasr_paged_attn import host as vh
     g_tables, g_prompt = [[3, 4], [6, 7]], [4, 5]  # paged_kv_cache.rs:1316-1376 golden case
-    cache = vh.golden_api().new_pool(1, 2, 8, 4, 16, "f32")
+    cache = vh.PagedKvCache.new_pool(1, 2, 8, 4, 16, "f32")
     t = torch.tensor([r + [0] * 2 for r in g_tables], dtype=torch.int32)
     st = dl.DecodeLoopState(g_prompt, [100, 101], [0], t.to(cuda_device), [2, 2], 4, 16, 200,
                             device=cuda_device)

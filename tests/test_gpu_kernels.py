@@ -191,7 +191,7 @@ def test_decode_config2_shapes_bf16(cuda_device):
 
 
 def test_decode_more_than_1024_sequences(cuda_device):
-    """Above 1024 sequences the grid kernel (one CTA per split) runs instead of the persistent one."""
+    """More than 1024 sequences (a wide grid of split CTAs; the merge counters per (sequence, kv head))."""
     lens = uniform_lens(3, 1100, 1, 60) - 1
     case = make_decode_case(3, lens, dtype="bf16", num_blocks=1100 * 4 + 8)
     t = upload(case, cuda_device)
@@ -202,7 +202,7 @@ def test_decode_more_than_1024_sequences(cuda_device):
 
 
 def test_decode_persistent_many_items_per_cta(cuda_device):
-    """Long bound with short true contexts: many (sequence, head, split) items per CTA."""
+    """Long bound with short true contexts: most splits of the bound are empty and exit at once."""
     lens = loguniform_lens(4, 300, 1, 3000) - 1
     case = make_decode_case(4, np.maximum(lens, 0), dtype="bf16",
                             num_blocks=int(np.maximum(lens, 0).sum() // 16 + 320))

@@ -41,10 +41,31 @@ def _oracle_api():
     )
 
 
-def _host_api():
+def host_golden_api():
+    """The C++ host mirror behind the same adapter shape as the oracle's."""
     from vasr_paged_attn import host  # C++ mirror; raises if the module is missing
 
-    return host.golden_api()
+    return SimpleNamespace(
+        name="host",
+        new=lambda l, h, d, bs, mt, dt: host.PagedKvCache.new(l, h, d, bs, mt, dt),
+        new_batched=lambda l, h, d, bs, b, mt, dt: host.PagedKvCache.new_batched(l, h, d, bs, b, mt, dt),
+        new_pool=lambda l, h, d, bs, nb, dt: host.PagedKvCache.new_pool(l, h, d, bs, nb, dt),
+        BlockManager=host.PagedBlockManager,
+        bytes_per_paged_block=host.bytes_per_paged_block,
+        blocks_for_byte_budget=host.blocks_for_byte_budget,
+        cuda_graph_batch_bucket=host.cuda_graph_batch_bucket,
+        cuda_graph_batch_buckets=host.cuda_graph_batch_buckets,
+        bucket_block_table_cols=host.bucket_block_table_cols,
+        pad_decode_batch_to_max=host.pad_decode_batch_to_max,
+        can_admit=host.can_admit_with_projected_kv,
+        allocatable_block_capacity=host.PagedBlockManager.allocatable_block_capacity,
+        graph_key=host.DecodeGraphRegistry,
+        Error=host.VasrHostError,
+    )
+
+
+def _host_api():
+    return host_golden_api()
 
 
 def _apis():
