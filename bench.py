@@ -87,6 +87,8 @@ def parse_args(argv=None):
     p.add_argument("--iters", type=int, default=20, help="timed launches per kernel microbenchmark")
     p.add_argument("--layers", type=int, default=28,
                    help="distinct per-layer caches cycled through by --kernel decode/copy")
+    p.add_argument("--pool-blocks", type=int, default=200_000,
+                   help="blocks per layer pool of --kernel copy (config 4: 200k; smaller for profiling)")
     args = p.parse_args(argv)
     if args.steps is None:
         args.steps = 64 if args.config == 5 else 100
@@ -912,6 +914,7 @@ def kb_prefill(args, dev, fp8=False):
         pools = _pool(dev, nb, nset, torch.bfloat16)
     t_all = _tables(rng, lens, nb)
     total_flops, total_ms = 0.0, 0.0
+    rounds_us = []
     for r in rounds:
         idx = [i for (i, _, _) in r]
         chunk = np.array([n for (_, _, n) in r])
@@ -928,12 +931,14 @@ def kb_prefill(args, dev, fp8=False):
         vis = sum(sum(int(s) + j + 1 for j in range(int(n))) for (_, s, n) in r)
         total_flops += 4.0 * D * HQ * vis
         total_ms += ms
+        rounds_us.append(round(ms * 1e3, 2))
     tflops = total_flops / (total_ms / 1e3) / 1e12
     tpeak, tkind = load_tensor_peak()
     return [{"kernel": "paged_prefill_varlen" + ("_fp8" if fp8 else ""),
              "config": "config3 (one layer, all chunk rounds)", "rounds": len(rounds),
              "us": total_ms * 1e3, "flops": total_flops, "achieved": tflops, "unit": "TFLOP/s",
              "peak": tpeak, "frac": tflops / tpeak, "peak_source": tkind, "input_sets_cycled": nset,
+             "rounds_us": rounds_us,
              "tflop_28_layers": total_flops * 28 / 1e12}]
 
 
@@ -946,7 +951,7 @@ def kb_copy(args, dev):
 
     rng = np.random.default_rng(args.seed)
     free, _ = torch.cuda.mem_get_info()
-    nb = 200_000
+    nb = args.pool_blocks
     per_layer = nb * HKV * D * BLOCK_SIZE * 2 * 2
     layers = max(1, min(args.layers, int(free * 0.8 // per_layer)))
     caches = [(torch.empty(nb, HKV, D // 8, BLOCK_SIZE, 8, dtype=torch.bfloat16, device=dev),
@@ -956,7 +961,8 @@ def kb_copy(args, dev):
     ms = _events_time(lambda i: pa.copy_blocks([c[0] for c in caches], [c[1] for c in caches], pairs),
                       args.iters)
     alg = 4096 * layers * 2 * (HKV * D * BLOCK_SIZE * 2) * 2
-    return [_hbm_line("copy_blocks", "config4", ms, alg, layers_allocated=layers,
+    return [_hbm_line("copy_blocks", "config4" if nb == 200_000 else f"config4 pairs, {nb}-block pools", ms, alg,
+                      layers_allocated=layers,
                       ms_28_layers_extrapolated=ms * 28 / layers)]
 
 

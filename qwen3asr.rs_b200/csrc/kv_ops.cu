@@ -611,25 +611,66 @@ struct AppendFp8Params {
   int row_pitch;  // bytes of one staged token row (one byte per element) + 16
 };
 
+// Two quotients x / s rounded to E4M3 (nearest even, saturating at 448), byte
+// for byte what converting the IEEE quotient RN_f32(x / s) gives, without a
+// division in the common case. With inv = RN(1 / s), t = RN(x * inv) lies
+// within 2.5 steps of the f32 grid of RN(x / s) (each of the two roundings
+// adds at most 2^-24 relative error; 5 steps if t falls into the binade
+// below). The conversion to E4M3 is monotonic in the magnitude, so when the
+// magnitudes kQuantWin steps below and above |t| convert to the same byte, so
+// does |RN(x / s)|, and the sign is that of t (= sign(x) xor sign(s), zeros
+// included). Otherwise — a quotient within kQuantWin steps of an E4M3
+// rounding boundary, about 16 in 2^20 values of a binade, or a non-finite,
+// huge or tiny operand — the pair takes the IEEE division.
+constexpr uint32_t kQuantWin = 8;
+
+__device__ __forceinline__ uint32_t e4m3x2_quotients(float x0, float x1, float s, float inv,
+                                                     bool fast) {
+  const float t0 = x0 * inv, t1 = x1 * inv;
+  const uint32_t a0 = __float_as_uint(t0) & 0x7fffffffu, a1 = __float_as_uint(t1) & 0x7fffffffu;
+  if (fast && a0 < 0x7f000000u && a1 < 0x7f000000u) {
+    const float l0 = __uint_as_float(a0 > kQuantWin ? a0 - kQuantWin : 0u);
+    const float l1 = __uint_as_float(a1 > kQuantWin ? a1 - kQuantWin : 0u);
+    const __nv_fp8x2_storage_t lo =
+        __nv_cvt_float2_to_fp8x2(make_float2(l0, l1), __NV_SATFINITE, __NV_E4M3);
+    const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+        make_float2(__uint_as_float(a0 + kQuantWin), __uint_as_float(a1 + kQuantWin)), __NV_SATFINITE,
+        __NV_E4M3);
+    if (lo == hi)
+      return (uint32_t)lo | ((__float_as_uint(t0) >> 24) & 0x80u) | ((__float_as_uint(t1) >> 16) & 0x8000u);
+  }
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(x0, s), __fdiv_rn(x1, s)),
+                                            __NV_SATFINITE, __NV_E4M3);
+}
+
+// The reciprocal the fast path multiplies by, and whether that path applies:
+// a normal, finite 1 / s keeps the error bound above.
+struct QuantScale {
+  float s, inv;
+  bool fast;
+};
+__device__ __forceinline__ QuantScale quant_scale(float s) {
+  const float inv = __frcp_rn(s);
+  const uint32_t e = __float_as_uint(inv) & 0x7f800000u;
+  return {s, inv, e != 0u && e != 0x7f800000u};
+}
+
 // 16 source elements at src (16-byte aligned) -> 16 E4M3 bytes of x / scale.
 template <typename T>
-__device__ __forceinline__ uint4 quantize16(const unsigned char *src, float scale) {
+__device__ __forceinline__ uint4 quantize16(const unsigned char *src, const QuantScale &q) {
   constexpr int kPer = Elem<T>::kX;  // elements per 16-byte load
   float f[16];
 #pragma unroll
-  for (int q = 0; q < 16 / kPer; ++q) {
+  for (int c = 0; c < 16 / kPer; ++c) {
     float g[kPer];
-    unpack_chunk<T>(__ldg(reinterpret_cast<const uint4 *>(src) + q), g);
+    unpack_chunk<T>(__ldg(reinterpret_cast<const uint4 *>(src) + c), g);
 #pragma unroll
-    for (int e = 0; e < kPer; ++e) f[q * kPer + e] = g[e];
+    for (int e = 0; e < kPer; ++e) f[c * kPer + e] = g[e];
   }
   uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const __nv_fp8x2_storage_t pr = __nv_cvt_float2_to_fp8x2(
-        make_float2(__fdiv_rn(f[2 * i], scale), __fdiv_rn(f[2 * i + 1], scale)), __NV_SATFINITE, __NV_E4M3);
-    w[i >> 1] |= (uint32_t)pr << (16 * (i & 1));
-  }
+  for (int i = 0; i < 8; ++i)
+    w[i >> 1] |= e4m3x2_quotients(f[2 * i], f[2 * i + 1], q.s, q.inv, q.fast) << (16 * (i & 1));
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -654,7 +695,7 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
   const int ntok = (int)min((int64_t)TT, p.num_tokens - t0);
   const int64_t max_slot = p.num_blocks * BS;
   const int tid = threadIdx.x;
-  const float ks = __ldg(p.k_scale), vs = __ldg(p.v_scale);
+  const QuantScale ks = quant_scale(__ldg(p.k_scale)), vs = quant_scale(__ldg(p.v_scale));
 
   if (tid < ntok) {
     int64_t s = p.slots[t0 + tid];
@@ -761,17 +802,20 @@ __global__ void __launch_bounds__(128) kv_append_fp8_token_kernel(const AppendFp
     if (lane == 0) raise_device_error(VASR_PA_DERR_SLOT_RANGE);
     return;
   }
-  const float ks = __ldg(p.k_scale), vs = __ldg(p.v_scale);
+  const QuantScale ks = quant_scale(__ldg(p.k_scale)), vs = quant_scale(__ldg(p.v_scale));
   const unsigned char *k = p.key + t * p.k_stride_bytes + (int64_t)h * D * sizeof(T);
   const T *v = reinterpret_cast<const T *>(p.value + t * p.v_stride_bytes) + (int64_t)h * D;
   const int64_t page = (int64_t)blk * p.num_kv_heads + h;
   if (lane < D / 16)
     *reinterpret_cast<uint4 *>(p.k_cache + ((page * (D / 16) + lane) * BS + off) * 16) =
         quantize16<T>(k + lane * 16 * sizeof(T), ks);
+  // lane covers dims lane and lane + 32 (a pair), then lane + 64 and lane + 96
 #pragma unroll
-  for (int d = lane; d < D; d += 32) {
-    const float x = __fdiv_rn(Elem<T>::to_f32(v[d]), vs);
-    p.v_cache[(page * D + d) * BS + off] = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  for (int d = lane; d < D; d += 64) {
+    const uint32_t pr = e4m3x2_quotients(Elem<T>::to_f32(v[d]), Elem<T>::to_f32(v[d + 32]), vs.s, vs.inv,
+                                         vs.fast);
+    p.v_cache[(page * D + d) * BS + off] = (unsigned char)(pr & 0xffu);
+    p.v_cache[(page * D + d + 32) * BS + off] = (unsigned char)(pr >> 8);
   }
 }
 

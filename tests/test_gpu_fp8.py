@@ -212,3 +212,29 @@ def test_fp8_prefill_matches_oracle(cuda_device, bs):
                              np.ascontiguousarray(tables.astype(np.uint32)), ctx.astype(np.uint32),
                              cu.astype(np.uint32), D ** -0.5)
     assert np.abs(out - exp).max() <= 2e-2
+
+
+@pytest.mark.parametrize("t", [64, 4160])  # a warp per (token, head) / 16-token tiles
+@pytest.mark.parametrize("src", [torch.bfloat16, torch.float16])
+def test_fp8_append_every_16bit_input_is_byte_exact(cuda_device, src, t):
+    """Every non-NaN bf16 / f16 bit pattern, for several scales, against the oracle's encoder of
+    the IEEE quotient: the append's division-free rounding must not move a single byte."""
+    bits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    vals = torch.from_numpy(bits.view(np.int16).copy()).view(src).float().numpy()
+    bits = np.where(np.isnan(vals), np.uint16(0), bits)  # NaN payloads need not match
+    reps = t * HKV * D // (1 << 16)
+    flat = np.concatenate([np.roll(bits, 4099 * i) for i in range(reps)])
+    x = torch.from_numpy(flat.view(np.int16).copy()).view(src).reshape(t, HKV, D)
+    bs, nb = 16, t // 16 + 2
+    slots = np.arange(t, dtype=np.int64) + bs  # page-aligned runs from block 1
+    for ks in (0.05, 0.02, 1.0, 1.0 / 3.0, 7.3e-3, 3.7, 1e-30, 5e29):
+        kc, vc = _u8_cache(nb, bs, cuda_device)
+        sk, sv = _scales(cuda_device, ks, ks * 1.37)
+        pa.reshape_and_cache(x.to(cuda_device), x.to(cuda_device), sk, sv, kc.view(torch.float8_e4m3fn),
+                             vc.view(torch.float8_e4m3fn), torch.from_numpy(slots).to(cuda_device))
+        ek = np.full((nb, HKV, D // 16, bs, 16), SENTINEL, np.uint8)
+        ev = np.full((nb, HKV, D, bs), SENTINEL, np.uint8)
+        xf = x.float().numpy()
+        ref.reshape_and_cache_fp8(xf, xf, ek, ev, slots, bs, np.float32(ks), np.float32(ks * 1.37))
+        assert np.array_equal(kc.cpu().numpy(), ek), ks
+        assert np.array_equal(vc.cpu().numpy(), ev), ks
