@@ -62,7 +62,7 @@ METRIC = "decode tok/s & paged-attn KV-read GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 BATCH = 64
 CTX_LO, CTX_HI = 200, 1500
 BLOCK_SIZE = 16
-KERNELS = ["decode", "decode5", "decode_fp8", "append", "gather", "prefill", "prefill_fp8",
+KERNELS = ["decode", "decode5", "decode_fp8", "decode5_fp8", "append", "gather", "prefill", "prefill_fp8",
            "copy", "swap", "config1"]
 
 
@@ -789,17 +789,23 @@ def kb_decode(args, dev, which="decode"):
     return lines
 
 
-def kb_decode_fp8(args, dev):
-    """Config 2 shapes over fp8 (E4M3) pages with per-tensor scales (half the KV bytes)."""
+def kb_decode_fp8(args, dev, which="config2"):
+    """Config 2 (or config 5) shapes over fp8 (E4M3) pages with per-tensor scales (half the KV bytes)."""
     import numpy as np
     import torch
 
     from vasr_paged_attn import mistralrs_paged_attn as pa
 
     rng = np.random.default_rng(args.seed)
-    lens = context_lens(args.seed, 0)
+    if which == "config5":
+        from vasr_paged_attn.workloads import config5_context_lens
+
+        lens = config5_context_lens(args.seed)
+        layers = min(args.layers, 4)
+    else:
+        lens = context_lens(args.seed, 0)
+        layers = args.layers
     nb = sum(-(-int(n) // BLOCK_SIZE) for n in lens) + 1
-    layers = args.layers
     caches = [((torch.randn(nb, HKV, D // 16, BLOCK_SIZE, 16, device=dev) * 8).to(torch.float8_e4m3fn),
                (torch.randn(nb, HKV, D, BLOCK_SIZE, device=dev) * 8).to(torch.float8_e4m3fn))
               for _ in range(layers)]
@@ -816,7 +822,7 @@ def kb_decode_fp8(args, dev):
 
     ms = _events_time(launch, args.iters)
     alg = int(lens.sum()) * HKV * D * 2 + q.numel() * 2 * 2
-    return [_hbm_line("paged_decode_fp8", "config2 shapes, fp8 E4M3 pages", ms, alg, layers_cycled=layers)]
+    return [_hbm_line("paged_decode_fp8", f"{which} shapes, fp8 E4M3 pages", ms, alg, layers_cycled=layers)]
 
 
 def kb_append(args, dev):
@@ -1004,6 +1010,7 @@ KERNEL_BENCH = {
     "decode5": lambda a, d: kb_decode(a, d, "decode5"),
     "config1": lambda a, d: kb_decode(a, d, "config1"),
     "decode_fp8": kb_decode_fp8,
+    "decode5_fp8": lambda a, d: kb_decode_fp8(a, d, "config5"),
     "append": kb_append,
     "gather": kb_gather,
     "prefill": lambda a, d: kb_prefill(a, d, fp8=False),

@@ -151,6 +151,120 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(const AppendP
   }
 }
 
+// ---------------------------------------------- 16-token tiles (prefill)
+// Prefill-sized appends: a CTA owns 16 consecutive tokens x HPT heads (512
+// bytes of each token row). Every tile shape is a compile-time constant, so
+// all index math is shifts and masks. Warp 0 reads the 16 slots and sorts the
+// tokens into V groups of kTPS tokens (one 16-byte vector of a page row): a
+// group whose slots are consecutive and start on a kTPS boundary leaves as
+// one vector store per (head, dim); any other group (pads, a page change
+// inside it, an unaligned start) stores its tokens element by element. K
+// leaves as 16-byte chunks (16 bytes of one token's row), token fastest, so
+// the tile's chunks of one page row form contiguous runs.
+constexpr int kTile16 = 16;
+
+// Warp 0: the tile's slots into s_slot (out of range -> skipped and flagged)
+// and, per V group of kTPS tokens, whether it is one aligned run of slots.
+template <int BS, int kTPS, int kGroups>
+__device__ __forceinline__ void tile16_slots(const int64_t *slots, int64_t t0, int ntok, int64_t num_blocks,
+                                             int64_t *s_slot, int *s_gok) {
+  const int lane = threadIdx.x;
+  int64_t sl = -1;
+  if (lane < ntok) {
+    sl = slots[t0 + lane];
+    if (sl >= num_blocks * BS) {
+      raise_device_error(VASR_PA_DERR_SLOT_RANGE);
+      sl = -1;
+    }
+  }
+  if (lane < kTile16) s_slot[lane] = sl;
+  const int g0 = lane & ~(kTPS - 1);
+  const int64_t first = __shfl_sync(0xffffffffu, sl, g0);
+  const bool ok = lane < kTile16 && sl >= 0 && (first & (kTPS - 1)) == 0 && sl == first + (lane - g0);
+  const uint32_t ball = __ballot_sync(0xffffffffu, ok);
+  constexpr uint32_t kAll = (1u << kTPS) - 1u;
+  if (lane < kGroups) s_gok[lane] = ((ball >> (lane * kTPS)) & kAll) == kAll;
+}
+
+template <typename T, int BS, int D, int HPT>
+__global__ void __launch_bounds__(kAppendThreads) kv_append_tile16_kernel(const AppendParams p) {
+  constexpr int kES = (int)sizeof(T);
+  constexpr int kX = 16 / kES;                     // elements per 16-byte chunk
+  constexpr int kCH = D / kX;                      // chunks per (token, head)
+  constexpr int kRow = HPT * kCH;                  // chunks per staged token row
+  constexpr int kPitch = HPT * D * kES + 16;       // staged row bytes (+16 spreads banks)
+  constexpr int kTPS = kX;                         // tokens per V vector
+  constexpr int kGroups = kTile16 / kTPS;
+  constexpr int kChunks = kTile16 * kRow;
+  constexpr int kVItems = HPT * D * kGroups;
+  static_assert(kTPS <= BS, "a V vector stays inside one page row");
+  static_assert((kRow & (kRow - 1)) == 0 && (kCH & (kCH - 1)) == 0, "power-of-two tile shapes");
+  __shared__ __align__(16) unsigned char kt[kTile16 * kPitch];
+  __shared__ __align__(16) unsigned char vt[kTile16 * kPitch];
+  __shared__ int64_t s_slot[kTile16];
+  __shared__ int s_gok[kGroups];
+  const int tid = threadIdx.x;
+  const int64_t t0 = (int64_t)blockIdx.x * kTile16;
+  const int h0 = blockIdx.y * HPT;
+  const int HC = min(HPT, p.num_kv_heads - h0);
+  const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
+  if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
+#pragma unroll
+  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+    const int i = tid + k * kAppendThreads;
+    const int tt = i / kRow, r = i % kRow;
+    if (i < kChunks && tt < ntok && r / kCH < HC) {
+      const int64_t col = (int64_t)h0 * D * kES + r * 16;
+      const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(p.key + (t0 + tt) * p.k_stride_bytes + col));
+      const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(p.value + (t0 + tt) * p.v_stride_bytes + col));
+      *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) = kv;
+      *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) = vv;
+    }
+  }
+  __syncthreads();
+  // K: item i = (chunk r of the row, token tt), token fastest
+#pragma unroll
+  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+    const int i = tid + k * kAppendThreads;
+    const int tt = i % kTile16, r = i / kTile16;
+    const int hc = r / kCH, c = r % kCH;
+    const int64_t sl = s_slot[tt];
+    if (i < kChunks && sl >= 0 && hc < HC) {
+      const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
+      const uint64_t dst = (((blk * (uint64_t)p.num_kv_heads + (uint64_t)(h0 + hc)) * kCH + c) * BS + off) * 16;
+      *reinterpret_cast<uint4 *>(p.k_cache + dst) = *reinterpret_cast<const uint4 *>(kt + tt * kPitch + r * 16);
+    }
+  }
+  // V: item i = (group g, dim d of head hc), group fastest: consecutive
+  // threads fill consecutive 16-byte pieces of the page rows
+#pragma unroll
+  for (int k = 0; k < (kVItems + kAppendThreads - 1) / kAppendThreads; ++k) {
+    const int i = tid + k * kAppendThreads;
+    const int g = i % kGroups, hd = i / kGroups;
+    const int hc = hd / D, d = hd % D;
+    if (i >= kVItems || hc >= HC) continue;
+    const unsigned char *src = vt + (g * kTPS) * kPitch + (hc * D + d) * kES;
+    const uint64_t row = ((uint64_t)h0 + hc) * D + d;  // page row of (head, dim) within a block
+    if (s_gok[g]) {
+      const uint64_t us = (uint64_t)s_slot[g * kTPS], blk = us / BS, off = us % BS;
+      T vals[kTPS];
+#pragma unroll
+      for (int e = 0; e < kTPS; ++e) vals[e] = *reinterpret_cast<const T *>(src + e * kPitch);
+      T *dst = reinterpret_cast<T *>(p.v_cache) + (blk * (uint64_t)p.num_kv_heads * D + row) * BS + off;
+      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(vals);
+    } else {
+#pragma unroll
+      for (int e = 0; e < kTPS; ++e) {
+        const int64_t sl = s_slot[g * kTPS + e];
+        if (sl < 0) continue;
+        const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
+        reinterpret_cast<T *>(p.v_cache)[(blk * (uint64_t)p.num_kv_heads * D + row) * BS + off] =
+            *reinterpret_cast<const T *>(src + e * kPitch);
+      }
+    }
+  }
+}
+
 template <typename T, int BS, int D>
 int launch_append_t(const AppendArgs &a, cudaStream_t stream) {
   AppendParams p{};
@@ -165,14 +279,20 @@ int launch_append_t(const AppendArgs &a, cudaStream_t stream) {
   p.num_blocks = a.num_blocks;
   p.num_kv_heads = a.num_kv_heads;
   // Decode-sized calls (one token per page) get one token per CTA for
-  // parallelism; mid-sized calls 8-token tiles of up to 2 KB of heads;
-  // prefill chunks (>= 4096 tokens) 16-token tiles of 512 bytes of heads, so
-  // one CTA writes whole 32-byte V page rows and small tiles keep many CTAs
-  // resident (8192-token chunk, inputs cycled beyond L2: 15.4 us against
-  // 18.6 us for 8 x 2 KB tiles and 23.8 us for 16 x 2 KB tiles). Shared
-  // memory is sized to the tile.
-  const int tt = a.num_tokens >= 4096 ? 16 : (a.num_tokens >= 128 ? 8 : 1);
-  const int row_bytes = tt == 16 ? 512 : kAppendRowBytes;
+  // parallelism; mid-sized calls 8-token tiles of up to 2 KB of heads, with
+  // shared memory sized to the tile; prefill chunks (>= 4096 tokens) the
+  // compile-time 16-token tiles of 512 bytes of heads above, so one CTA
+  // writes whole 32-byte V page rows and small tiles keep many CTAs resident.
+  if (a.num_tokens >= 4096) {  // prefill chunks: 16-token tiles of 512 bytes of heads
+    constexpr int kHPT = 512 / (D * (int)sizeof(T)) > 0 ? 512 / (D * (int)sizeof(T)) : 1;
+    const int64_t tiles = (a.num_tokens + kTile16 - 1) / kTile16;
+    if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+    dim3 grid((unsigned)tiles, (unsigned)((a.num_kv_heads + kHPT - 1) / kHPT));
+    kv_append_tile16_kernel<T, BS, D, kHPT><<<grid, kAppendThreads, 0, stream>>>(p);
+    return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+  }
+  const int tt = a.num_tokens >= 128 ? 8 : 1;
+  const int row_bytes = kAppendRowBytes;
   p.tile_tokens = tt;
   p.heads_per_tile = row_bytes / (D * (int)sizeof(T)) > 0 ? row_bytes / (D * (int)sizeof(T)) : 1;
   p.row_pitch = p.heads_per_tile * D * (int)sizeof(T) + 16;
@@ -611,48 +731,36 @@ struct AppendFp8Params {
   int row_pitch;  // bytes of one staged token row (one byte per element) + 16
 };
 
-// Two quotients x / s rounded to E4M3 (nearest even, saturating at 448), byte
-// for byte what converting the IEEE quotient RN_f32(x / s) gives, without a
-// division in the common case. With inv = RN(1 / s), t = RN(x * inv) lies
-// within 2.5 steps of the f32 grid of RN(x / s) (each of the two roundings
-// adds at most 2^-24 relative error; 5 steps if t falls into the binade
-// below). The conversion to E4M3 is monotonic in the magnitude, so when the
-// magnitudes kQuantWin steps below and above |t| convert to the same byte, so
-// does |RN(x / s)|, and the sign is that of t (= sign(x) xor sign(s), zeros
-// included). Otherwise — a quotient within kQuantWin steps of an E4M3
-// rounding boundary, about 16 in 2^20 values of a binade, or a non-finite,
-// huge or tiny operand — the pair takes the IEEE division.
-constexpr uint32_t kQuantWin = 8;
-
-__device__ __forceinline__ uint32_t e4m3x2_quotients(float x0, float x1, float s, float inv,
-                                                     bool fast) {
-  const float t0 = x0 * inv, t1 = x1 * inv;
-  const uint32_t a0 = __float_as_uint(t0) & 0x7fffffffu, a1 = __float_as_uint(t1) & 0x7fffffffu;
-  if (fast && a0 < 0x7f000000u && a1 < 0x7f000000u) {
-    const float l0 = __uint_as_float(a0 > kQuantWin ? a0 - kQuantWin : 0u);
-    const float l1 = __uint_as_float(a1 > kQuantWin ? a1 - kQuantWin : 0u);
-    const __nv_fp8x2_storage_t lo =
-        __nv_cvt_float2_to_fp8x2(make_float2(l0, l1), __NV_SATFINITE, __NV_E4M3);
-    const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
-        make_float2(__uint_as_float(a0 + kQuantWin), __uint_as_float(a1 + kQuantWin)), __NV_SATFINITE,
-        __NV_E4M3);
-    if (lo == hi)
-      return (uint32_t)lo | ((__float_as_uint(t0) >> 24) & 0x80u) | ((__float_as_uint(t1) >> 16) & 0x8000u);
-  }
-  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(x0, s), __fdiv_rn(x1, s)),
-                                            __NV_SATFINITE, __NV_E4M3);
-}
-
-// The reciprocal the fast path multiplies by, and whether that path applies:
-// a normal, finite 1 / s keeps the error bound above.
+// The quotient x / s as the IEEE division rounds it, RN(x / s), from a
+// multiply by inv = RN(1 / s) and one correction step: Markstein's theorem
+// (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990): when y is within
+// half an ulp of 1 / b and q within one ulp of a / b, the remainder
+// r = a - b q is exact (one fma) and RN(q + r y) = RN(a / b). Here t = RN(x
+// inv) is within one ulp of x / s. Outside the range where those conditions
+// hold (s or inv not normal, |x| small enough for r to underflow, |t| large
+// enough for t s to overflow) the IEEE division runs instead; a |t| below
+// 2^-12 converts to a signed E4M3 zero whatever its last bits, so t stands.
 struct QuantScale {
   float s, inv;
   bool fast;
 };
 __device__ __forceinline__ QuantScale quant_scale(float s) {
   const float inv = __frcp_rn(s);
-  const uint32_t e = __float_as_uint(inv) & 0x7f800000u;
-  return {s, inv, e != 0u && e != 0x7f800000u};
+  const uint32_t ei = __float_as_uint(inv) & 0x7f800000u, es = __float_as_uint(s) & 0x7f800000u;
+  return {s, inv, ei != 0u && ei != 0x7f800000u && es != 0u && es != 0x7f800000u};
+}
+__device__ __forceinline__ float quotient_rn(float x, const QuantScale &q) {
+  const float t = x * q.inv;
+  const float at = fabsf(t);
+  if (at < 0x1p-12f) return t;
+  if (q.fast && at < 0x1p100f && fabsf(x) >= 0x1p-90f) return fmaf(fmaf(-t, q.s, x), q.inv, t);
+  return __fdiv_rn(x, q.s);
+}
+// Two quotients -> two E4M3 bytes (nearest even, saturating at 448), x0 low.
+__device__ __forceinline__ uint32_t e4m3x2_quotients(float x0, float x1, const QuantScale &q) {
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(quotient_rn(x0, q), quotient_rn(x1, q)),
+                                            __NV_SATFINITE, __NV_E4M3);
 }
 
 // 16 source elements at src (16-byte aligned) -> 16 E4M3 bytes of x / scale.
@@ -670,7 +778,7 @@ __device__ __forceinline__ uint4 quantize16(const unsigned char *src, const Quan
   uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    w[i >> 1] |= e4m3x2_quotients(f[2 * i], f[2 * i + 1], q.s, q.inv, q.fast) << (16 * (i & 1));
+    w[i >> 1] |= e4m3x2_quotients(f[2 * i], f[2 * i + 1], q) << (16 * (i & 1));
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -784,6 +892,89 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
   }
 }
 
+// Prefill-sized fp8 appends: the 16-token tiles of kv_append_tile16_kernel
+// with HPT heads per tile, quantised while staging (one byte per element).
+// V groups hold kTPS = min(16, BS) tokens: one 16-byte (8-byte at BS 8)
+// vector of a page row.
+template <typename T, int BS, int D, int HPT>
+__global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_tile16_kernel(const AppendFp8Params p) {
+  constexpr int kES = (int)sizeof(T);
+  constexpr int kCH = D / 16;                      // 16-element chunks per (token, head)
+  constexpr int kRow = HPT * kCH;                  // chunks per staged token row
+  constexpr int kPitch = HPT * D + 16;             // staged row bytes
+  constexpr int kTPS = BS < 16 ? BS : 16;          // tokens per V vector
+  constexpr int kGroups = kTile16 / kTPS;
+  constexpr int kChunks = kTile16 * kRow;
+  constexpr int kVItems = HPT * D * kGroups;
+  static_assert((kRow & (kRow - 1)) == 0 && (kCH & (kCH - 1)) == 0, "power-of-two tile shapes");
+  __shared__ __align__(16) unsigned char kt[kTile16 * kPitch];
+  __shared__ __align__(16) unsigned char vt[kTile16 * kPitch];
+  __shared__ int64_t s_slot[kTile16];
+  __shared__ int s_gok[kGroups];
+  const int tid = threadIdx.x;
+  const int64_t t0 = (int64_t)blockIdx.x * kTile16;
+  const int h0 = blockIdx.y * HPT;
+  const int HC = min(HPT, p.num_kv_heads - h0);
+  const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
+  const QuantScale ks = quant_scale(__ldg(p.k_scale)), vs = quant_scale(__ldg(p.v_scale));
+  if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
+#pragma unroll
+  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+    const int i = tid + k * kAppendThreads;
+    const int tt = i / kRow, r = i % kRow;
+    if (i < kChunks && tt < ntok && r / kCH < HC) {
+      const int64_t col = ((int64_t)h0 * D + (int64_t)r * 16) * kES;
+      *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) =
+          quantize16<T>(p.key + (t0 + tt) * p.k_stride_bytes + col, ks);
+      *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) =
+          quantize16<T>(p.value + (t0 + tt) * p.v_stride_bytes + col, vs);
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+    const int i = tid + k * kAppendThreads;
+    const int tt = i % kTile16, r = i / kTile16;
+    const int hc = r / kCH, c = r % kCH;
+    const int64_t sl = s_slot[tt];
+    if (i < kChunks && sl >= 0 && hc < HC) {
+      const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
+      const uint64_t dst = (((blk * (uint64_t)p.num_kv_heads + (uint64_t)(h0 + hc)) * kCH + c) * BS + off) * 16;
+      *reinterpret_cast<uint4 *>(p.k_cache + dst) = *reinterpret_cast<const uint4 *>(kt + tt * kPitch + r * 16);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < (kVItems + kAppendThreads - 1) / kAppendThreads; ++k) {
+    const int i = tid + k * kAppendThreads;
+    const int g = i % kGroups, hd = i / kGroups;
+    const int hc = hd / D, d = hd % D;
+    if (i >= kVItems || hc >= HC) continue;
+    const unsigned char *src = vt + (g * kTPS) * kPitch + hc * D + d;
+    const uint64_t row = ((uint64_t)h0 + hc) * D + d;
+    if (s_gok[g]) {
+      const uint64_t us = (uint64_t)s_slot[g * kTPS], blk = us / BS, off = us % BS;
+      uint32_t w[kTPS / 4];
+#pragma unroll
+      for (int q = 0; q < kTPS / 4; ++q)
+        w[q] = (uint32_t)src[(4 * q) * kPitch] | ((uint32_t)src[(4 * q + 1) * kPitch] << 8) |
+               ((uint32_t)src[(4 * q + 2) * kPitch] << 16) | ((uint32_t)src[(4 * q + 3) * kPitch] << 24);
+      unsigned char *dst = p.v_cache + (blk * (uint64_t)p.num_kv_heads * D + row) * BS + off;
+      if constexpr (kTPS == 16)
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      else
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < kTPS; ++e) {
+        const int64_t sl = s_slot[g * kTPS + e];
+        if (sl < 0) continue;
+        const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
+        p.v_cache[(blk * (uint64_t)p.num_kv_heads * D + row) * BS + off] = src[e * kPitch];
+      }
+    }
+  }
+}
+
 // Decode-sized fp8 appends (a few tokens, one per page row): one warp per
 // (token, kv head), K as 16-byte chunks (lane c < D / 16 writes chunk c), V
 // one byte per dim — the layout admits no wider V store for a lone token.
@@ -812,8 +1003,7 @@ __global__ void __launch_bounds__(128) kv_append_fp8_token_kernel(const AppendFp
   // lane covers dims lane and lane + 32 (a pair), then lane + 64 and lane + 96
 #pragma unroll
   for (int d = lane; d < D; d += 64) {
-    const uint32_t pr = e4m3x2_quotients(Elem<T>::to_f32(v[d]), Elem<T>::to_f32(v[d + 32]), vs.s, vs.inv,
-                                         vs.fast);
+    const uint32_t pr = e4m3x2_quotients(Elem<T>::to_f32(v[d]), Elem<T>::to_f32(v[d + 32]), vs);
     p.v_cache[(page * D + d) * BS + off] = (unsigned char)(pr & 0xffu);
     p.v_cache[(page * D + d + 32) * BS + off] = (unsigned char)(pr >> 8);
   }
@@ -840,12 +1030,16 @@ int launch_append_fp8_t(const AppendArgs &a, cudaStream_t stream) {
     kv_append_fp8_token_kernel<T, BS, D><<<(unsigned)ctas, 128, 0, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
-  const int tt = a.num_tokens >= 4096 ? 16 : 8;  // prefill-sized: 8 / 16-token tiles
+  if (a.num_tokens >= 4096) {  // prefill chunks: 16-token tiles of 2 heads
+    const int64_t tiles = (a.num_tokens + kTile16 - 1) / kTile16;
+    if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+    dim3 grid((unsigned)tiles, (unsigned)((a.num_kv_heads + 1) / 2));
+    kv_append_fp8_tile16_kernel<T, BS, D, 2><<<grid, kAppendThreads, 0, stream>>>(p);
+    return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+  }
+  const int tt = 8;  // mid-sized: 8-token tiles of up to 2 KB of heads (one byte per element)
   p.tile_tokens = tt;
-  // one byte per staged element; 16-token tiles take 2 heads each, so that
-  // small tiles keep many CTAs resident (8192-token chunk, inputs cycled
-  // beyond L2: 18.7 us against 19.5 us with all 8 heads per tile)
-  p.heads_per_tile = tt == 16 ? 2 : kAppendRowBytes / D;
+  p.heads_per_tile = kAppendRowBytes / D;
   // staged rows hold the tile's heads only; shared memory sized to the tile
   p.row_pitch = (a.num_kv_heads < p.heads_per_tile ? a.num_kv_heads : p.heads_per_tile) * D + 16;
   constexpr int kTail = kAppendMaxTokens * 8 + (2 * kAppendMaxTokens + 1) * 4;

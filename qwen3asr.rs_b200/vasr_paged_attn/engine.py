@@ -152,11 +152,12 @@ class RandomQwen3Decoder:
             # starts streaming older pages while it finishes
             attn = pa.paged_attention(q, None, None, kc, vc, block_tables, context_lens, None,
                                       max_context_len, scale, 1.0, None, after_append=fused)
-            x = x + attn.view(b, hq * d) @ l["w_o"].t()
+            # residual adds folded into the GEMMs (beta = 1, accumulating into x)
+            x.addmm_(attn.view(b, hq * d), l["w_o"].t())
             h = F.rms_norm(x, (cfg.hidden_size,), l["post_norm"], cfg.rms_norm_eps)
             gu = h @ l["w_gate_up"].t()
             gate, up = gu[:, : cfg.intermediate_size], gu[:, cfg.intermediate_size:]
-            x = x + (F.silu(gate) * up) @ l["w_down"].t()
+            x.addmm_(F.silu(gate) * up, l["w_down"].t())
         x = F.rms_norm(x, (cfg.hidden_size,), self.final_norm, cfg.rms_norm_eps)
         logits = x @ self.embed.t()
         if return_logits:
