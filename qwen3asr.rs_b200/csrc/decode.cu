@@ -47,17 +47,7 @@ DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_
                                : VASR_DECODE_SPLIT_TOKENS;
   w.pages_per_split =
       decode_pages_per_split(num_seqs, num_kv_heads, block_size, max_context_len, split_tokens);
-  // fp8 pages carry half the bytes per token: the same split length would
-  // leave a small batch (config 2: ~800 CTAs over 592 resident slots) with a
-  // long last wave, so their splits are half as long. The workspace holds
-  // partial slots for the shorter split, so one size serves both.
-  w.pages_per_split_fp8 =
-      (num_kv_heads > 0 && num_heads == 2 * num_kv_heads)
-          ? decode_pages_per_split(num_seqs, num_kv_heads, block_size, max_context_len,
-                                   VASR_DECODE_SPLIT_TOKENS_FP8)
-          : w.pages_per_split;
-  const int P = (w.pages_per_split_fp8 < w.pages_per_split ? w.pages_per_split_fp8 : w.pages_per_split) *
-                block_size;
+  const int P = w.pages_per_split * block_size;
   w.max_splits = (max_context_len + P - 1) / P;
   if (w.max_splits < 1) w.max_splits = 1;
   const size_t slots = (size_t)num_seqs * num_kv_heads * w.max_splits;
@@ -75,7 +65,7 @@ DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_
 
 namespace {
 
-DecodeParams make_decode_params(const DecodeArgs &a, const DecodeWorkspace &w, int pages_per_split) {
+DecodeParams make_decode_params(const DecodeArgs &a, const DecodeWorkspace &w) {
   DecodeParams p{};
   p.out = a.out;
   p.q = a.query;
@@ -93,7 +83,7 @@ DecodeParams make_decode_params(const DecodeArgs &a, const DecodeWorkspace &w, i
   p.num_heads = a.num_heads;
   p.num_kv_heads = a.num_kv_heads;
   p.cols = a.max_num_blocks_per_seq;
-  p.pages_per_split = pages_per_split;
+  p.pages_per_split = w.pages_per_split;
   p.max_splits = w.max_splits;
   p.scale = a.scale;
   p.softcap = a.softcapping;
@@ -108,15 +98,8 @@ int check_workspace(const DecodeArgs &a, int max_pages_per_split, DecodeWorkspac
                                a.block_size, a.max_context_len);
   if ((size_t)a.num_seqs * a.num_kv_heads > kDecodeMaxCounters) return VASR_PA_ENOT_SUPPORTED;
   if (a.workspace == nullptr || a.workspace_bytes < w->total) return VASR_PA_EINVAL_WORKSPACE;
-  if (w->pages_per_split > max_pages_per_split || w->pages_per_split_fp8 > max_pages_per_split)
-    return VASR_PA_ENOT_SUPPORTED;
+  if (w->pages_per_split > max_pages_per_split) return VASR_PA_ENOT_SUPPORTED;
   return VASR_PA_OK;
-}
-
-// grid.x: splits of the longest context the bound allows at this split length
-unsigned split_grid(const DecodeArgs &a, int pages_per_split) {
-  const int P = pages_per_split * a.block_size;
-  return (unsigned)((a.max_context_len + P - 1) / P);
 }
 
 // grid = (split, kv head, sequence): the splits of one (sequence, kv head)
@@ -127,11 +110,11 @@ int launch_decode_generic(const DecodeArgs &a, cudaStream_t stream) {
   DecodeWorkspace w;
   const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
   if (st != VASR_PA_OK) return st;
-  const DecodeParams p = make_decode_params(a, w, w.pages_per_split);
+  const DecodeParams p = make_decode_params(a, w);
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(paged_decode_kernel<T, BS, D, G>, C::kSmemBytes, attr_done))
     return VASR_PA_ELAUNCH;
-  dim3 grid(split_grid(a, w.pages_per_split), (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+  dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
   paged_decode_kernel<T, BS, D, G><<<grid, C::kThreads, C::kSmemBytes, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
@@ -151,15 +134,14 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
   DecodeWorkspace w;
   const int st = check_workspace(a, C::kMaxPagesPerSplit, &w);
   if (st != VASR_PA_OK) return st;
-  const int pps = kFp8Pages ? w.pages_per_split_fp8 : w.pages_per_split;
-  const DecodeParams p = make_decode_params(a, w, pps);
+  const DecodeParams p = make_decode_params(a, w);
   constexpr bool kMma = VASR_DECODE_MMA && !std::is_same<T, float>::value &&
                         (std::is_same<T, TC>::value || BS >= 16);
   if constexpr (kMma) {
     auto kern = paged_decode_mma_kernel<T, BS, D, kNST, kMinB, TC>;
     static std::atomic<uint64_t> attr_done{0};
     if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
-    dim3 grid(split_grid(a, pps), (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+    dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
     if (VASR_DECODE_PDL && a.overlap_append) {
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = grid;
@@ -179,7 +161,7 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
   auto kern = paged_decode_g2_kernel<T, BS, D, kNST, kMinB, TC>;
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
-  dim3 grid(split_grid(a, pps), (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+  dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
   kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }

@@ -453,9 +453,6 @@ __global__ void __launch_bounds__(128, 2) paged_decode_kernel(const DecodeParams
 #ifndef VASR_DECODE_SPLIT_TOKENS_G2
 #define VASR_DECODE_SPLIT_TOKENS_G2 1024
 #endif
-#ifndef VASR_DECODE_SPLIT_TOKENS_FP8
-#define VASR_DECODE_SPLIT_TOKENS_FP8 512
-#endif
 constexpr int kDecodeMaxPagesPerSplit = 64;
 inline int decode_pages_per_split(int num_seqs, int num_kv_heads, int block_size,
                                   int max_context_len, int split_tokens) {

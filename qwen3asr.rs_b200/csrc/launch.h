@@ -174,9 +174,8 @@ int read_error_fused(uint32_t *bits, bool clear, cudaStream_t s);
 // [counters: kDecodeMaxCounters x u32][partial o][partial (m, l)].
 constexpr size_t kDecodeMaxCounters = 65536;  // num_seqs * num_kv_heads limit
 struct DecodeWorkspace {
-  int pages_per_split;       // 16-bit pages
-  int pages_per_split_fp8;   // fp8 pages (GQA 2): shorter splits, more CTAs for half the bytes
-  int max_splits;            // partial slots per (sequence, kv head): enough for either split
+  int pages_per_split;
+  int max_splits;
   size_t off_o, off_ml, off_counters, total;
 };
 DecodeWorkspace decode_workspace_layout(int num_seqs, int num_heads, int num_kv_heads,
