@@ -14,9 +14,12 @@
 //        stored back over the first half of its S buffer in TMEM
 //   O += P V     one tcgen05.mma M128 N128 K16 per 16-token page, A = P read
 //        from TMEM, accumulator O in TMEM
-// Warp roles (192 threads): warps 0-3 own TMEM lanes 0-127 (one row per
+// Warp roles (224 threads): warps 0-3 own TMEM lanes 0-127 (one row per
 // thread: softmax, O rescale, epilogue); warp 4 issues the MMAs; warp 5
-// stages Q, K and V with TMA. S is double-buffered in TMEM, so Q K^T of
+// stages Q (TMA) and K (16-byte cp.async), warp 6 stages V (TMA). Issuing a
+// TMA operation takes tens of nanoseconds and the SM's TMA unit serves both
+// resident CTAs, so K, whose 16-byte page rows would need 16 gathers per
+// tile, does not use it. S is double-buffered in TMEM, so Q K^T of
 // tile j + 1 is ready while the softmax warps work on tile j, and the
 // softmax of tile j + 1 does not wait for P V of tile j unless O needs a
 // rescale.
@@ -26,8 +29,8 @@
 //   Q  [2 dim halves][128 rows][128 B]   the 128-byte swizzle (SBO 1024),
 //      the canonical SW128 K-major layout; one 3-D TMA load per half
 //      (64 elements x head x token), 128-byte rows
-//   K  [16 dim chunks][64 keys][16 B]    no swizzle, LBO 1024, SBO 128; per
-//      dim chunk one TMA gather4 of that chunk's 256-byte row in 4 pages
+//   K  [16 dim chunks][64 keys][16 B]    no swizzle, LBO 1024, SBO 128; the
+//      K loader warp fills it with 16-byte cp.async copies (32 per lane)
 //   V  one page = [128 dims][16 tokens] rows of 32 B, one 2-D TMA load with
 //      the 32-byte swizzle = the canonical SW32 K-major layout (SBO 256) that
 //      the page's 16 tokens feed as one K = 16 step
@@ -67,19 +70,24 @@ constexpr int kOffV = kOffK + kStages * kKVTile;
 constexpr int kOffBar = kOffV + kStages * kKVTile;
 // One commit per MMA group: "Q K^T j done" both fills S j and frees K
 // stage j & 1; "P V j done" both frees V stage j & 1 and the S buffer of j.
+// K and V stages are full after 32 cp.async arrivals (one per loader lane).
 constexpr int kBarFullK = 0, kBarFullV = 2, kBarSFull = 4, kBarPFull = 6, kBarPvDone = 8,
               kBarQ = 10;
 constexpr int kBarEmptyK = kBarSFull, kBarEmptyV = kBarPvDone;
 constexpr int kNumBars = 11;
+__host__ __device__ constexpr uint32_t bar_count(int i) {
+  return (i == kBarPFull || i == kBarPFull + 1) ? 128u : (i < kBarSFull ? 32u : 1u);
+}
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemUsed = kOffTmemSlot + 16;
 constexpr int kSmemAlign = 1024;             // SW128 Q tile: 1024-byte alignment
 constexpr int kSmemBytes = kSmemUsed + kSmemAlign;
 constexpr int kTmemCols = 256;               // S ring 2 x 64 columns + O 128 columns
 constexpr int kTmemS = 0, kTmemO = 128;
-constexpr int kThreads = 192;              // warps 0-3 rows, warp 4 MMA, warp 5 loads
+constexpr int kThreads = 224;              // warps 0-3 rows, 4 MMA, 5 Q + K loads, 6 V loads
 constexpr int kMmaWarp = 4;
 constexpr int kLoadWarp = 5;
+constexpr int kVLoadWarp = 6;
 constexpr int kIdRegs = 4;                 // block ids of pages 0..127 held in registers
 constexpr float kRescaleLog2 = 8.f;          // rescale O only when the max grows > 2^8
 constexpr uint64_t kWaitNs = 200000000ull;   // 200 ms per wait before giving up
@@ -178,14 +186,13 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
-// 2-D tiled TMA load into this CTA's shared memory (no cluster fan-out).
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
-      "[%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(map), "r"(x), "r"(y), "r"(bar)
-      : "memory");
+// 16-byte asynchronous copy global -> shared (L2 only), and an arrive on
+// `bar` once every such copy of this thread has landed (not counted up first).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -225,16 +232,6 @@ __device__ __forceinline__ void wait_phase(uint32_t bar, uint32_t parity, bool &
   dead = __any_sync(0xffffffffu, dead);
 }
 
-// 2-D TMA gather of four rows (box one row high) into four consecutive
-// shared-memory rows.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int x, int r0,
-                                            int r1, int r2, int r3, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
-      "l"(map), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
-      : "memory");
-}
 // 3-D tiled TMA load (the Q tile: 64 elements x heads x tokens).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
                                             int c2, uint32_t bar) {
@@ -286,9 +283,7 @@ __device__ __forceinline__ uint32_t pack2f<__half>(float lo, float hi) {
 template <typename T, int G>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_umma_kernel(const PrefillArgs p, const int tiles,
-                        const __grid_constant__ CUtensorMap q_map,
-                        const __grid_constant__ CUtensorMap k_map,
-                        const __grid_constant__ CUtensorMap v_map) {
+                        const __grid_constant__ CUtensorMap q_map) {
   constexpr int kPos = kM / G;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
@@ -302,30 +297,28 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int kvh = (int)(blockIdx.x % (unsigned)p.num_kv_heads);
   const int item = (int)(blockIdx.x / (unsigned)p.num_kv_heads);
   const int b = item % p.num_seqs, tile = tiles - 1 - item / p.num_seqs;
-  if (warp == kLoadWarp && lane == 0) {
-    prefetch_tensormap(&q_map);
-    prefetch_tensormap(&k_map);
-    prefetch_tensormap(&v_map);
-  }
+  if (warp == kLoadWarp && lane == 0) prefetch_tensormap(&q_map);
 
   const int cols = p.max_num_blocks_per_seq;
-  // The load warp fetches the sequence's first block ids (pages lane + 32 i)
-  // together with its lengths, before it knows how many it needs.
+  // The load warps fetch the sequence's first block ids (pages lane + 32 i)
+  // together with its lengths, before they know how many they need.
   const uint32_t *table = p.block_tables + (int64_t)b * cols;
   uint32_t ids[kIdRegs];
 #pragma unroll
   for (int i = 0; i < kIdRegs; ++i) ids[i] = 0u;
-  if (warp == kLoadWarp) {
+  if (warp == kLoadWarp || warp == kVLoadWarp) {
 #pragma unroll
     for (int i = 0; i < kIdRegs; ++i)
       if (lane + 32 * i < cols) ids[i] = __ldg(table + lane + 32 * i);
   }
+  // the lengths are read together (independent loads, one round trip)
   const int64_t q0 = p.cu_seqlens_q[b];
-  const int qlen = (int)(p.cu_seqlens_q[b + 1] - q0);
+  const int64_t q1 = p.cu_seqlens_q[b + 1];
+  int ctx = (int)p.context_lens[b];
+  const int qlen = (int)(q1 - q0);
   if (tile == tiles - 1 && qlen > tiles * kPos && tid == 0)
     raise_device_error(VASR_PA_DERR_QLEN_RANGE);
   if (tile * kPos >= qlen) return;
-  int ctx = (int)p.context_lens[b];
   if (ctx > cols * kBS) {
     if (tid == 0) raise_device_error(VASR_PA_DERR_CTX_RANGE);
     ctx = cols * kBS;
@@ -349,91 +342,72 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar = sbase + kOffBar;
   auto B = [&](int i) { return bar + 8u * (uint32_t)i; };
 
+  // page id of tile j for this lane (page lane & 3 of the tile; lanes past
+  // the context get any valid page: its keys are masked). Lane l keeps the
+  // block ids of pages l, l + 32, l + 64, l + 96 in registers.
+  auto tile_page = [&](int j, int &np) -> uint32_t {
+    const int pg0 = j * kPagesPerTile;
+    np = min(kPagesPerTile, n_pages - pg0);
+    const int grp = pg0 >> 5;  // warp-uniform: a tile's pages share one group of 32
+    uint32_t v = ids[0];
+#pragma unroll
+    for (int i = 1; i < kIdRegs; ++i) v = grp == i ? ids[i] : v;
+    uint32_t id = __shfl_sync(0xffffffffu, v, (pg0 & 31) + (lane & (kPagesPerTile - 1)));
+    if (grp >= kIdRegs && lane < np) id = __ldg(table + pg0 + lane);
+    if (lane < np && (int64_t)id >= p.num_blocks) {
+      raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
+      id = 0;
+    }
+    const uint32_t id0 = __shfl_sync(0xffffffffu, id, 0);
+    return (lane & (kPagesPerTile - 1)) < np ? id : id0;
+  };
+
   if (warp == kLoadWarp) {
-    // ------------------------------------------------------------ loads
-    // K tile j -> K stage j & 1 as 16 TMA gathers (one 16-byte dim chunk of
-    // four pages each); V tile j -> V stage j & 1 as one swizzled 2-D TMA
-    // load per page. K j + 2 waits for Q K^T j, V j + 2 for P V j. Lane l
-    // keeps the block ids of pages l, l + 32, l + 64, l + 96 in registers.
+    // ------------------------------------------------------- Q and K loads
+    // K tile j -> K stage j & 1 by 16-byte asynchronous copies (no TMA: a
+    // page's key rows are 16 bytes wide, so a K tile would cost 16 TMA
+    // gathers, and the SM's TMA unit is shared with the V loads of both
+    // resident CTAs). K j + 2 waits for Q K^T j.
     if (lane == 0) {
-      for (int i = 0; i < kNumBars; ++i) mbar_init(B(i), (i == kBarPFull || i == kBarPFull + 1) ? 4 * 32 : 1);
+      for (int i = 0; i < kNumBars; ++i) mbar_init(B(i), bar_count(i));
       mbar_fence_init();
       mbar_arrive_expect_tx(B(kBarQ), (uint32_t)kQBytes);
       tma_load_3d(sbase + kOffQ, &q_map, 0, kvh * G, (int)(q0 + i0), B(kBarQ));
       tma_load_3d(sbase + kOffQ + kQBytes / 2, &q_map, kD / 2, kvh * G, (int)(q0 + i0), B(kBarQ));
     }
     __syncwarp();
-    auto tile_page = [&](int j, int &np) -> uint32_t {  // page id of tile j held by this lane
-      const int pg0 = j * kPagesPerTile;
-      np = min(kPagesPerTile, n_pages - pg0);
-      const int grp = pg0 >> 5;  // warp-uniform: a tile's pages share one group of 32
-      uint32_t v = ids[0];
-#pragma unroll
-      for (int i = 1; i < kIdRegs; ++i) v = grp == i ? ids[i] : v;
-      uint32_t id = __shfl_sync(0xffffffffu, v, (pg0 & 31) + (lane & (kPagesPerTile - 1)));
-      if (grp >= kIdRegs && lane < np) id = __ldg(table + pg0 + lane);
-      if (lane < np && (int64_t)id >= p.num_blocks) {
-        raise_device_error(VASR_PA_DERR_BLOCK_RANGE);
-        id = 0;
-      }
-      return id;
-    };
     auto load_k = [&](int j) {
-      // one gather of the four pages' 256-byte rows of dim chunk c per lane c
-      int np;
-      uint32_t id = tile_page(j, np);
-      const uint32_t id0 = __shfl_sync(0xffffffffu, id, 0);
-      if (lane >= np) id = id0;  // pages past the context: any valid row (masked)
-      int row[kPagesPerTile];
-#pragma unroll
-      for (int pg = 0; pg < kPagesPerTile; ++pg)
-        row[pg] = (int)(((int64_t)__shfl_sync(0xffffffffu, id, pg) * p.num_kv_heads + kvh) * 16);
-      const uint32_t fb = B(kBarFullK + (j & 1));
-      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)kKVTile);
-      __syncwarp();
-      if (lane < kD / 8)
-        tma_gather4(sbase + kOffK + (j & 1) * kKVTile + lane * (kNT * 16), &k_map, 0,
-                    row[0] + lane, row[1] + lane, row[2] + lane, row[3] + lane, fb);
-    };
-    auto load_v = [&](int j) {
+      // 1024 16-byte pieces (dim chunk c, key k) of the tile, 32 per lane:
+      // instruction i moves chunk i / 2 of keys (i & 1) * 32 + lane, i.e. 16
+      // bytes at c * 256 + token * 16 of page (i & 1) * 2 + lane / 16
       int np;
       const uint32_t id = tile_page(j, np);
-      const uint32_t fb = B(kBarFullV + (j & 1));
-      if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)(np * kPageBytes));
-      __syncwarp();
-      if (lane < np)
-        tma_load_2d(sbase + kOffV + (j & 1) * kKVTile + lane * kPageBytes, &v_map, 0,
-                    (int)(((int64_t)id * p.num_kv_heads + kvh) * kD), fb);
+      const int pga = lane >> 4, pgb = pga + 2, tok = lane & (kBS - 1);
+      const uint32_t ida = __shfl_sync(0xffffffffu, id, pga), idb = __shfl_sync(0xffffffffu, id, pgb);
+      const unsigned char *kc = static_cast<const unsigned char *>(p.key_cache);
+      const unsigned char *src_a = kc + ((int64_t)ida * p.num_kv_heads + kvh) * kPageBytes + tok * 16;
+      const unsigned char *src_b = kc + ((int64_t)idb * p.num_kv_heads + kvh) * kPageBytes + tok * 16;
+      const uint32_t dst = sbase + kOffK + (j & 1) * kKVTile + lane * 16;
+#pragma unroll
+      for (int c = 0; c < kD / 8; ++c) {
+        if (pga < np) cp_async16(dst + c * (kNT * 16), src_a + c * (kBS * 16));
+        if (pgb < np) cp_async16(dst + c * (kNT * 16) + 32 * 16, src_b + c * (kBS * 16));
+      }
+      cp_async_arrive_noinc(B(kBarFullK + (j & 1)));  // one of 32 arrivals, when this lane's copies land
     };
-    // the first two K and V tiles start before the CTA-wide sync
     load_k(0);
     if (n_kt > 1) load_k(1);
-    load_v(0);
-    if (n_kt > 1) load_v(1);
-    int k_issued = min(n_kt, 2), v_issued = min(n_kt, 2);
+    int k_issued = min(n_kt, 2);
     __syncthreads();
-    // The tensor core completes Q K^T 0, Q K^T 1, P V 0, Q K^T 2, P V 1, ...
-    // in this order; the loads wait for those events in the same order. Once
-    // a wait gives up, nothing more is issued: a stage whose previous copy or
-    // reader has not finished must not receive another.
+    // Q K^T j completes in order; K j + 2 goes into its stage once it has.
+    // Once a wait gives up, nothing more is issued: a stage whose reader has
+    // not finished must not receive another copy.
     bool dead = false;
-    for (int j = 2; j < min(n_kt, 4) && !dead; ++j) {
+    for (int j = 2; j < n_kt && !dead; ++j) {
       wait_phase(B(kBarEmptyK + (j & 1)), ((j >> 1) - 1) & 1, dead);
       if (dead) break;
       load_k(j);
       k_issued = j + 1;
-    }
-    for (int j = 2; j < n_kt && !dead; ++j) {
-      wait_phase(B(kBarEmptyV + (j & 1)), ((j >> 1) - 1) & 1, dead);
-      if (dead) break;
-      load_v(j);
-      v_issued = j + 1;
-      if (j + 2 < n_kt) {
-        wait_phase(B(kBarEmptyK + (j & 1)), (((j + 2) >> 1) - 1) & 1, dead);
-        if (dead) break;
-        load_k(j + 2);
-        k_issued = j + 3;
-      }
     }
     // copies still in flight must land before the CTA's shared memory goes
     // away: the last phase issued on each stage (in a healthy run every one
@@ -441,6 +415,47 @@ __global__ void __launch_bounds__(kThreads, 2)
     dead = false;
     for (int j = max(0, k_issued - kStages); j < k_issued; ++j)
       wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
+    __syncthreads();
+    return;
+  }
+  if (warp == kVLoadWarp) {
+    // -------------------------------------------------------------- V loads
+    // V tile j -> V stage j & 1 by 16-byte cp.async copies into the 32-byte
+    // swizzled layout of each page (a TMA load of it runs in 32-byte pieces
+    // and took ~1.4 us per tile); V j + 2 waits for P V j. The barriers are
+    // initialised by the K loader before the CTA-wide sync.
+    auto load_v = [&](int j) {
+      // 1024 16-byte pieces of the tile, 32 per lane: instruction i moves
+      // half h of dim row d of page i / 8, (d, h) = ((i % 8) * 32 + lane) /
+      // 2, % 2, to its place in the 32-byte-swizzled page image
+      int np;
+      const uint32_t id = tile_page(j, np);
+      const unsigned char *vc = static_cast<const unsigned char *>(p.value_cache);
+      const uint32_t dst = sbase + kOffV + (j & 1) * kKVTile;
+#pragma unroll
+      for (int pg = 0; pg < kPagesPerTile; ++pg) {
+        const uint32_t idp = __shfl_sync(0xffffffffu, id, pg);
+        if (pg >= np) continue;
+        const unsigned char *src = vc + ((int64_t)idp * p.num_kv_heads + kvh) * kPageBytes;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = i * 32 + lane, d = r >> 1, h = r & 1;
+          cp_async16(dst + pg * kPageBytes + d * 32 + ((h ^ ((d >> 2) & 1)) << 4), src + r * 16);
+        }
+      }
+      cp_async_arrive_noinc(B(kBarFullV + (j & 1)));  // one of 32 arrivals
+    };
+    __syncthreads();
+    load_v(0);
+    if (n_kt > 1) load_v(1);
+    int v_issued = min(n_kt, 2);
+    bool dead = false;
+    for (int j = 2; j < n_kt && !dead; ++j) {
+      wait_phase(B(kBarEmptyV + (j & 1)), ((j >> 1) - 1) & 1, dead);
+      if (dead) break;
+      load_v(j);
+      v_issued = j + 1;
+    }
     dead = false;
     for (int j = max(0, v_issued - kStages); j < v_issued; ++j)
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
@@ -448,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
 
-  // ------------------------------------------------------ warps 0-3 and 5
+  // ------------------------------------------------------ warps 0-4
   if (warp == 0) tmem_alloc(sbase + kOffTmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
@@ -461,6 +476,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     // Order on the tensor core: Q K^T 0, Q K^T 1, then per tile j: P V j,
     // Q K^T j + 2. Backpressure from the tensor core stalls only this warp.
     const uint32_t idesc_s = idesc_f16<T>(kNT), idesc_o = idesc_f16<T>(kD);
+    // Descriptors are built once; a later operand differs only in its start
+    // address, the low field of the descriptor (address / 16 < 2^14 for any
+    // shared-memory address), so it is the base descriptor plus offset / 16.
+    const uint64_t qd0 = sdesc(sbase + kOffQ, 16, 1024, 2);
+    const uint64_t kd0 = sdesc(sbase + kOffK, kNT * 16, 128, 0);
+    const uint64_t vd0 = sdesc(sbase + kOffV, 16, 256, 6);
     // last commit issued (barrier index, phase parity): once it arrives every
     // MMA this warp issued has completed
     int last_bar = -1;
@@ -468,14 +489,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     auto issue_s = [&](int j) {  // S(j & 1) = Q K_j^T
       wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
       if (dead) return;
+      // the K copies are generic-proxy writes; the MMA reads through the
+      // async proxy
+      fence_proxy_async_smem();
       tc_fence_after();
       {
-        const uint32_t sk = sbase + kOffK + (j & 1) * kKVTile;
+        const uint64_t kd = kd0 + (uint64_t)(((j & 1) * kKVTile) >> 4);
 #pragma unroll
         for (int ks = 0; ks < kD / 16; ++ks)
-          umma_f16(tmem + kTmemS + (j & 1) * kNT,
-                   sdesc(sbase + kOffQ + (ks >> 2) * (kQBytes / 2) + (ks & 3) * 32, 16, 1024, 2),
-                   sdesc(sk + ks * 2 * (kNT * 16), kNT * 16, 128, 0), idesc_s, ks > 0);
+          umma_f16(tmem + kTmemS + (j & 1) * kNT, qd0 + (uint64_t)(((ks >> 2) * (kQBytes / 2) + (ks & 3) * 32) >> 4),
+                   kd + (uint64_t)((ks * 2 * (kNT * 16)) >> 4), idesc_s, ks > 0);
         umma_commit(B(kBarSFull + (j & 1)));  // = kBarEmptyK
         last_bar = kBarSFull + (j & 1);
         last_par = (j >> 1) & 1;
@@ -488,6 +511,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = 0; j < n_kt && !dead; ++j) {
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
       if (dead) break;
+      fence_proxy_async_smem();  // the V copies are generic-proxy writes
       if (j == n_kt - 1 && (kv_end % kBS) != 0) {
         // V of tokens >= kv_end in the last page holds other data (possibly
         // non-finite); zero it so that P = 0 there contributes exactly 0.
@@ -503,10 +527,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_after();
       {
         const int np = min(kPagesPerTile, n_pages - j * kPagesPerTile);
-        const uint32_t sv = sbase + kOffV + (j & 1) * kKVTile;
+        const uint64_t vd = vd0 + (uint64_t)(((j & 1) * kKVTile) >> 4);
         for (int pg = 0; pg < np; ++pg)
           umma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * kNT + pg * (kBS / 2),
-                      sdesc(sv + pg * kPageBytes, 16, 256, 6), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
+                      vd + (uint64_t)((pg * kPageBytes) >> 4), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
         umma_commit(B(kBarPvDone + (j & 1)));  // = kBarEmptyV
         last_bar = kBarPvDone + (j & 1);
         last_par = (j >> 1) & 1;
@@ -664,37 +688,6 @@ EncodeTiledFn tensor_map_encoder() {
   return fn;
 }
 
-// V cache viewed as rows of one token page line: [nb * Hkv * 128 dims][16 tokens].
-bool make_v_map(CUtensorMap *map, const void *v_cache, int64_t num_blocks, int num_kv_heads) {
-  EncodeTiledFn enc = tensor_map_encoder();
-  if (!enc) return false;
-  const int64_t rows = num_blocks * num_kv_heads * kD;
-  if (rows <= 0 || rows >= (int64_t(1) << 31)) return false;  // int32 TMA row coordinates
-  const cuuint64_t dims[2] = {(cuuint64_t)kBS, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)kBS * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBS, (cuuint32_t)kD};
-  const cuuint32_t estr[2] = {1, 1};
-  std::memset(map, 0, sizeof(*map));
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(v_cache), dims, strides,
-             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// K cache viewed as rows of one dim chunk of one page: [nb * Hkv * 16][16 tokens x 8].
-bool make_k_map(CUtensorMap *map, const void *k_cache, int64_t num_blocks, int num_kv_heads) {
-  EncodeTiledFn enc = tensor_map_encoder();
-  if (!enc) return false;
-  const int64_t rows = num_blocks * num_kv_heads * (kD / 8);
-  const cuuint64_t dims[2] = {(cuuint64_t)kBS * 8, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)kBS * 8 * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBS * 8, 1};
-  const cuuint32_t estr[2] = {1, 1};
-  std::memset(map, 0, sizeof(*map));
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(k_cache), dims, strides,
-             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // Q viewed as [tokens][heads][128 elements]: a box of (64, G, 128 / G) at
 // element offset 0 or 64 lands as 128 rows (row = position * G + head) of
 // 128 bytes with the 128-byte swizzle, half of the CTA's Q in the canonical
@@ -713,15 +706,14 @@ bool make_q_map(CUtensorMap *map, const PrefillArgs &a, int g) {
 }
 
 template <typename T, int G>
-int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, const CUtensorMap &kmap,
-             const CUtensorMap &map, cudaStream_t s) {
+int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0};
   if (!ensure_smem_attr(prefill_umma_kernel<T, G>, kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
   constexpr int kPos = kM / G;
   const int64_t tiles = prefill_tiles_per_seq(a, kPos);
   if (tiles <= 0 || tiles * a.num_seqs * a.num_kv_heads > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
   dim3 grid((unsigned)(tiles * a.num_seqs * a.num_kv_heads));
-  prefill_umma_kernel<T, G><<<grid, kThreads, kSmemBytes, s>>>(a, (int)tiles, qmap, kmap, map);
+  prefill_umma_kernel<T, G><<<grid, kThreads, kSmemBytes, s>>>(a, (int)tiles, qmap);
   return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
 }
 
@@ -732,27 +724,23 @@ int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s) {
   if (a.dtype != VASR_PA_BF16 && a.dtype != VASR_PA_F16) return VASR_PA_ENOT_SUPPORTED;
   const int g = a.num_heads / a.num_kv_heads;
   if (g != 1 && g != 2 && g != 4) return VASR_PA_ENOT_SUPPORTED;
-  if ((int64_t)a.num_blocks * a.num_kv_heads * kD >= (int64_t(1) << 31))
-    return VASR_PA_ENOT_SUPPORTED;  // int32 TMA row coordinates
   if (a.total_q_tokens >= (int64_t(1) << 31)) return VASR_PA_ENOT_SUPPORTED;
-  // tensor maps want 16-byte aligned bases and strides; other views take the
-  // mma.sync kernel
+  // the Q tensor map and the 16-byte page copies want 16-byte aligned bases
+  // and strides; other views take the mma.sync kernel
   if ((reinterpret_cast<uintptr_t>(a.query) | reinterpret_cast<uintptr_t>(a.key_cache) |
        reinterpret_cast<uintptr_t>(a.value_cache)) % 16 != 0 ||
       (a.q_token_stride * 2) % 16 != 0)
     return VASR_PA_ENOT_SUPPORTED;
-  CUtensorMap qmap, kmap, map;
-  if (!make_v_map(&map, a.value_cache, a.num_blocks, a.num_kv_heads)) return VASR_PA_ELAUNCH;
-  if (!make_k_map(&kmap, a.key_cache, a.num_blocks, a.num_kv_heads)) return VASR_PA_ELAUNCH;
+  CUtensorMap qmap;
   if (!make_q_map(&qmap, a, g)) return VASR_PA_ELAUNCH;
   const bool bf = a.dtype == VASR_PA_BF16;
   switch (g) {
     case 1:
-      return bf ? launch_g<__nv_bfloat16, 1>(a, qmap, kmap, map, s) : launch_g<__half, 1>(a, qmap, kmap, map, s);
+      return bf ? launch_g<__nv_bfloat16, 1>(a, qmap, s) : launch_g<__half, 1>(a, qmap, s);
     case 2:
-      return bf ? launch_g<__nv_bfloat16, 2>(a, qmap, kmap, map, s) : launch_g<__half, 2>(a, qmap, kmap, map, s);
+      return bf ? launch_g<__nv_bfloat16, 2>(a, qmap, s) : launch_g<__half, 2>(a, qmap, s);
     default:
-      return bf ? launch_g<__nv_bfloat16, 4>(a, qmap, kmap, map, s) : launch_g<__half, 4>(a, qmap, kmap, map, s);
+      return bf ? launch_g<__nv_bfloat16, 4>(a, qmap, s) : launch_g<__half, 4>(a, qmap, s);
   }
 }
 
