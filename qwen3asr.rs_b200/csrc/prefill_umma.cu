@@ -643,7 +643,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   wait_phase(B(kBarPvDone + ((n_kt - 1) & 1)), ((n_kt - 1) >> 1) & 1, dead);
   tc_fence_after();
   const float inv = l > 0.f ? 1.f / l : 0.f;
-  T *dst = out + (q0 + i0 + r / G) * row_stride + (int64_t)(kvh * G + r % G) * kD;
+  // O / l (16-bit) is staged in the Q buffer, which no MMA reads any more:
+  // row r at r * 256 bytes, its 16-byte chunk c at slot c ^ (r % 16), so a
+  // warp's stores of one chunk of 32 rows and the later reads of one row
+  // hit distinct banks. The rows then leave as whole token rows (the G
+  // heads of a kv head are adjacent in out), 16 bytes per thread.
+  unsigned char *stg = smem + kOffQ;
 #pragma unroll 1
   for (int cc = 0; cc < kD; cc += 64) {
     uint32_t o[64];
@@ -654,11 +659,20 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int i = 0; i < 32; ++i)
       w[i] = pack2f<T>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-    if (row_ok) {
-      uint4 *d4 = reinterpret_cast<uint4 *>(dst + cc);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    for (int i = 0; i < 8; ++i) {
+      const int c = cc / 8 + i;
+      *reinterpret_cast<uint4 *>(stg + r * 256 + ((c ^ (r & 15)) << 4)) =
+          make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
     }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+  const int chunks = n_pos * G * (kD * 2 / 16);
+  for (int e = r; e < chunks; e += 128) {
+    const int row = e >> 4, c = e & 15;  // row = position * G + head
+    const uint4 v = *reinterpret_cast<const uint4 *>(stg + row * 256 + ((c ^ (row & 15)) << 4));
+    *reinterpret_cast<uint4 *>(out + (q0 + i0 + row / G) * row_stride + (int64_t)(kvh * G + row % G) * kD +
+                               c * 8) = v;
   }
   tc_fence_before();
   __syncthreads();
