@@ -44,6 +44,7 @@ struct AppendParams {
   int tile_tokens;
   int heads_per_tile;
   int row_pitch;  // bytes of one staged token row: heads_per_tile * D * es + 16 (conflict-free columns)
+  int tiles_per_cta;  // 16-token tiles: consecutive tiles one CTA handles in turn
 };
 
 template <typename T, int BS, int D>
@@ -163,6 +164,16 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_kernel(const AppendP
 // the tile's chunks of one page row form contiguous runs.
 constexpr int kTile16 = 16;
 
+// Tiles per CTA for `items` 16-token tiles over `resident` CTA slots: the
+// fewest that fit every CTA into one wave, so that no CTA starts after
+// another has finished (a second, partial wave of whole tiles left SMs idle
+// for a quarter of the launch). 1 when the slots are unknown.
+inline int tile16_per_cta(int64_t items, int64_t resident) {
+  if (resident <= 0 || items <= resident) return 1;
+  const int64_t t = (items + resident - 1) / resident;
+  return t > 64 ? 64 : (int)t;
+}
+
 // Warp 0: the tile's slots into s_slot (out of range -> skipped and flagged)
 // and, per V group of kTPS tokens, whether it is one aligned run of slots.
 template <int BS, int kTPS, int kGroups>
@@ -204,62 +215,66 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_tile16_kernel(const 
   __shared__ int64_t s_slot[kTile16];
   __shared__ int s_gok[kGroups];
   const int tid = threadIdx.x;
-  const int64_t t0 = (int64_t)blockIdx.x * kTile16;
   const int h0 = blockIdx.y * HPT;
   const int HC = min(HPT, p.num_kv_heads - h0);
-  const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
-  if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
+  for (int it = 0; it < p.tiles_per_cta; ++it) {
+    const int64_t t0 = ((int64_t)blockIdx.x * p.tiles_per_cta + it) * kTile16;
+    if (t0 >= p.num_tokens) break;
+    if (it > 0) __syncthreads();  // the previous tile's staged rows and slots are read
+    const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
+    if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
 #pragma unroll
-  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
-    const int i = tid + k * kAppendThreads;
-    const int tt = i / kRow, r = i % kRow;
-    if (i < kChunks && tt < ntok && r / kCH < HC) {
-      const int64_t col = (int64_t)h0 * D * kES + r * 16;
-      const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(p.key + (t0 + tt) * p.k_stride_bytes + col));
-      const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(p.value + (t0 + tt) * p.v_stride_bytes + col));
-      *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) = kv;
-      *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) = vv;
+    for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+      const int i = tid + k * kAppendThreads;
+      const int tt = i / kRow, r = i % kRow;
+      if (i < kChunks && tt < ntok && r / kCH < HC) {
+        const int64_t col = (int64_t)h0 * D * kES + r * 16;
+        const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(p.key + (t0 + tt) * p.k_stride_bytes + col));
+        const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(p.value + (t0 + tt) * p.v_stride_bytes + col));
+        *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) = kv;
+        *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) = vv;
+      }
     }
-  }
-  __syncthreads();
-  // K: item i = (chunk r of the row, token tt), token fastest
+    __syncthreads();
+    // K: item i = (chunk r of the row, token tt), token fastest
 #pragma unroll
-  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
-    const int i = tid + k * kAppendThreads;
-    const int tt = i % kTile16, r = i / kTile16;
-    const int hc = r / kCH, c = r % kCH;
-    const int64_t sl = s_slot[tt];
-    if (i < kChunks && sl >= 0 && hc < HC) {
-      const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
-      const uint64_t dst = (((blk * (uint64_t)p.num_kv_heads + (uint64_t)(h0 + hc)) * kCH + c) * BS + off) * 16;
-      *reinterpret_cast<uint4 *>(p.k_cache + dst) = *reinterpret_cast<const uint4 *>(kt + tt * kPitch + r * 16);
-    }
-  }
-  // V: item i = (group g, dim d of head hc), group fastest: consecutive
-  // threads fill consecutive 16-byte pieces of the page rows
-#pragma unroll
-  for (int k = 0; k < (kVItems + kAppendThreads - 1) / kAppendThreads; ++k) {
-    const int i = tid + k * kAppendThreads;
-    const int g = i % kGroups, hd = i / kGroups;
-    const int hc = hd / D, d = hd % D;
-    if (i >= kVItems || hc >= HC) continue;
-    const unsigned char *src = vt + (g * kTPS) * kPitch + (hc * D + d) * kES;
-    const uint64_t row = ((uint64_t)h0 + hc) * D + d;  // page row of (head, dim) within a block
-    if (s_gok[g]) {
-      const uint64_t us = (uint64_t)s_slot[g * kTPS], blk = us / BS, off = us % BS;
-      T vals[kTPS];
-#pragma unroll
-      for (int e = 0; e < kTPS; ++e) vals[e] = *reinterpret_cast<const T *>(src + e * kPitch);
-      T *dst = reinterpret_cast<T *>(p.v_cache) + (blk * (uint64_t)p.num_kv_heads * D + row) * BS + off;
-      *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(vals);
-    } else {
-#pragma unroll
-      for (int e = 0; e < kTPS; ++e) {
-        const int64_t sl = s_slot[g * kTPS + e];
-        if (sl < 0) continue;
+    for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+      const int i = tid + k * kAppendThreads;
+      const int tt = i % kTile16, r = i / kTile16;
+      const int hc = r / kCH, c = r % kCH;
+      const int64_t sl = s_slot[tt];
+      if (i < kChunks && sl >= 0 && hc < HC) {
         const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
-        reinterpret_cast<T *>(p.v_cache)[(blk * (uint64_t)p.num_kv_heads * D + row) * BS + off] =
-            *reinterpret_cast<const T *>(src + e * kPitch);
+        const uint64_t dst = (((blk * (uint64_t)p.num_kv_heads + (uint64_t)(h0 + hc)) * kCH + c) * BS + off) * 16;
+        *reinterpret_cast<uint4 *>(p.k_cache + dst) = *reinterpret_cast<const uint4 *>(kt + tt * kPitch + r * 16);
+      }
+    }
+    // V: item i = (group g, dim d of head hc), group fastest: consecutive
+    // threads fill consecutive 16-byte pieces of the page rows
+#pragma unroll
+    for (int k = 0; k < (kVItems + kAppendThreads - 1) / kAppendThreads; ++k) {
+      const int i = tid + k * kAppendThreads;
+      const int g = i % kGroups, hd = i / kGroups;
+      const int hc = hd / D, d = hd % D;
+      if (i >= kVItems || hc >= HC) continue;
+      const unsigned char *src = vt + (g * kTPS) * kPitch + (hc * D + d) * kES;
+      const uint64_t row = ((uint64_t)h0 + hc) * D + d;  // page row of (head, dim) within a block
+      if (s_gok[g]) {
+        const uint64_t us = (uint64_t)s_slot[g * kTPS], blk = us / BS, off = us % BS;
+        T vals[kTPS];
+#pragma unroll
+        for (int e = 0; e < kTPS; ++e) vals[e] = *reinterpret_cast<const T *>(src + e * kPitch);
+        T *dst = reinterpret_cast<T *>(p.v_cache) + (blk * (uint64_t)p.num_kv_heads * D + row) * BS + off;
+        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(vals);
+      } else {
+#pragma unroll
+        for (int e = 0; e < kTPS; ++e) {
+          const int64_t sl = s_slot[g * kTPS + e];
+          if (sl < 0) continue;
+          const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
+          reinterpret_cast<T *>(p.v_cache)[(blk * (uint64_t)p.num_kv_heads * D + row) * BS + off] =
+              *reinterpret_cast<const T *>(src + e * kPitch);
+        }
       }
     }
   }
@@ -285,9 +300,14 @@ int launch_append_t(const AppendArgs &a, cudaStream_t stream) {
   // writes whole 32-byte V page rows and small tiles keep many CTAs resident.
   if (a.num_tokens >= 4096) {  // prefill chunks: 16-token tiles of 512 bytes of heads
     constexpr int kHPT = 512 / (D * (int)sizeof(T)) > 0 ? 512 / (D * (int)sizeof(T)) : 1;
+    static std::atomic<int64_t> resident[64];
     const int64_t tiles = (a.num_tokens + kTile16 - 1) / kTile16;
-    if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
-    dim3 grid((unsigned)tiles, (unsigned)((a.num_kv_heads + kHPT - 1) / kHPT));
+    const int hg = (a.num_kv_heads + kHPT - 1) / kHPT;
+    p.tiles_per_cta = tile16_per_cta(tiles * hg, resident_ctas(kv_append_tile16_kernel<T, BS, D, kHPT>,
+                                                                kAppendThreads, 0, resident));
+    const int64_t gx = (tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
+    if (gx > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+    dim3 grid((unsigned)gx, (unsigned)hg);
     kv_append_tile16_kernel<T, BS, D, kHPT><<<grid, kAppendThreads, 0, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
@@ -729,6 +749,7 @@ struct AppendFp8Params {
   int tile_tokens;
   int heads_per_tile;
   int row_pitch;  // bytes of one staged token row (one byte per element) + 16
+  int tiles_per_cta;  // 16-token tiles: consecutive tiles one CTA handles in turn
 };
 
 // The quotient x / s as the IEEE division rounds it, RN(x / s), from a
@@ -912,64 +933,68 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_tile16_kernel(co
   __shared__ int64_t s_slot[kTile16];
   __shared__ int s_gok[kGroups];
   const int tid = threadIdx.x;
-  const int64_t t0 = (int64_t)blockIdx.x * kTile16;
   const int h0 = blockIdx.y * HPT;
   const int HC = min(HPT, p.num_kv_heads - h0);
-  const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
   const QuantScale ks = quant_scale(__ldg(p.k_scale)), vs = quant_scale(__ldg(p.v_scale));
-  if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
+  for (int it = 0; it < p.tiles_per_cta; ++it) {
+    const int64_t t0 = ((int64_t)blockIdx.x * p.tiles_per_cta + it) * kTile16;
+    if (t0 >= p.num_tokens) break;
+    if (it > 0) __syncthreads();  // the previous tile's staged rows and slots are read
+    const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
+    if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
 #pragma unroll
-  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
-    const int i = tid + k * kAppendThreads;
-    const int tt = i / kRow, r = i % kRow;
-    if (i < kChunks && tt < ntok && r / kCH < HC) {
-      const int64_t col = ((int64_t)h0 * D + (int64_t)r * 16) * kES;
-      *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) =
-          quantize16<T>(p.key + (t0 + tt) * p.k_stride_bytes + col, ks);
-      *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) =
-          quantize16<T>(p.value + (t0 + tt) * p.v_stride_bytes + col, vs);
+    for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+      const int i = tid + k * kAppendThreads;
+      const int tt = i / kRow, r = i % kRow;
+      if (i < kChunks && tt < ntok && r / kCH < HC) {
+        const int64_t col = ((int64_t)h0 * D + (int64_t)r * 16) * kES;
+        *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) =
+            quantize16<T>(p.key + (t0 + tt) * p.k_stride_bytes + col, ks);
+        *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) =
+            quantize16<T>(p.value + (t0 + tt) * p.v_stride_bytes + col, vs);
+      }
     }
-  }
-  __syncthreads();
+    __syncthreads();
 #pragma unroll
-  for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
-    const int i = tid + k * kAppendThreads;
-    const int tt = i % kTile16, r = i / kTile16;
-    const int hc = r / kCH, c = r % kCH;
-    const int64_t sl = s_slot[tt];
-    if (i < kChunks && sl >= 0 && hc < HC) {
-      const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
-      const uint64_t dst = (((blk * (uint64_t)p.num_kv_heads + (uint64_t)(h0 + hc)) * kCH + c) * BS + off) * 16;
-      *reinterpret_cast<uint4 *>(p.k_cache + dst) = *reinterpret_cast<const uint4 *>(kt + tt * kPitch + r * 16);
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < (kVItems + kAppendThreads - 1) / kAppendThreads; ++k) {
-    const int i = tid + k * kAppendThreads;
-    const int g = i % kGroups, hd = i / kGroups;
-    const int hc = hd / D, d = hd % D;
-    if (i >= kVItems || hc >= HC) continue;
-    const unsigned char *src = vt + (g * kTPS) * kPitch + hc * D + d;
-    const uint64_t row = ((uint64_t)h0 + hc) * D + d;
-    if (s_gok[g]) {
-      const uint64_t us = (uint64_t)s_slot[g * kTPS], blk = us / BS, off = us % BS;
-      uint32_t w[kTPS / 4];
-#pragma unroll
-      for (int q = 0; q < kTPS / 4; ++q)
-        w[q] = (uint32_t)src[(4 * q) * kPitch] | ((uint32_t)src[(4 * q + 1) * kPitch] << 8) |
-               ((uint32_t)src[(4 * q + 2) * kPitch] << 16) | ((uint32_t)src[(4 * q + 3) * kPitch] << 24);
-      unsigned char *dst = p.v_cache + (blk * (uint64_t)p.num_kv_heads * D + row) * BS + off;
-      if constexpr (kTPS == 16)
-        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-      else
-        *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < kTPS; ++e) {
-        const int64_t sl = s_slot[g * kTPS + e];
-        if (sl < 0) continue;
+    for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+      const int i = tid + k * kAppendThreads;
+      const int tt = i % kTile16, r = i / kTile16;
+      const int hc = r / kCH, c = r % kCH;
+      const int64_t sl = s_slot[tt];
+      if (i < kChunks && sl >= 0 && hc < HC) {
         const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
-        p.v_cache[(blk * (uint64_t)p.num_kv_heads * D + row) * BS + off] = src[e * kPitch];
+        const uint64_t dst = (((blk * (uint64_t)p.num_kv_heads + (uint64_t)(h0 + hc)) * kCH + c) * BS + off) * 16;
+        *reinterpret_cast<uint4 *>(p.k_cache + dst) = *reinterpret_cast<const uint4 *>(kt + tt * kPitch + r * 16);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < (kVItems + kAppendThreads - 1) / kAppendThreads; ++k) {
+      const int i = tid + k * kAppendThreads;
+      const int g = i % kGroups, hd = i / kGroups;
+      const int hc = hd / D, d = hd % D;
+      if (i >= kVItems || hc >= HC) continue;
+      const unsigned char *src = vt + (g * kTPS) * kPitch + hc * D + d;
+      const uint64_t row = ((uint64_t)h0 + hc) * D + d;
+      if (s_gok[g]) {
+        const uint64_t us = (uint64_t)s_slot[g * kTPS], blk = us / BS, off = us % BS;
+        uint32_t w[kTPS / 4];
+#pragma unroll
+        for (int q = 0; q < kTPS / 4; ++q)
+          w[q] = (uint32_t)src[(4 * q) * kPitch] | ((uint32_t)src[(4 * q + 1) * kPitch] << 8) |
+                 ((uint32_t)src[(4 * q + 2) * kPitch] << 16) | ((uint32_t)src[(4 * q + 3) * kPitch] << 24);
+        unsigned char *dst = p.v_cache + (blk * (uint64_t)p.num_kv_heads * D + row) * BS + off;
+        if constexpr (kTPS == 16)
+          *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        else
+          *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < kTPS; ++e) {
+          const int64_t sl = s_slot[g * kTPS + e];
+          if (sl < 0) continue;
+          const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
+          p.v_cache[(blk * (uint64_t)p.num_kv_heads * D + row) * BS + off] = src[e * kPitch];
+        }
       }
     }
   }
@@ -1031,9 +1056,14 @@ int launch_append_fp8_t(const AppendArgs &a, cudaStream_t stream) {
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
   if (a.num_tokens >= 4096) {  // prefill chunks: 16-token tiles of 2 heads
+    static std::atomic<int64_t> resident[64];
     const int64_t tiles = (a.num_tokens + kTile16 - 1) / kTile16;
-    if (tiles > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
-    dim3 grid((unsigned)tiles, (unsigned)((a.num_kv_heads + 1) / 2));
+    const int hg = (a.num_kv_heads + 1) / 2;
+    p.tiles_per_cta = tile16_per_cta(tiles * hg, resident_ctas(kv_append_fp8_tile16_kernel<T, BS, D, 2>,
+                                                                kAppendThreads, 0, resident));
+    const int64_t gx = (tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
+    if (gx > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+    dim3 grid((unsigned)gx, (unsigned)hg);
     kv_append_fp8_tile16_kernel<T, BS, D, 2><<<grid, kAppendThreads, 0, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }

@@ -243,4 +243,23 @@ inline bool ensure_smem_attr(F *func, int bytes, std::atomic<uint64_t> &done_mas
   return true;
 }
 
+// CTAs of `func` (block `threads`, dynamic shared memory `smem`) resident on
+// the whole current device at once: SM count x blocks per SM, queried once
+// per device (cache[dev] = 0 until then). 0 on error.
+template <typename F>
+inline int64_t resident_ctas(F *func, int threads, size_t smem, std::atomic<int64_t> (&cache)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  int64_t v = cache[dev].load(std::memory_order_acquire);
+  if (v > 0) return v;
+  int sms = 0, per_sm = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void *>(func), threads,
+                                                    smem) != cudaSuccess)
+    return 0;
+  v = (int64_t)sms * per_sm;
+  cache[dev].store(v, std::memory_order_release);
+  return v;
+}
+
 }  // namespace vasr
