@@ -174,19 +174,21 @@ inline int tile16_per_cta(int64_t items, int64_t resident) {
   return t > 64 ? 64 : (int)t;
 }
 
-// Warp 0: the tile's slots into s_slot (out of range -> skipped and flagged)
-// and, per V group of kTPS tokens, whether it is one aligned run of slots.
-template <int BS, int kTPS, int kGroups>
-__device__ __forceinline__ void tile16_slots(const int64_t *slots, int64_t t0, int ntok, int64_t num_blocks,
-                                             int64_t *s_slot, int *s_gok) {
+// Warp 0, lane l < ntok: the slot of token t0 + l (-1 for the other lanes).
+__device__ __forceinline__ int64_t tile16_load_slot(const int64_t *slots, int64_t t0, int ntok) {
   const int lane = threadIdx.x;
-  int64_t sl = -1;
-  if (lane < ntok) {
-    sl = slots[t0 + lane];
-    if (sl >= num_blocks * BS) {
-      raise_device_error(VASR_PA_DERR_SLOT_RANGE);
-      sl = -1;
-    }
+  return lane < ntok ? slots[t0 + lane] : -1;
+}
+
+// Warp 0: the tile's slots (loaded by tile16_load_slot) into s_slot (out of
+// range -> skipped and flagged) and, per V group of kTPS tokens, whether it
+// is one aligned run of slots.
+template <int BS, int kTPS, int kGroups>
+__device__ __forceinline__ void tile16_slots(int64_t sl, int64_t num_blocks, int64_t *s_slot, int *s_gok) {
+  const int lane = threadIdx.x;
+  if (sl >= num_blocks * BS) {
+    raise_device_error(VASR_PA_DERR_SLOT_RANGE);
+    sl = -1;
   }
   if (lane < kTile16) s_slot[lane] = sl;
   const int g0 = lane & ~(kTPS - 1);
@@ -214,28 +216,48 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_tile16_kernel(const 
   __shared__ __align__(16) unsigned char vt[kTile16 * kPitch];
   __shared__ int64_t s_slot[kTile16];
   __shared__ int s_gok[kGroups];
+  constexpr int kLd = (kChunks + kAppendThreads - 1) / kAppendThreads;  // 16-byte loads per thread
   const int tid = threadIdx.x;
   const int h0 = blockIdx.y * HPT;
   const int HC = min(HPT, p.num_kv_heads - h0);
-  for (int it = 0; it < p.tiles_per_cta; ++it) {
-    const int64_t t0 = ((int64_t)blockIdx.x * p.tiles_per_cta + it) * kTile16;
-    if (t0 >= p.num_tokens) break;
-    if (it > 0) __syncthreads();  // the previous tile's staged rows and slots are read
+  // The next tile's rows and slots are loaded into registers while this
+  // tile's stores go out (software pipeline over the CTA's tiles).
+  uint4 kr[kLd], vr[kLd];
+  int64_t sl_next = -1;
+  auto load_tile = [&](int64_t t0) {
     const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
-    if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
+    if (tid < 32) sl_next = tile16_load_slot(p.slots, t0, ntok);
 #pragma unroll
-    for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
+    for (int k = 0; k < kLd; ++k) {
       const int i = tid + k * kAppendThreads;
       const int tt = i / kRow, r = i % kRow;
       if (i < kChunks && tt < ntok && r / kCH < HC) {
         const int64_t col = (int64_t)h0 * D * kES + r * 16;
-        const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(p.key + (t0 + tt) * p.k_stride_bytes + col));
-        const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(p.value + (t0 + tt) * p.v_stride_bytes + col));
-        *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) = kv;
-        *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) = vv;
+        kr[k] = __ldg(reinterpret_cast<const uint4 *>(p.key + (t0 + tt) * p.k_stride_bytes + col));
+        vr[k] = __ldg(reinterpret_cast<const uint4 *>(p.value + (t0 + tt) * p.v_stride_bytes + col));
+      }
+    }
+  };
+  const int64_t first = (int64_t)blockIdx.x * p.tiles_per_cta;
+  if (first * kTile16 >= p.num_tokens) return;
+  load_tile(first * kTile16);
+  for (int it = 0; it < p.tiles_per_cta; ++it) {
+    const int64_t t0 = (first + it) * kTile16;
+    if (t0 >= p.num_tokens) break;
+    if (it > 0) __syncthreads();  // the previous tile's staged rows and slots are read
+    const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
+    if (tid < 32) tile16_slots<BS, kTPS, kGroups>(sl_next, p.num_blocks, s_slot, s_gok);
+#pragma unroll
+    for (int k = 0; k < kLd; ++k) {
+      const int i = tid + k * kAppendThreads;
+      const int tt = i / kRow, r = i % kRow;
+      if (i < kChunks && tt < ntok && r / kCH < HC) {
+        *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) = kr[k];
+        *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) = vr[k];
       }
     }
     __syncthreads();
+    if (it + 1 < p.tiles_per_cta && t0 + kTile16 < p.num_tokens) load_tile(t0 + kTile16);
     // K: item i = (chunk r of the row, token tt), token fastest
 #pragma unroll
     for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
@@ -941,7 +963,8 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_tile16_kernel(co
     if (t0 >= p.num_tokens) break;
     if (it > 0) __syncthreads();  // the previous tile's staged rows and slots are read
     const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
-    if (tid < 32) tile16_slots<BS, kTPS, kGroups>(p.slots, t0, ntok, p.num_blocks, s_slot, s_gok);
+    if (tid < 32)
+      tile16_slots<BS, kTPS, kGroups>(tile16_load_slot(p.slots, t0, ntok), p.num_blocks, s_slot, s_gok);
 #pragma unroll
     for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
       const int i = tid + k * kAppendThreads;
