@@ -31,7 +31,8 @@ every N, one process per GPU, no collective on the hot path).
              captured as one graph and replayed back to back.
   config2    the same step for config 2 (0.6B decoder, 64 sequences per GPU,
              weak scaling) with its decode-kernel roofline.
-  prefill / append / decode_fp8 / copy_blocks / swap_blocks / gather_kv_cache
+  prefill / append / decode_fp8 (config 2) / decode_fp8_config5 / copy_blocks /
+  swap_blocks / gather_kv_cache
              (one GPU only) each kernel on its BASELINE config, timed with
              CUDA events over a captured graph of launches whose inputs
              together exceed L2: us, achieved, peak, frac.
@@ -584,10 +585,18 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        # NCCL's communicator lines (rank count per communicator) stay in the log
+        # NCCL's own init lines stay in the log; rank 0 adds a one-line summary
+        # of the communicator (the only NCCL traffic: barriers and the
+        # max-over-ranks reductions of the timings, outside the timed regions)
         os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+        dist.barrier()
+        if rank == 0:
+            ver = torch.cuda.nccl.version()
+            print(json.dumps({"nccl": {"version": ".".join(map(str, ver)) if isinstance(ver, tuple) else ver,
+                                       "backend": dist.get_backend(), "world_size": world,
+                                       "collectives": "barrier + all-reduce(max) of timings, outside timed regions"}}),
+                  file=sys.stderr, flush=True)
     ranks = Ranks(world, dev)
     peak, peak_kind = load_peaks()
 
@@ -635,7 +644,8 @@ def run_ours(args):
     if world == 1 and not args.no_extras:
         # each kernel on its own BASELINE config (one GPU; inputs cycled beyond L2)
         for name, kern in (("prefill", "prefill"), ("append", "append"), ("decode_fp8", "decode_fp8"),
-                           ("copy_blocks", "copy"), ("swap_blocks", "swap"), ("gather_kv_cache", "gather")):
+                           ("decode_fp8_config5", "decode5_fp8"), ("copy_blocks", "copy"),
+                           ("swap_blocks", "swap"), ("gather_kv_cache", "gather")):
             lines = KERNEL_BENCH[kern](args, torch.device("cuda", local))
             extras[name] = lines[0] if len(lines) == 1 else {ln["config"]: ln for ln in lines}
             torch.cuda.empty_cache()
