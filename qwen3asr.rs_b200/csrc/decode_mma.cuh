@@ -78,6 +78,135 @@ __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t v16) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// One stage of a warp's tokens (n_valid of them, kNTT tiles of 16 at sk / sv
+// in shared memory) through the tensor cores: per 16-token tile S = Q Kᵀ,
+// the running-max softmax update of rows 0 / 1 (lanes 0-7) and O += P V.
+template <typename T, int BS, int D, typename TC, int kNTT, int kPB>
+__device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_valid,
+                                              const uint32_t (&qa)[D / 16][2], float c_log2,
+                                              bool use_softcap, float scale, float softcap,
+                                              float (&o)[D / 8][4], float &m_used, float &l_part) {
+  constexpr bool kFp8 = std::is_same<TC, __nv_fp8_e4m3>::value;
+  using TM = typename std::conditional<kFp8, __half, T>::type;  // MMA operand type
+  constexpr int kKS = D / 16;
+  constexpr float kRescale = 8.f;
+  const int lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int ti = 0; ti < kNTT; ++ti) {
+    const int t0 = ti * 16;  // first token of this 16-token tile within the stage
+    if (t0 >= n_valid) break;
+    // ---- S = Q K^T (two 8-token n-tiles)
+    float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if constexpr (kFp8) {
+      // matrices: (n-tile 0, chunk 2kp), (n-tile 1, 2kp), (n-tile 0, 2kp+1), (n-tile 1, 2kp+1)
+      const int r = lane & 7;
+      const int ktok = t0 + 4 * (r >> 1) + 2 * ((lane >> 3) & 1) + (r & 1);
+      const uint32_t krow = sk + (ktok / BS) * kPB + ((lane >> 4) * BS + ktok % BS) * 16;
+#pragma unroll
+      for (int kp = 0; kp < kKS / 2; ++kp) {
+        uint32_t r0, r1, r2, r3;
+        dec_ldmatrix_x4(krow + kp * 2 * (BS * 16), r0, r1, r2, r3);
+        dec_mma<TM>(sacc[0], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r0), fp8x2_to_h2(r0 >> 16));
+        dec_mma<TM>(sacc[1], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r1), fp8x2_to_h2(r1 >> 16));
+        dec_mma<TM>(sacc[0], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r2),
+                    fp8x2_to_h2(r2 >> 16));
+        dec_mma<TM>(sacc[1], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r3),
+                    fp8x2_to_h2(r3 >> 16));
+      }
+    } else {
+      const int ktok = t0 + (lane & 7) + (lane >> 4) * 8;
+      const uint32_t krow = sk + (ktok / BS) * kPB + (ktok % BS) * 16 + ((lane >> 3) & 1) * (BS * 16);
+#pragma unroll
+      for (int ks = 0; ks < kKS; ++ks) {
+        uint32_t b0, b1, b2, b3;
+        dec_ldmatrix_x4(krow + ks * 2 * (BS * 16), b0, b1, b2, b3);
+        dec_mma<TM>(sacc[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+        dec_mma<TM>(sacc[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+      }
+    }
+    // ---- scores of row grp: tokens t0 + n*8 + tig*2 + {0, 1}
+    float x[4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float v = sacc[n][e];
+        if (use_softcap) v = softcap * tanhf(v * scale / softcap) * kLog2e;
+        else v *= c_log2;
+        const int tok = kFp8 ? t0 + 4 * tig + 2 * n + e : t0 + n * 8 + tig * 2 + e;
+        x[n * 2 + e] = (tok < n_valid) ? v : -INFINITY;
+      }
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (__any_sync(0xffffffffu, mx > m_used + kRescale)) {
+      const float m_new = fmaxf(m_used, mx);
+      const float alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
+      m_used = m_new;
+      l_part *= alpha;
+#pragma unroll
+      for (int j = 0; j < D / 8; ++j) {
+        o[j][0] *= alpha;
+        o[j][1] *= alpha;
+      }
+    }
+    const float off = (m_used == -INFINITY) ? 0.f : m_used;
+    float pv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      pv[e] = exp2f(x[e] - off);
+      l_part += pv[e];
+    }
+    // P as the A operand (rows 8-15 zero): k = tokens of the tile
+    const uint32_t pa0 = dec_pack2<TM>(pv[0], pv[1]), pa2 = dec_pack2<TM>(pv[2], pv[3]);
+    const bool tail = (t0 + 16 > n_valid);
+    if constexpr (kFp8) {
+      // ---- O += P V: one ldmatrix row = the tile's 16 tokens of one dim;
+      // matrix j of an x4 = 8 dims, lane tig holds tokens 4 tig .. 4 tig + 3
+      const int vd = (lane >> 3) * 8 + (lane & 7);
+      const uint32_t vrow = sv + (t0 / BS) * kPB + vd * BS + t0 % BS;
+      const int tk = t0 + 4 * tig;
+      const uint32_t mlo = (tk < n_valid ? 0xffffu : 0u) | (tk + 1 < n_valid ? 0xffff0000u : 0u);
+      const uint32_t mhi = (tk + 2 < n_valid ? 0xffffu : 0u) | (tk + 3 < n_valid ? 0xffff0000u : 0u);
+#pragma unroll
+      for (int dq = 0; dq < D / 32; ++dq) {
+        uint32_t r[4];
+        dec_ldmatrix_x4(vrow + dq * 32 * BS, r[0], r[1], r[2], r[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t b0 = fp8x2_to_h2(r[j]), b1 = fp8x2_to_h2(r[j] >> 16);
+          if (tail) {
+            b0 &= mlo;
+            b1 &= mhi;
+          }
+          dec_mma<TM>(o[dq * 4 + j], pa0, 0u, pa2, 0u, b0, b1);
+        }
+      }
+      continue;
+    }
+    // ---- O += P V: V rows = dims, 8 tokens per ldmatrix row
+    const int vd = (lane & 7) + (lane >> 4) * 8;
+    const int vtok = t0 + ((lane >> 3) & 1) * 8;
+    const uint32_t vrow = sv + (vtok / BS) * kPB + (vd * BS + vtok % BS) * 2;
+    const int tk0 = t0 + tig * 2;  // tokens of b0 / b2 halves; b1 / b3: +8
+#pragma unroll
+    for (int dp = 0; dp < D / 16; ++dp) {
+      uint32_t b0, b1, b2, b3;
+      dec_ldmatrix_x4(vrow + dp * 16 * BS * 2, b0, b1, b2, b3);
+      if (tail) {
+        const uint32_t m0 = (tk0 < n_valid ? 0xffffu : 0u) | (tk0 + 1 < n_valid ? 0xffff0000u : 0u);
+        const uint32_t m1 = (tk0 + 8 < n_valid ? 0xffffu : 0u) | (tk0 + 9 < n_valid ? 0xffff0000u : 0u);
+        b0 &= m0;
+        b2 &= m0;
+        b1 &= m1;
+        b3 &= m1;
+      }
+      dec_mma<TM>(o[2 * dp], pa0, 0u, pa2, 0u, b0, b1);
+      dec_mma<TM>(o[2 * dp + 1], pa0, 0u, pa2, 0u, b2, b3);
+    }
+  }
+}
+
 // TC = T: bf16 / f16 pages, the MMAs in T. TC = fp8 E4M3 (bs 16 or 32): the
 // MMAs run in f16 on pages converted in registers, and the reduction index is
 // permuted so one ldmatrix row of 16 fp8 bytes feeds one k-step: lane tig
@@ -219,120 +348,8 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
     const int n_valid = min(C::kST, tok_end - (tok_begin + u * C::kST));
     const uint32_t sk = s_base + C::kOffK + s * C::kSP * C::kPB;
     const uint32_t sv = s_base + C::kOffV + s * C::kSP * C::kPB;
-#pragma unroll
-    for (int ti = 0; ti < C::kNTT; ++ti) {
-      const int t0 = ti * 16;  // first token of this 16-token tile within the stage
-      if (t0 >= n_valid) break;
-      // ---- S = Q K^T (two 8-token n-tiles)
-      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      if constexpr (kFp8) {
-        // matrices: (n-tile 0, chunk 2kp), (n-tile 1, 2kp), (n-tile 0, 2kp+1), (n-tile 1, 2kp+1)
-        const int r = lane & 7;
-        const int ktok = t0 + 4 * (r >> 1) + 2 * ((lane >> 3) & 1) + (r & 1);
-        const uint32_t krow = sk + (ktok / BS) * C::kPB + ((lane >> 4) * BS + ktok % BS) * 16;
-#pragma unroll
-        for (int kp = 0; kp < kKS / 2; ++kp) {
-          uint32_t r0, r1, r2, r3;
-          dec_ldmatrix_x4(krow + kp * 2 * (BS * 16), r0, r1, r2, r3);
-          dec_mma<TM>(sacc[0], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r0), fp8x2_to_h2(r0 >> 16));
-          dec_mma<TM>(sacc[1], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r1), fp8x2_to_h2(r1 >> 16));
-          dec_mma<TM>(sacc[0], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r2),
-                      fp8x2_to_h2(r2 >> 16));
-          dec_mma<TM>(sacc[1], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r3),
-                      fp8x2_to_h2(r3 >> 16));
-        }
-      } else {
-        const int ktok = t0 + (lane & 7) + (lane >> 4) * 8;
-        const uint32_t krow = sk + (ktok / BS) * C::kPB + (ktok % BS) * 16 + ((lane >> 3) & 1) * (BS * 16);
-#pragma unroll
-        for (int ks = 0; ks < kKS; ++ks) {
-          uint32_t b0, b1, b2, b3;
-          dec_ldmatrix_x4(krow + ks * 2 * (BS * 16), b0, b1, b2, b3);
-          dec_mma<TM>(sacc[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
-          dec_mma<TM>(sacc[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
-        }
-      }
-      // ---- scores of row grp: tokens t0 + n*8 + tig*2 + {0, 1}
-      float x[4];
-#pragma unroll
-      for (int n = 0; n < 2; ++n)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float v = sacc[n][e];
-          if (use_softcap) v = p.softcap * tanhf(v * p.scale / p.softcap) * kLog2e;
-          else v *= c_log2;
-          const int tok = kFp8 ? t0 + 4 * tig + 2 * n + e : t0 + n * 8 + tig * 2 + e;
-          x[n * 2 + e] = (tok < n_valid) ? v : -INFINITY;
-        }
-      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      if (__any_sync(0xffffffffu, mx > m_used + kRescale)) {
-        const float m_new = fmaxf(m_used, mx);
-        const float alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
-        m_used = m_new;
-        l_part *= alpha;
-#pragma unroll
-        for (int j = 0; j < D / 8; ++j) {
-          o[j][0] *= alpha;
-          o[j][1] *= alpha;
-        }
-      }
-      const float off = (m_used == -INFINITY) ? 0.f : m_used;
-      float pv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        pv[e] = exp2f(x[e] - off);
-        l_part += pv[e];
-      }
-      // P as the A operand (rows 8-15 zero): k = tokens of the tile
-      const uint32_t pa0 = dec_pack2<TM>(pv[0], pv[1]), pa2 = dec_pack2<TM>(pv[2], pv[3]);
-      const bool tail = (t0 + 16 > n_valid);
-      if constexpr (kFp8) {
-        // ---- O += P V: one ldmatrix row = the tile's 16 tokens of one dim;
-        // matrix j of an x4 = 8 dims, lane tig holds tokens 4 tig .. 4 tig + 3
-        const int vd = (lane >> 3) * 8 + (lane & 7);
-        const uint32_t vrow = sv + (t0 / BS) * C::kPB + vd * BS + t0 % BS;
-        const int tk = t0 + 4 * tig;
-        const uint32_t mlo = (tk < n_valid ? 0xffffu : 0u) | (tk + 1 < n_valid ? 0xffff0000u : 0u);
-        const uint32_t mhi = (tk + 2 < n_valid ? 0xffffu : 0u) | (tk + 3 < n_valid ? 0xffff0000u : 0u);
-#pragma unroll
-        for (int dq = 0; dq < D / 32; ++dq) {
-          uint32_t r[4];
-          dec_ldmatrix_x4(vrow + dq * 32 * BS, r[0], r[1], r[2], r[3]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t b0 = fp8x2_to_h2(r[j]), b1 = fp8x2_to_h2(r[j] >> 16);
-            if (tail) {
-              b0 &= mlo;
-              b1 &= mhi;
-            }
-            dec_mma<TM>(o[dq * 4 + j], pa0, 0u, pa2, 0u, b0, b1);
-          }
-        }
-        continue;
-      }
-      // ---- O += P V: V rows = dims, 8 tokens per ldmatrix row
-      const int vd = (lane & 7) + (lane >> 4) * 8;
-      const int vtok = t0 + ((lane >> 3) & 1) * 8;
-      const uint32_t vrow = sv + (vtok / BS) * C::kPB + (vd * BS + vtok % BS) * 2;
-      const int tk0 = t0 + tig * 2;  // tokens of b0 / b2 halves; b1 / b3: +8
-#pragma unroll
-      for (int dp = 0; dp < D / 16; ++dp) {
-        uint32_t b0, b1, b2, b3;
-        dec_ldmatrix_x4(vrow + dp * 16 * BS * 2, b0, b1, b2, b3);
-        if (tail) {
-          const uint32_t m0 = (tk0 < n_valid ? 0xffffu : 0u) | (tk0 + 1 < n_valid ? 0xffff0000u : 0u);
-          const uint32_t m1 = (tk0 + 8 < n_valid ? 0xffffu : 0u) | (tk0 + 9 < n_valid ? 0xffff0000u : 0u);
-          b0 &= m0;
-          b2 &= m0;
-          b1 &= m1;
-          b3 &= m1;
-        }
-        dec_mma<TM>(o[2 * dp], pa0, 0u, pa2, 0u, b0, b1);
-        dec_mma<TM>(o[2 * dp + 1], pa0, 0u, pa2, 0u, b2, b3);
-      }
-    }
+    dec_mma_stage<T, BS, D, TC, C::kNTT, C::kPB>(sk, sv, n_valid, qa, c_log2, use_softcap, p.scale,
+                                                  p.softcap, o, m_used, l_part);
     __syncwarp();
     const int nu = u + C::kNST;
     if (nu < n_units && lane == 0) {
