@@ -280,22 +280,137 @@ __device__ __forceinline__ uint32_t pack2f<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// ---------------------------------------------- split items: cluster combine
+// Every thread of every CTA of the cluster: a full cluster barrier (arrive has
+// release, wait acquire semantics, so shared-memory writes before it are
+// visible to the cluster's reads after it).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// the shared-memory address `addr` of this CTA, in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float2 ld_cluster_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+constexpr int kMaxSplits = 8;             // CTAs per cluster (portable limit)
+constexpr int kCPitch = kD + 4;           // floats per staged O row (rows 16 bytes apart mod 128)
+constexpr int kOffRed = kOffQ + kM * kCPitch * 4;  // (m, l) per row
+static_assert(kOffRed + kM * 8 <= kOffBar, "the combine staging fits in the Q, K and V buffers");
+
+// The softmax threads (row r each) of one CTA of a split item. After the
+// CTA's last barrier (which the loader and MMA warps meet before their two
+// cluster barriers) the CTA's unnormalised O rows (f32) and (m, l) go to its
+// own shared memory; after a cluster barrier each CTA reads every CTA's rows
+// for its share of the 32 four-dim chunks, weights them by 2^(m_s - M) and
+// writes O / L for those dims; a second cluster barrier keeps every CTA's
+// shared memory alive until all reads are done. A CTA without key tiles (or
+// whose waits gave up) contributes m = -inf and zeros.
 template <typename T, int G>
+__device__ void combine_splits(unsigned char *smem, uint32_t sbase, uint32_t t_o, int r, bool have,
+                               float m, float l, int splits, int n_pos, T *out, int64_t row_stride) {
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  float *stg = reinterpret_cast<float *>(smem + kOffQ) + r * kCPitch;
+#pragma unroll 1
+  for (int cc = 0; cc < kD; cc += 32) {
+    uint32_t o[32];
+    tmem_ld32(t_o + cc, o);  // warp-collective
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      *reinterpret_cast<float4 *>(stg + cc + 4 * i) =
+          have ? make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                             __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]))
+               : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  reinterpret_cast<float2 *>(smem + kOffRed)[r] = have ? make_float2(m, l) : make_float2(-INFINITY, 0.f);
+  cluster_sync_all();
+  const uint32_t me = cluster_rank();
+  float w[kMaxSplits];
+  float M = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < kMaxSplits; ++s) {
+    w[s] = -INFINITY;
+    if (s < splits) {
+      const float2 ml = ld_cluster_f2(cluster_map(sbase + kOffRed + r * 8, (uint32_t)s));
+      w[s] = ml.x;
+      M = fmaxf(M, ml.x);
+    }
+  }
+  float L = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMaxSplits; ++s) {
+    if (s >= splits) continue;
+    const float2 ml = ld_cluster_f2(cluster_map(sbase + kOffRed + r * 8, (uint32_t)s));
+    w[s] = (M == -INFINITY || ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+    L = fmaf(ml.y, w[s], L);
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int c0 = (int)(me * (kD / 4) / splits), c1 = (int)((me + 1) * (kD / 4) / splits);
+  const bool row_ok = (r / G) < n_pos;
+  T *orow = out + (int64_t)(r / G) * row_stride + (int64_t)(r % G) * kD;
+  for (int c = c0; c < c1; ++c) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s) {
+      if (s >= splits) continue;
+      const float4 v = ld_cluster_f4(cluster_map(sbase + kOffQ + (uint32_t)(r * kCPitch + 4 * c) * 4, (uint32_t)s));
+      acc.x = fmaf(v.x, w[s], acc.x);
+      acc.y = fmaf(v.y, w[s], acc.y);
+      acc.z = fmaf(v.z, w[s], acc.z);
+      acc.w = fmaf(v.w, w[s], acc.w);
+    }
+    if (row_ok)
+      *reinterpret_cast<uint2 *>(orow + 4 * c) =
+          make_uint2(pack2f<T>(acc.x * inv, acc.y * inv), pack2f<T>(acc.z * inv, acc.w * inv));
+  }
+  cluster_sync_all();
+}
+
+// kSplit: launched as clusters of `splits` CTAs per item (else splits == 1
+// and the split code compiles away)
+template <typename T, int G, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 2)
-    prefill_umma_kernel(const PrefillArgs p, const int tiles,
+    prefill_umma_kernel(const PrefillArgs p, const int tiles, const int splits_arg,
                         const __grid_constant__ CUtensorMap q_map) {
+  const int splits = kSplit ? splits_arg : 1;
   constexpr int kPos = kM / G;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t sbase = (raw + kSmemAlign - 1) & ~(uint32_t)(kSmemAlign - 1);
   unsigned char *smem = smem_raw + (sbase - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // ---- work item: blockIdx.x = (r * num_seqs + b) * Hkv + kv head, tile =
-  // tiles - 1 - r. The hardware hands out CTAs in index order, so every
-  // sequence's last position tile (the one with the most keys) goes first
-  // and the kv heads of one (sequence, tile) run side by side.
-  const int kvh = (int)(blockIdx.x % (unsigned)p.num_kv_heads);
-  const int item = (int)(blockIdx.x / (unsigned)p.num_kv_heads);
+  // ---- work item: blockIdx.x / splits = (r * num_seqs + b) * Hkv + kv head,
+  // tile = tiles - 1 - r. The hardware hands out CTAs in index order, so
+  // every sequence's last position tile (the one with the most keys) goes
+  // first and the kv heads of one (sequence, tile) run side by side. With
+  // splits > 1 the item's `splits` CTAs form a cluster, each takes an equal
+  // share of its key tiles, and their partial results are combined through
+  // distributed shared memory.
+  const int citem = (int)(blockIdx.x / (unsigned)splits);
+  const int kvh = (int)(citem % p.num_kv_heads);
+  const int item = citem / p.num_kv_heads;
   const int b = item % p.num_seqs, tile = tiles - 1 - item / p.num_seqs;
   if (warp == kLoadWarp && lane == 0) prefetch_tensormap(&q_map);
 
@@ -339,6 +454,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   const int n_pages = (kv_end + kBS - 1) / kBS;
   const int n_kt = (kv_end + kNT - 1) / kNT;
+  // this CTA's key tiles jb .. jb + n_loc - 1 (all of them without splits)
+  const int split = (int)(blockIdx.x % (unsigned)splits);
+  const int jb = (int)((int64_t)split * n_kt / splits);
+  const int n_loc = (int)((int64_t)(split + 1) * n_kt / splits) - jb;
+  // leaving: every warp passes the CTA's last barrier, then (with splits)
+  // the two cluster barriers around the combine
+  auto cluster_tail = [&]() {
+    if constexpr (kSplit) {
+      cluster_sync_all();
+      cluster_sync_all();
+    }
+  };
   const uint32_t bar = sbase + kOffBar;
   auto B = [&](int i) { return bar + 8u * (uint32_t)i; };
 
@@ -381,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // instruction i moves chunk i / 2 of keys (i & 1) * 32 + lane, i.e. 16
       // bytes at c * 256 + token * 16 of page (i & 1) * 2 + lane / 16
       int np;
-      const uint32_t id = tile_page(j, np);
+      const uint32_t id = tile_page(jb + j, np);
       const int pga = lane >> 4, pgb = pga + 2, tok = lane & (kBS - 1);
       const uint32_t ida = __shfl_sync(0xffffffffu, id, pga), idb = __shfl_sync(0xffffffffu, id, pgb);
       const unsigned char *kc = static_cast<const unsigned char *>(p.key_cache);
@@ -395,15 +522,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       cp_async_arrive_noinc(B(kBarFullK + (j & 1)));  // one of 32 arrivals, when this lane's copies land
     };
-    load_k(0);
-    if (n_kt > 1) load_k(1);
-    int k_issued = min(n_kt, 2);
+    if (n_loc > 0) load_k(0);
+    if (n_loc > 1) load_k(1);
+    int k_issued = min(n_loc, 2);
     __syncthreads();
     // Q K^T j completes in order; K j + 2 goes into its stage once it has.
     // Once a wait gives up, nothing more is issued: a stage whose reader has
     // not finished must not receive another copy.
     bool dead = false;
-    for (int j = 2; j < n_kt && !dead; ++j) {
+    for (int j = 2; j < n_loc && !dead; ++j) {
       wait_phase(B(kBarEmptyK + (j & 1)), ((j >> 1) - 1) & 1, dead);
       if (dead) break;
       load_k(j);
@@ -416,6 +543,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = max(0, k_issued - kStages); j < k_issued; ++j)
       wait_phase(B(kBarFullK + (j & 1)), (j >> 1) & 1, dead);
     __syncthreads();
+    cluster_tail();
     return;
   }
   if (warp == kVLoadWarp) {
@@ -429,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // half h of dim row d of page i / 8, (d, h) = ((i % 8) * 32 + lane) /
       // 2, % 2, to its place in the 32-byte-swizzled page image
       int np;
-      const uint32_t id = tile_page(j, np);
+      const uint32_t id = tile_page(jb + j, np);
       const unsigned char *vc = static_cast<const unsigned char *>(p.value_cache);
       const uint32_t dst = sbase + kOffV + (j & 1) * kKVTile;
 #pragma unroll
@@ -446,11 +574,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       cp_async_arrive_noinc(B(kBarFullV + (j & 1)));  // one of 32 arrivals
     };
     __syncthreads();
-    load_v(0);
-    if (n_kt > 1) load_v(1);
-    int v_issued = min(n_kt, 2);
+    if (n_loc > 0) load_v(0);
+    if (n_loc > 1) load_v(1);
+    int v_issued = min(n_loc, 2);
     bool dead = false;
-    for (int j = 2; j < n_kt && !dead; ++j) {
+    for (int j = 2; j < n_loc && !dead; ++j) {
       wait_phase(B(kBarEmptyV + (j & 1)), ((j >> 1) - 1) & 1, dead);
       if (dead) break;
       load_v(j);
@@ -460,6 +588,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = max(0, v_issued - kStages); j < v_issued; ++j)
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
     __syncthreads();
+    cluster_tail();
     return;
   }
 
@@ -506,17 +635,17 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
     };
     wait_phase(B(kBarQ), 0, dead);
-    if (!dead) issue_s(0);
-    if (n_kt > 1 && !dead) issue_s(1);
-    for (int j = 0; j < n_kt && !dead; ++j) {
+    if (n_loc > 0 && !dead) issue_s(0);
+    if (n_loc > 1 && !dead) issue_s(1);
+    for (int j = 0; j < n_loc && !dead; ++j) {
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
       if (dead) break;
       fence_proxy_async_smem();  // the V copies are generic-proxy writes
-      if (j == n_kt - 1 && (kv_end % kBS) != 0) {
+      if (jb + j == n_kt - 1 && (kv_end % kBS) != 0) {
         // V of tokens >= kv_end in the last page holds other data (possibly
         // non-finite); zero it so that P = 0 there contributes exactly 0.
-        const int pl = (kv_end - 1) / kBS - j * kPagesPerTile;
-        const int valid = kv_end - (j * kPagesPerTile + pl) * kBS;
+        const int pl = (kv_end - 1) / kBS - (jb + j) * kPagesPerTile;
+        const int valid = kv_end - ((jb + j) * kPagesPerTile + pl) * kBS;
         zero_v_page_tail(smem + kOffV + (j & 1) * kKVTile + pl * kPageBytes, valid, lane);
         fence_proxy_async_smem();
         __syncwarp();
@@ -526,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (dead) break;
       tc_fence_after();
       {
-        const int np = min(kPagesPerTile, n_pages - j * kPagesPerTile);
+        const int np = min(kPagesPerTile, n_pages - (jb + j) * kPagesPerTile);
         const uint64_t vd = vd0 + (uint64_t)(((j & 1) * kKVTile) >> 4);
         for (int pg = 0; pg < np; ++pg)
           umma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * kNT + pg * (kBS / 2),
@@ -536,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         last_par = (j >> 1) & 1;
       }
       __syncwarp();
-      if (j + 2 < n_kt) {
+      if (j + 2 < n_loc) {
         // Q K^T j + 2 overwrites the S buffer that holds P j: the tensor core
         // does not order a later MMA's D writes after an earlier MMA's TMEM A
         // reads, so P V j must have completed first.
@@ -556,6 +685,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     tc_fence_before();
     __syncthreads();
+    cluster_tail();
     return;
   }
 
@@ -567,7 +697,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const bool use_softcap = (p.softcapping != 1.0f) && (p.softcapping > 0.f);
   const float cx = use_softcap ? 1.f : p.scale * kLog2e;
   float m = -INFINITY, l = 0.f;
-  for (int j = 0; j < n_kt; ++j) {
+  for (int j = 0; j < n_loc; ++j) {
     wait_phase(B(kBarSFull + (j & 1)), (j >> 1) & 1, dead);
     tc_fence_after();
     uint32_t u[kNT];
@@ -575,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     tmem_ld32(ts, u);
     tmem_ld32(ts + 32, u + 32);
     tmem_wait_ld();
-    const int kmax = lim - j * kNT;  // elements k <= kmax are visible to this row
+    const int kmax = lim - (jb + j) * kNT;  // elements k <= kmax are visible to this row
     // x holds raw scores (exponent x * c - m) or, with softcapping, log2-domain
     // capped logits (c = 1); m is kept in log2 units either way.
     float x[kNT];
@@ -640,8 +770,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---- epilogue: O / l -> out (the last P V commit covers every MMA)
-  wait_phase(B(kBarPvDone + ((n_kt - 1) & 1)), ((n_kt - 1) >> 1) & 1, dead);
+  if (n_loc > 0) wait_phase(B(kBarPvDone + ((n_loc - 1) & 1)), ((n_loc - 1) >> 1) & 1, dead);
   tc_fence_after();
+  if constexpr (kSplit) {
+    combine_splits<T, G>(smem, sbase, tmem + lane_base + kTmemO, r, n_loc > 0 && !dead, m, l, splits,
+                         n_pos, out + (q0 + i0) * row_stride + (int64_t)kvh * G * kD, row_stride);
+    if (warp == 0) {
+      tc_fence_after();
+      tmem_dealloc(tmem, kTmemCols);
+    }
+    return;
+  }
   const float inv = l > 0.f ? 1.f / l : 0.f;
   // O / l (16-bit) is staged in the Q buffer, which no MMA reads any more:
   // row r at r * 256 bytes, its 16-byte chunk c at slot c ^ (r % 16), so a
@@ -721,14 +860,55 @@ bool make_q_map(CUtensorMap *map, const PrefillArgs &a, int g) {
 
 template <typename T, int G>
 int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
-  static std::atomic<uint64_t> attr_done{0};
-  if (!ensure_smem_attr(prefill_umma_kernel<T, G>, kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
+  static std::atomic<uint64_t> attr_done{0}, attr_done_split{0};
+  if (!ensure_smem_attr(prefill_umma_kernel<T, G, false>, kSmemBytes, attr_done) ||
+      !ensure_smem_attr(prefill_umma_kernel<T, G, true>, kSmemBytes, attr_done_split))
+    return VASR_PA_ELAUNCH;
   constexpr int kPos = kM / G;
   const int64_t tiles = prefill_tiles_per_seq(a, kPos);
-  if (tiles <= 0 || tiles * a.num_seqs * a.num_kv_heads > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
-  dim3 grid((unsigned)(tiles * a.num_seqs * a.num_kv_heads));
-  prefill_umma_kernel<T, G><<<grid, kThreads, kSmemBytes, s>>>(a, (int)tiles, qmap);
-  return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+  const int64_t items = tiles * a.num_seqs * a.num_kv_heads;
+  if (tiles <= 0 || items * kMaxSplits > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+  // Few items (a long context with few new tokens: the last chunk rounds)
+  // leave most SMs idle while each CTA walks its key tiles one by one: then
+  // each item's tiles are shared by a cluster of CTAs, as many as fill about
+  // one CTA per SM and leave at least one key tile each (bounded by the
+  // block table's width), combined through distributed shared memory.
+  static std::atomic<int64_t> sm_cache[64];
+  int splits = 1;
+  {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+      sms = (int)sm_cache[dev].load(std::memory_order_acquire);
+      if (sms == 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+        sm_cache[dev].store(sms, std::memory_order_release);
+    }
+    const int64_t kt_bound = ((int64_t)a.max_num_blocks_per_seq * kBS + kNT - 1) / kNT;
+    if (sms > 0 && items * 2 <= sms) {
+      int64_t sp = sms / items;
+      if (sp > kMaxSplits) sp = kMaxSplits;
+      if (sp > kt_bound) sp = kt_bound;
+      splits = sp >= 2 ? (int)sp : 1;
+    }
+  }
+  if (splits == 1) {
+    prefill_umma_kernel<T, G, false><<<dim3((unsigned)items), kThreads, kSmemBytes, s>>>(a, (int)tiles, 1, qmap);
+    return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(items * splits));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prefill_umma_kernel<T, G, true>, a, (int)tiles, splits, qmap) == cudaSuccess
+             ? VASR_PA_OK
+             : VASR_PA_ELAUNCH;
 }
 
 }  // namespace

@@ -103,3 +103,13 @@ def test_prefill_max_query_len_bound(cuda_device):
     assert pa.device_error() == 0
     pa.paged_attention_varlen_prefill(*args, 20)
     assert pa.device_error(clear=True) & 0x20  # VASR_PA_DERR_QLEN_RANGE
+
+
+@pytest.mark.parametrize("cached,chunk", [([1500, 20], [12, 9]), ([780], [12]), ([900, 600, 64], [3, 40, 1])])
+def test_prefill_split_items_long_context(cuda_device, cached, chunk):
+    """Few items over long contexts: each item's key tiles are shared by a cluster of CTAs
+    (up to 8, combined through distributed shared memory). Short sequences next to a long one
+    have fewer key tiles than CTAs in their cluster, so some CTAs hold none."""
+    case = make_prefill_case(7, cached, chunk, dtype="bf16")
+    got = run_prefill(case, cuda_device)
+    assert np.abs(got - oracle_prefill(case)).max() <= TOL["bf16"]
