@@ -84,10 +84,13 @@ constexpr int kSmemAlign = 1024;             // SW128 Q tile: 1024-byte alignmen
 constexpr int kSmemBytes = kSmemUsed + kSmemAlign;
 constexpr int kTmemCols = 256;               // S ring 2 x 64 columns + O 128 columns
 constexpr int kTmemS = 0, kTmemO = 128;
-constexpr int kThreads = 224;              // warps 0-3 rows, 4 MMA, 5 Q + K loads, 6 V loads
+// warps 0-3 rows, 4 P V MMAs, 5 Q + K loads, 6 V loads, 7 Q K^T MMAs; the
+// split variant has no warp 7 (warp 4 issues both kinds of MMA there)
+constexpr int kThreadsFor(bool split) { return split ? 224 : 256; }
 constexpr int kMmaWarp = 4;
 constexpr int kLoadWarp = 5;
 constexpr int kVLoadWarp = 6;
+constexpr int kSMmaWarp = 7;
 constexpr int kIdRegs = 4;                 // block ids of pages 0..127 held in registers
 constexpr float kRescaleLog2 = 8.f;          // rescale O only when the max grows > 2^8
 constexpr uint64_t kWaitNs = 200000000ull;   // 200 ms per wait before giving up
@@ -391,7 +394,7 @@ __device__ void combine_splits(unsigned char *smem, uint32_t sbase, uint32_t t_o
 // kSplit: launched as clusters of `splits` CTAs per item (else splits == 1
 // and the split code compiles away)
 template <typename T, int G, bool kSplit>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
     prefill_umma_kernel(const PrefillArgs p, const int tiles, const int splits_arg,
                         const __grid_constant__ CUtensorMap q_map) {
   const int splits = kSplit ? splits_arg : 1;
@@ -445,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   T *out = reinterpret_cast<T *>(p.out);
   const int64_t row_stride = (int64_t)p.num_heads * kD;
   if (kv_end <= 0) {
-    for (int e = tid; e < n_pos * G * kD; e += kThreads) {
+    for (int e = tid; e < n_pos * G * kD; e += kThreadsFor(kSplit)) {
       const int r = e / kD, d = e % kD;
       out[(q0 + i0 + r / G) * row_stride + (int64_t)(kvh * G + r % G) * kD + d] =
           Elem<T>::from_f32(0.f);
@@ -592,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     return;
   }
 
-  // ------------------------------------------------------ warps 0-4
+  // ------------------------------------------------------ warps 0-4 and 7
   if (warp == 0) tmem_alloc(sbase + kOffTmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
@@ -600,10 +603,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = *reinterpret_cast<const uint32_t *>(smem + kOffTmemSlot);
   bool dead = false;  // this warp gave up on a wait
 
-  if (warp == kMmaWarp) {
-    // ---------------------------------------------------------- MMA issuer
-    // Order on the tensor core: Q K^T 0, Q K^T 1, then per tile j: P V j,
-    // Q K^T j + 2. Backpressure from the tensor core stalls only this warp.
+  if (warp == kMmaWarp || warp == kSMmaWarp) {
+    // ------------------------------------------------------- MMA issuers
+    // Two issuing warps, so that neither kind of MMA waits behind the other's
+    // issue (an MMA's issue stalls while the tensor core is busy): warp 7
+    // issues Q K^T j into S buffer j & 1 once P V j - 2, the last reader of
+    // that buffer (P j - 2 lives there), has completed; warp 4 issues P V j
+    // once P j is stored. Each warp's commits track only its own MMAs. The
+    // split variant (CTAs of one or two key tiles) issues both from warp 4,
+    // which measured faster there.
     const uint32_t idesc_s = idesc_f16<T>(kNT), idesc_o = idesc_f16<T>(kD);
     // Descriptors are built once; a later operand differs only in its start
     // address, the low field of the descriptor (address / 16 < 2^14 for any
@@ -622,24 +630,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       // async proxy
       fence_proxy_async_smem();
       tc_fence_after();
-      {
-        const uint64_t kd = kd0 + (uint64_t)(((j & 1) * kKVTile) >> 4);
+      const uint64_t kd = kd0 + (uint64_t)(((j & 1) * kKVTile) >> 4);
 #pragma unroll
-        for (int ks = 0; ks < kD / 16; ++ks)
-          umma_f16(tmem + kTmemS + (j & 1) * kNT, qd0 + (uint64_t)(((ks >> 2) * (kQBytes / 2) + (ks & 3) * 32) >> 4),
-                   kd + (uint64_t)((ks * 2 * (kNT * 16)) >> 4), idesc_s, ks > 0);
-        umma_commit(B(kBarSFull + (j & 1)));  // = kBarEmptyK
-        last_bar = kBarSFull + (j & 1);
-        last_par = (j >> 1) & 1;
-      }
+      for (int ks = 0; ks < kD / 16; ++ks)
+        umma_f16(tmem + kTmemS + (j & 1) * kNT, qd0 + (uint64_t)(((ks >> 2) * (kQBytes / 2) + (ks & 3) * 32) >> 4),
+                 kd + (uint64_t)((ks * 2 * (kNT * 16)) >> 4), idesc_s, ks > 0);
+      umma_commit(B(kBarSFull + (j & 1)));  // = kBarEmptyK
+      last_bar = kBarSFull + (j & 1);
+      last_par = (j >> 1) & 1;
       __syncwarp();
     };
-    wait_phase(B(kBarQ), 0, dead);
-    if (n_loc > 0 && !dead) issue_s(0);
-    if (n_loc > 1 && !dead) issue_s(1);
-    for (int j = 0; j < n_loc && !dead; ++j) {
+    auto issue_pv = [&](int j) {  // O += P_j V_j
       wait_phase(B(kBarFullV + (j & 1)), (j >> 1) & 1, dead);
-      if (dead) break;
+      if (dead) return;
       fence_proxy_async_smem();  // the V copies are generic-proxy writes
       if (jb + j == n_kt - 1 && (kv_end % kBS) != 0) {
         // V of tokens >= kv_end in the last page holds other data (possibly
@@ -652,33 +655,52 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       // P of tile j (a ring of two: the softmax warps may run one tile ahead)
       wait_phase(B(kBarPFull + (j & 1)), (j >> 1) & 1, dead);
-      if (dead) break;
+      if (dead) return;
       tc_fence_after();
-      {
-        const int np = min(kPagesPerTile, n_pages - (jb + j) * kPagesPerTile);
-        const uint64_t vd = vd0 + (uint64_t)(((j & 1) * kKVTile) >> 4);
-        for (int pg = 0; pg < np; ++pg)
-          umma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * kNT + pg * (kBS / 2),
-                      vd + (uint64_t)((pg * kPageBytes) >> 4), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
-        umma_commit(B(kBarPvDone + (j & 1)));  // = kBarEmptyV
-        last_bar = kBarPvDone + (j & 1);
-        last_par = (j >> 1) & 1;
-      }
+      const int np = min(kPagesPerTile, n_pages - (jb + j) * kPagesPerTile);
+      const uint64_t vd = vd0 + (uint64_t)(((j & 1) * kKVTile) >> 4);
+      for (int pg = 0; pg < np; ++pg)
+        umma_f16_ts(tmem + kTmemO, tmem + kTmemS + (j & 1) * kNT + pg * (kBS / 2),
+                    vd + (uint64_t)((pg * kPageBytes) >> 4), idesc_o, (j > 0 || pg > 0) ? 1u : 0u);
+      umma_commit(B(kBarPvDone + (j & 1)));  // = kBarEmptyV
+      last_bar = kBarPvDone + (j & 1);
+      last_par = (j >> 1) & 1;
       __syncwarp();
-      if (j + 2 < n_loc) {
-        // Q K^T j + 2 overwrites the S buffer that holds P j: the tensor core
-        // does not order a later MMA's D writes after an earlier MMA's TMEM A
-        // reads, so P V j must have completed first.
-        wait_phase(B(kBarPvDone + (j & 1)), (j >> 1) & 1, dead);
-        if (dead) break;
-        tc_fence_after();
-        issue_s(j + 2);
+    };
+    // Q K^T j overwrites the S buffer that holds P j - 2: the tensor core does
+    // not order a later MMA's D writes after an earlier MMA's TMEM A reads, so
+    // P V j - 2 must have completed first.
+    auto wait_pv_before_s = [&](int j) {
+      wait_phase(B(kBarPvDone + (j & 1)), ((j - 2) >> 1) & 1, dead);
+      if (!dead) tc_fence_after();
+    };
+    if constexpr (!kSplit) {  // two issuing warps
+      if (warp == kSMmaWarp) {
+        wait_phase(B(kBarQ), 0, dead);
+        for (int j = 0; j < n_loc && !dead; ++j) {
+          if (j >= 2) wait_pv_before_s(j);
+          if (!dead) issue_s(j);
+        }
+      } else {
+        for (int j = 0; j < n_loc && !dead; ++j) issue_pv(j);
+      }
+    } else if (warp == kMmaWarp) {  // split items (one or two key tiles per CTA): warp 4 issues both
+      wait_phase(B(kBarQ), 0, dead);
+      if (n_loc > 0 && !dead) issue_s(0);
+      if (n_loc > 1 && !dead) issue_s(1);
+      for (int j = 0; j < n_loc && !dead; ++j) {
+        issue_pv(j);
+        if (j + 2 < n_loc && !dead) {
+          wait_pv_before_s(j + 2);
+          if (!dead) issue_s(j + 2);
+        }
       }
     }
     // In a healthy run the last P V commit (waited for by the epilogue)
-    // covers every MMA issued here. After a wait gave up, nothing more was
-    // issued, and this warp waits (bounded) for its last commit so that no
-    // MMA still writes tensor memory when it is freed.
+    // covers every MMA (Q K^T j completed before the softmax read S j).
+    // After a wait gave up, this warp issues nothing more and waits (bounded)
+    // for its own last commit, so that no MMA still writes tensor memory when
+    // it is freed.
     if (dead && last_bar >= 0) {
       bool d2 = false;
       wait_phase(B(last_bar), last_par, d2);
@@ -891,12 +913,13 @@ int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
     }
   }
   if (splits == 1) {
-    prefill_umma_kernel<T, G, false><<<dim3((unsigned)items), kThreads, kSmemBytes, s>>>(a, (int)tiles, 1, qmap);
+    prefill_umma_kernel<T, G, false><<<dim3((unsigned)items), kThreadsFor(false), kSmemBytes, s>>>(a, (int)tiles, 1,
+                                                                                               qmap);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(items * splits));
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kThreadsFor(true));
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
