@@ -14,15 +14,20 @@
 //        stored back over the first half of its S buffer in TMEM
 //   O += P V     one tcgen05.mma M128 N128 K16 per 16-token page, A = P read
 //        from TMEM, accumulator O in TMEM
-// Warp roles (224 threads): warps 0-3 own TMEM lanes 0-127 (one row per
-// thread: softmax, O rescale, epilogue); warp 4 issues the MMAs; warp 5
-// stages Q (TMA) and K (16-byte cp.async), warp 6 stages V (TMA). Issuing a
-// TMA operation takes tens of nanoseconds and the SM's TMA unit serves both
-// resident CTAs, so K, whose 16-byte page rows would need 16 gathers per
-// tile, does not use it. S is double-buffered in TMEM, so Q K^T of
-// tile j + 1 is ready while the softmax warps work on tile j, and the
-// softmax of tile j + 1 does not wait for P V of tile j unless O needs a
-// rescale.
+// Warp roles (256 threads): warps 0-3 own TMEM lanes 0-127 (one row per
+// thread: softmax, O rescale, epilogue); warp 4 issues P V, warp 7 Q K^T
+// (two issuers, so that neither kind of MMA waits behind the other's issue,
+// which stalls while the tensor core is busy); warp 5 stages Q (TMA) and K,
+// warp 6 stages V, both by 16-byte cp.async (a K page row is 16 bytes wide,
+// so a K tile would cost 16 TMA gathers, and the SM's TMA unit serves both
+// resident CTAs). S is double-buffered in TMEM, so Q K^T of tile j + 1 is
+// ready while the softmax warps work on tile j, and the softmax of tile
+// j + 1 does not wait for P V of tile j unless O needs a rescale.
+//
+// Launches with few items (a long context with few new tokens) use a
+// second variant (224 threads, warp 4 issues both kinds of MMA): each item's
+// key tiles are shared by a thread-block cluster of up to 8 CTAs whose
+// partial O rows are combined through distributed shared memory.
 //
 // Shared-memory operand layouts (all "K-major", the reduction dim inside a
 // 16-byte chunk):
@@ -31,9 +36,10 @@
 //      (64 elements x head x token), 128-byte rows
 //   K  [16 dim chunks][64 keys][16 B]    no swizzle, LBO 1024, SBO 128; the
 //      K loader warp fills it with 16-byte cp.async copies (32 per lane)
-//   V  one page = [128 dims][16 tokens] rows of 32 B, one 2-D TMA load with
-//      the 32-byte swizzle = the canonical SW32 K-major layout (SBO 256) that
-//      the page's 16 tokens feed as one K = 16 step
+//   V  one page = [128 dims][16 tokens] rows of 32 B in the 32-byte-swizzled
+//      image (16-byte half h of dim d at h ^ ((d >> 2) & 1)), written by the
+//      V loader's 16-byte cp.async copies = the canonical SW32 K-major layout
+//      (SBO 256) that the page's 16 tokens feed as one K = 16 step
 // Softmax keeps a per-row running max that only moves when a tile's max
 // exceeds it by more than 2^8, so O in TMEM is rescaled rarely (exact in
 // real arithmetic: numerator and denominator use the same offset).
