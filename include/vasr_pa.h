@@ -236,9 +236,13 @@ int32_t vasr_pa_gather_kv_cache(void *key_out, void *value_out,
  * This replaces gather_kv_cache + flash_attn_varlen
  * (thinker_text.rs:1344-1365, attention.rs:580-657) in one kernel.
  * max_query_len bounds every q_len (flash_attn_varlen's max_seqlen_q); the
- * kernel schedules num_seqs x ceil(max_query_len / rows per CTA) CTAs, so a
- * sequence longer than it is cut short and sets VASR_PA_DERR_QLEN_RANGE.
- * 0 means "unknown" and schedules for the worst case (total_q_tokens).
+ * kernel schedules num_seqs x ceil(max_query_len / rows per CTA) work items
+ * per kv head, so a sequence longer than it is cut short and sets
+ * VASR_PA_DERR_QLEN_RANGE. 0 means "unknown" and schedules for the worst case
+ * (total_q_tokens). When the items are few next to the SM count (a long
+ * context with few new tokens), each item's key range is shared by a
+ * thread-block cluster of up to 8 CTAs (bf16 / f16 pages of 16 tokens,
+ * head_dim 128); the results are the same computation up to float rounding.
  */
 int32_t vasr_pa_paged_attention_varlen_prefill(
     void *out, const void *query, const void *key_cache,
