@@ -329,9 +329,9 @@ static_assert(kOffRed + kM * 8 <= kOffBar, "the combine staging fits in the Q, K
 // The softmax threads (row r each) of one CTA of a split item. After the
 // CTA's last barrier (which the loader and MMA warps meet before their two
 // cluster barriers) the CTA's unnormalised O rows (f32) and (m, l) go to its
-// own shared memory; after a cluster barrier each CTA reads every CTA's rows
-// for its share of the 32 four-dim chunks, weights them by 2^(m_s - M) and
-// writes O / L for those dims; a second cluster barrier keeps every CTA's
+// own shared memory; after a cluster barrier each CTA reads every CTA's copy
+// of its run of the rows that hold query positions, weights them by
+// 2^(m_s - M) and writes O / L for those rows; a second cluster barrier keeps every CTA's
 // shared memory alive until all reads are done. A CTA without key tiles (or
 // whose waits gave up) contributes m = -inf and zeros.
 template <typename T, int G>
@@ -355,44 +355,43 @@ __device__ void combine_splits(unsigned char *smem, uint32_t sbase, uint32_t t_o
   }
   reinterpret_cast<float2 *>(smem + kOffRed)[r] = have ? make_float2(m, l) : make_float2(-INFINITY, 0.f);
   cluster_sync_all();
+  // Rows of real query positions only, dealt to the cluster's CTAs in equal
+  // runs and to the four warps row by row; lane i owns dims 4i .. 4i + 3, so
+  // a warp reads each split's row as one contiguous 512-byte line.
   const uint32_t me = cluster_rank();
-  float w[kMaxSplits];
-  float M = -INFINITY;
+  const int rows = n_pos * G < kM ? n_pos * G : kM;
+  const int r0 = (int)(me * rows / splits), r1 = (int)((me + 1) * rows / splits);
+  const int lane = r & 31;
+  for (int row = r0 + (r >> 5); row < r1; row += 4) {  // warp-uniform
+    // lane s < splits holds split s's (m, l); max and weighted sum over lanes 0..7
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (lane < splits) ml = ld_cluster_f2(cluster_map(sbase + kOffRed + row * 8, (uint32_t)lane));
+    float M = ml.x;
 #pragma unroll
-  for (int s = 0; s < kMaxSplits; ++s) {
-    w[s] = -INFINITY;
-    if (s < splits) {
-      const float2 ml = ld_cluster_f2(cluster_map(sbase + kOffRed + r * 8, (uint32_t)s));
-      w[s] = ml.x;
-      M = fmaxf(M, ml.x);
-    }
-  }
-  float L = 0.f;
+    for (int x = kMaxSplits / 2; x > 0; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+    const float ws = (M == -INFINITY || ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+    float L = ml.y * ws;
 #pragma unroll
-  for (int s = 0; s < kMaxSplits; ++s) {
-    if (s >= splits) continue;
-    const float2 ml = ld_cluster_f2(cluster_map(sbase + kOffRed + r * 8, (uint32_t)s));
-    w[s] = (M == -INFINITY || ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
-    L = fmaf(ml.y, w[s], L);
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  const int c0 = (int)(me * (kD / 4) / splits), c1 = (int)((me + 1) * (kD / 4) / splits);
-  const bool row_ok = (r / G) < n_pos;
-  T *orow = out + (int64_t)(r / G) * row_stride + (int64_t)(r % G) * kD;
-  for (int c = c0; c < c1; ++c) {
+    for (int x = kMaxSplits / 2; x > 0; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+    L = __shfl_sync(0xffffffffu, L, 0);
+    const uint32_t src = sbase + kOffQ + (uint32_t)(row * kCPitch + 4 * lane) * 4;
+    float4 v[kMaxSplits];
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s)
+      v[s] = s < splits ? ld_cluster_f4(cluster_map(src, (uint32_t)s)) : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int s = 0; s < kMaxSplits; ++s) {
-      if (s >= splits) continue;
-      const float4 v = ld_cluster_f4(cluster_map(sbase + kOffQ + (uint32_t)(r * kCPitch + 4 * c) * 4, (uint32_t)s));
-      acc.x = fmaf(v.x, w[s], acc.x);
-      acc.y = fmaf(v.y, w[s], acc.y);
-      acc.z = fmaf(v.z, w[s], acc.z);
-      acc.w = fmaf(v.w, w[s], acc.w);
+      const float w = __shfl_sync(0xffffffffu, ws, s);
+      acc.x = fmaf(v[s].x, w, acc.x);
+      acc.y = fmaf(v[s].y, w, acc.y);
+      acc.z = fmaf(v[s].z, w, acc.z);
+      acc.w = fmaf(v[s].w, w, acc.w);
     }
-    if (row_ok)
-      *reinterpret_cast<uint2 *>(orow + 4 * c) =
-          make_uint2(pack2f<T>(acc.x * inv, acc.y * inv), pack2f<T>(acc.z * inv, acc.w * inv));
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    T *orow = out + (int64_t)(row / G) * row_stride + (int64_t)(row % G) * kD;
+    *reinterpret_cast<uint2 *>(orow + 4 * lane) =
+        make_uint2(pack2f<T>(acc.x * inv, acc.y * inv), pack2f<T>(acc.z * inv, acc.w * inv));
   }
   cluster_sync_all();
 }
