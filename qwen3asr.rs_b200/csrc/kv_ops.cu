@@ -935,92 +935,340 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
   }
 }
 
-// Prefill-sized fp8 appends: the 16-token tiles of kv_append_tile16_kernel
-// with HPT heads per tile, quantised while staging (one byte per element).
-// V groups hold kTPS = min(16, BS) tokens: one 16-byte (8-byte at BS 8)
-// vector of a page row.
-template <typename T, int BS, int D, int HPT>
-__global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_tile16_kernel(const AppendFp8Params p) {
+// Quotients RN(x / s) without a division, two elements per packed f32x2
+// instruction, for positive scales in a range where per-element range checks
+// reduce to a clamp of the source (QuantScale2::fast): s in [2^-60, 2^60]
+// (f16 sources: [2^-60, 2^7]). The source is clamped first to +-B, B the
+// 16-bit value nearest s 2^15 (at most 65504 for f16); NaN stays NaN. Any
+// |x| above B has |x / s| > 2^14 and saturates to +-448 like B itself, so the
+// clamp moves no byte; after it |t| = |RN(x inv)| <= 2^15 (1 + 2^-8), t s
+// stays finite, and
+//  - |x / s| >= 2^-11: |x| >= 2^-71 keeps the remainder x - t s normal and
+//    exact (s >= 2^-60), quotient_rn's conditions, and one correction step
+//    gives RN(x / s);
+//  - |x / s| < 2^-11: the byte is a signed zero; the corrected value stays
+//    below 2^-10 in magnitude and takes t's sign (for x = -0 the step adds a
+//    +0 remainder to t = -0, which would give +0).
+// Other scales use quotient_rn element by element.
+struct QuantScale2 {
+  float2 inv;      // (1 / s, 1 / s) rounded
+  float2 ns;       // (-s, -s)
+  uint32_t bhi;    // (B, B) and (-B, -B) as packed 16-bit source values
+  uint32_t blo;
+  float bf;        // B for f32 sources
+  QuantScale one;
+  bool fast;
+};
+template <typename T>
+__device__ __forceinline__ QuantScale2 quant_scale2(float s) {
+  QuantScale2 q;
+  q.one = quant_scale(s);
+  q.inv = make_float2(q.one.inv, q.one.inv);
+  q.ns = make_float2(-s, -s);
+  const float top = std::is_same<T, __half>::value ? 0x1p7f : 0x1p60f;
+  q.fast = s >= 0x1p-60f && s <= top;  // false for NaN and negative scales
+  const float b = fminf(s * 0x1p15f, 65504.f * (std::is_same<T, __half>::value ? 1.f : 0x1p100f));
+  q.bf = b;
+  uint32_t h = 0;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    h = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b));
+  else if constexpr (std::is_same<T, __half>::value)
+    h = (uint32_t)__half_as_ushort(__float2half_rn(b));
+  q.bhi = h | (h << 16);
+  q.blo = q.bhi | 0x80008000u;
+  return q;
+}
+// Clamp a packed pair of 16-bit source values to [-B, B] (NaN propagates).
+template <typename T>
+__device__ __forceinline__ uint32_t clamp_pair(uint32_t w, const QuantScale2 &q) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&w);
+    const uint32_t hi = q.bhi, lo = q.blo;
+    v = __hmin2_nan(__hmax2_nan(v, *reinterpret_cast<const __nv_bfloat162 *>(&lo)),
+                    *reinterpret_cast<const __nv_bfloat162 *>(&hi));
+    return *reinterpret_cast<uint32_t *>(&v);
+  } else {
+    __half2 v = *reinterpret_cast<__half2 *>(&w);
+    const uint32_t hi = q.bhi, lo = q.blo;
+    v = __hmin2_nan(__hmax2_nan(v, *reinterpret_cast<const __half2 *>(&lo)),
+                    *reinterpret_cast<const __half2 *>(&hi));
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+}
+__device__ __forceinline__ float clamp_f32(float x, float b) {
+  float y;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(y) : "f"(x), "f"(-b));
+  asm("min.NaN.f32 %0, %0, %1;" : "+f"(y) : "f"(b));
+  return y;
+}
+// Two clamped values -> RN(x / s) each (fast scales).
+__device__ __forceinline__ float2 quot2_fast(float2 x, const QuantScale2 &q) {
+  const float2 t = __fmul2_rn(x, q.inv);
+  const float2 v = __ffma2_rn(__ffma2_rn(t, q.ns, x), q.inv, t);
+  return make_float2(copysignf(v.x, t.x), copysignf(v.y, t.y));
+}
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float a, float b) {  // a -> low byte
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+}
+// One 32-bit source word (a pair of 16-bit values, or one f32 in .x with
+// .y = next word) -> the pair's quotients in f32.
+template <typename T, bool kFast>
+__device__ __forceinline__ float2 quot_word(uint32_t w, const QuantScale2 &q) {
+  float2 x;
+  if constexpr (kFast) w = clamp_pair<T>(w, q);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    unpack_bf16x2(w, x.x, x.y);
+  else
+    unpack_half2(w, x.x, x.y);
+  if constexpr (kFast) return quot2_fast(x, q);
+  return make_float2(quotient_rn(x.x, q.one), quotient_rn(x.y, q.one));
+}
+template <bool kFast>
+__device__ __forceinline__ float2 quot_f32(float2 x, const QuantScale2 &q) {
+  if constexpr (kFast) return quot2_fast(make_float2(clamp_f32(x.x, q.bf), clamp_f32(x.y, q.bf)), q);
+  return make_float2(quotient_rn(x.x, q.one), quotient_rn(x.y, q.one));
+}
+
+// Prefill-sized fp8 appends (4096 tokens or more): a persistent grid of
+// CTAs of 8 consumer warps and one producer warp over (16-token tile, pair
+// of kv heads) items, dealt round-robin (item = tile * pairs + pair). The
+// producer fills a ring of shared-memory stages: per token one bulk copy of
+// its K row and one of its V row (the pair's 2 x D elements, contiguous in
+// the source) and an 8-byte asynchronous copy of its slot, all completing on
+// the stage's full barrier. A consumer warp reads its values of a stage,
+// releases the stage (one arrive per warp on its empty barrier) and
+// quantises from registers, 32 elements per thread:
+//  warps 0-3 (K): head w >> 1, 16-dim chunk (lane >> 3) + 4 (w & 1), tokens
+//     lane & 7 and (lane & 7) + 8: one 16-byte page chunk each, converted
+//     in dim pairs;
+//  warps 4-7 (V): head (w - 4) >> 1, dims 2 j and 2 j + 1 with j = 32
+//     ((w - 4) & 1) + lane, all 16 tokens, converted in token pairs so that
+//     each conversion yields two adjacent bytes of a dim's page row: a row
+//     of min(16, BS) consecutive slots from an aligned start leaves as one
+//     vector store, any other group byte by byte.
+// Staged rows are kRow + 16 bytes apart, so the 8 K rows a quarter-warp
+// reads at one offset fall in different bank groups. Every wait is bounded;
+// a warp whose wait gave up stops, and the producer then waits (bounded) for
+// the copies of its last stages before the CTA leaves.
+constexpr int kRingConsumers = 256;
+constexpr int kRingThreads = kRingConsumers + 32;
+template <typename T, int D, int HPT>
+struct RingLayout {
+  static constexpr int kRow = HPT * D * (int)sizeof(T);  // one token's K (or V) row of the pair
+  static constexpr int kPitch = kRow + 16;
+  static constexpr int kSlots = 2 * kTile16 * kPitch;     // 16 int64 slots after the rows
+  static constexpr int kStage = kSlots + kTile16 * 8;
+  static constexpr int kStages = sizeof(T) == 4 ? 3 : 4;
+  static constexpr int kBars = kStages * kStage;          // full[kStages], empty[kStages]
+  static constexpr int kBytes = kBars + 2 * kStages * 8;
+  static_assert(kPitch % 16 == 0 && kStage % 16 == 0, "bulk copy destinations 16-byte aligned");
+};
+
+template <typename T, int BS, int D, int HPT, bool kFast>
+__device__ __forceinline__ void fp8_ring_body(const AppendFp8Params &p, const QuantScale2 &ks,
+                                              const QuantScale2 &vs, const unsigned char *smem,
+                                              uint32_t sbase) {
+  static_assert(D == 128 && HPT == 2 && kRingConsumers == 256, "thread map: 2 heads x 128 dims x 16 tokens");
+  using L = RingLayout<T, D, HPT>;
   constexpr int kES = (int)sizeof(T);
-  constexpr int kCH = D / 16;                      // 16-element chunks per (token, head)
-  constexpr int kRow = HPT * kCH;                  // chunks per staged token row
-  constexpr int kPitch = HPT * D + 16;             // staged row bytes
-  constexpr int kTPS = BS < 16 ? BS : 16;          // tokens per V vector
+  constexpr int kTPS = BS < 16 ? BS : 16;  // tokens per V page-row vector
   constexpr int kGroups = kTile16 / kTPS;
-  constexpr int kChunks = kTile16 * kRow;
-  constexpr int kVItems = HPT * D * kGroups;
-  static_assert((kRow & (kRow - 1)) == 0 && (kCH & (kCH - 1)) == 0, "power-of-two tile shapes");
-  __shared__ __align__(16) unsigned char kt[kTile16 * kPitch];
-  __shared__ __align__(16) unsigned char vt[kTile16 * kPitch];
-  __shared__ int64_t s_slot[kTile16];
-  __shared__ int s_gok[kGroups];
-  const int tid = threadIdx.x;
-  const int h0 = blockIdx.y * HPT;
-  const int HC = min(HPT, p.num_kv_heads - h0);
-  const QuantScale ks = quant_scale(__ldg(p.k_scale)), vs = quant_scale(__ldg(p.v_scale));
-  for (int it = 0; it < p.tiles_per_cta; ++it) {
-    const int64_t t0 = ((int64_t)blockIdx.x * p.tiles_per_cta + it) * kTile16;
-    if (t0 >= p.num_tokens) break;
-    if (it > 0) __syncthreads();  // the previous tile's staged rows and slots are read
-    const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
-    if (tid < 32)
-      tile16_slots<BS, kTPS, kGroups>(tile16_load_slot(p.slots, t0, ntok), p.num_blocks, s_slot, s_gok);
-#pragma unroll
-    for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
-      const int i = tid + k * kAppendThreads;
-      const int tt = i / kRow, r = i % kRow;
-      if (i < kChunks && tt < ntok && r / kCH < HC) {
-        const int64_t col = ((int64_t)h0 * D + (int64_t)r * 16) * kES;
-        *reinterpret_cast<uint4 *>(kt + tt * kPitch + r * 16) =
-            quantize16<T>(p.key + (t0 + tt) * p.k_stride_bytes + col, ks);
-        *reinterpret_cast<uint4 *>(vt + tt * kPitch + r * 16) =
-            quantize16<T>(p.value + (t0 + tt) * p.v_stride_bytes + col, vs);
-      }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pairs = (p.num_kv_heads + HPT - 1) / HPT;
+  const int tiles = (int)((p.num_tokens + kTile16 - 1) / kTile16);
+  // items blockIdx.x, + gridDim.x, ... as (tile, pair), advanced without division
+  const int step_t = (int)gridDim.x / pairs, step_p = (int)gridDim.x % pairs;
+  auto full = [&](int st) { return sbase + (uint32_t)L::kBars + 8u * (uint32_t)st; };
+  auto empty = [&](int st) { return sbase + (uint32_t)L::kBars + 8u * (uint32_t)(L::kStages + st); };
+  int tile = (int)blockIdx.x / pairs, pair = (int)blockIdx.x % pairs;
+  auto advance = [&]() {
+    tile += step_t;
+    pair += step_p;
+    if (pair >= pairs) {
+      pair -= pairs;
+      ++tile;
     }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < (kChunks + kAppendThreads - 1) / kAppendThreads; ++k) {
-      const int i = tid + k * kAppendThreads;
-      const int tt = i % kTile16, r = i / kTile16;
-      const int hc = r / kCH, c = r % kCH;
-      const int64_t sl = s_slot[tt];
-      if (i < kChunks && sl >= 0 && hc < HC) {
-        const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
-        const uint64_t dst = (((blk * (uint64_t)p.num_kv_heads + (uint64_t)(h0 + hc)) * kCH + c) * BS + off) * 16;
-        *reinterpret_cast<uint4 *>(p.k_cache + dst) = *reinterpret_cast<const uint4 *>(kt + tt * kPitch + r * 16);
+  };
+
+  if (warp == kRingConsumers / 32) {
+    // ------------------------------------------------------------ producer
+    int k = 0;
+    for (; tile < tiles; advance(), ++k) {
+      const int st = k % L::kStages;
+      if (k >= L::kStages) {
+        const bool ok = mbar_wait_bounded(empty(st), (uint32_t)((k / L::kStages - 1) & 1));
+        if (!__all_sync(0xffffffffu, ok)) break;
       }
+      const int64_t t0 = (int64_t)tile * kTile16;
+      const int h0 = pair * HPT;
+      const int hc = min(HPT, p.num_kv_heads - h0);
+      const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
+      const uint32_t row = (uint32_t)(hc * D * kES);
+      const uint32_t base = sbase + (uint32_t)(st * L::kStage);
+      if (lane == 0) mbar_arrive_expect_tx(full(st), 2u * (uint32_t)ntok * row);
+      __syncwarp();
+      if (lane < ntok) {
+        const int64_t tok = t0 + lane, col = (int64_t)h0 * D * kES;
+        bulk_g2s(base + (uint32_t)(lane * L::kPitch), p.key + tok * p.k_stride_bytes + col, row, full(st));
+        bulk_g2s(base + (uint32_t)((kTile16 + lane) * L::kPitch), p.value + tok * p.v_stride_bytes + col, row,
+                 full(st));
+        cp_async8(base + (uint32_t)(L::kSlots + lane * 8), p.slots + tok);
+      }
+      cp_async_arrive_noinc(full(st));  // one of the 32 lane arrivals of the phase
     }
+    // the copies of the last stages issued land before shared memory is let go
+    // (already waited for by the consumers in a healthy run)
+    for (int j = max(0, k - L::kStages); j < k; ++j)
+      mbar_wait_bounded(full(j % L::kStages), (uint32_t)((j / L::kStages) & 1));
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const bool kwarp = warp < 4;
+  const int hc = kwarp ? warp >> 1 : (warp - 4) >> 1;  // head of the pair (warp-uniform)
+  const int kt = lane & 7, kc = (lane >> 3) + 4 * (warp & 1);  // K: tokens kt, kt + 8; 16-dim chunk
+  const int jp = 32 * ((warp - 4) & 1) + lane;                // V: dims 2 jp, 2 jp + 1
+  const int64_t max_slot = p.num_blocks * BS;
+  const uint64_t kpage = (uint64_t)p.num_kv_heads * D * BS;  // bytes of one block of the fp8 cache
+  int k = 0;
+  for (; tile < tiles; advance(), ++k) {
+    const int st = k % L::kStages;
+    const bool ok = mbar_wait_bounded(full(st), (uint32_t)((k / L::kStages) & 1));
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const int h = pair * HPT + hc;
+    const bool live = h < p.num_kv_heads;
+    const int ntok = (int)min((int64_t)kTile16, p.num_tokens - (int64_t)tile * kTile16);
+    const unsigned char *stage = smem + st * L::kStage;
+    const int64_t *sslot = reinterpret_cast<const int64_t *>(stage + L::kSlots);
+    if (kwarp) {
+      // ------------------------------------------------------------- K
+      uint4 raw[2][kES];
+      int64_t sl[2];
 #pragma unroll
-    for (int k = 0; k < (kVItems + kAppendThreads - 1) / kAppendThreads; ++k) {
-      const int i = tid + k * kAppendThreads;
-      const int g = i % kGroups, hd = i / kGroups;
-      const int hc = hd / D, d = hd % D;
-      if (i >= kVItems || hc >= HC) continue;
-      const unsigned char *src = vt + (g * kTPS) * kPitch + hc * D + d;
-      const uint64_t row = ((uint64_t)h0 + hc) * D + d;
-      if (s_gok[g]) {
-        const uint64_t us = (uint64_t)s_slot[g * kTPS], blk = us / BS, off = us % BS;
-        uint32_t w[kTPS / 4];
+      for (int u = 0; u < 2; ++u) {
+        const int t = kt + 8 * u;
+        sl[u] = t < ntok ? sslot[t] : -1;
+        const unsigned char *src = stage + t * L::kPitch + (hc * D + kc * 16) * kES;
 #pragma unroll
-        for (int q = 0; q < kTPS / 4; ++q)
-          w[q] = (uint32_t)src[(4 * q) * kPitch] | ((uint32_t)src[(4 * q + 1) * kPitch] << 8) |
-                 ((uint32_t)src[(4 * q + 2) * kPitch] << 16) | ((uint32_t)src[(4 * q + 3) * kPitch] << 24);
-        unsigned char *dst = p.v_cache + (blk * (uint64_t)p.num_kv_heads * D + row) * BS + off;
-        if constexpr (kTPS == 16)
-          *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-        else
-          *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+        for (int i = 0; i < kES; ++i) raw[u][i] = *reinterpret_cast<const uint4 *>(src + 16 * i);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty(st));  // this warp is done with the stage
+      if (!live) continue;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (sl[u] >= max_slot) {
+          raise_device_error(VASR_PA_DERR_SLOT_RANGE);
+          continue;
+        }
+        if (sl[u] < 0) continue;
+        const uint32_t *wd = reinterpret_cast<const uint32_t *>(raw[u]);
+        uint32_t out[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // output word i = dims 4 i .. 4 i + 3
+          float2 a, b;
+          if constexpr (kES == 2) {
+            a = quot_word<T, kFast>(wd[2 * i], ks);
+            b = quot_word<T, kFast>(wd[2 * i + 1], ks);
+          } else {
+            a = quot_f32<kFast>(make_float2(__uint_as_float(wd[4 * i]), __uint_as_float(wd[4 * i + 1])), ks);
+            b = quot_f32<kFast>(make_float2(__uint_as_float(wd[4 * i + 2]), __uint_as_float(wd[4 * i + 3])), ks);
+          }
+          out[i] = cvt_e4m3x2(a.x, a.y) | (cvt_e4m3x2(b.x, b.y) << 16);
+        }
+        const uint64_t us = (uint64_t)sl[u];
+        const uint64_t dst = (us / BS) * kpage + (((uint64_t)h * (D / 16) + kc) * BS + us % BS) * 16;
+        *reinterpret_cast<uint4 *>(p.k_cache + dst) = make_uint4(out[0], out[1], out[2], out[3]);
+      }
+      continue;
+    }
+    // --------------------------------------------------------------- V
+    float2 v[kTile16];  // quotients of (dim 2 jp, dim 2 jp + 1) of each token
+    const unsigned char *vsrc = stage + kTile16 * L::kPitch + (hc * D + 2 * jp) * kES;
+    int64_t s = lane < ntok && lane < kTile16 ? sslot[lane] : -1;  // lanes 0-15: token lane's slot
+    if constexpr (kES == 2) {
+      uint32_t wv[kTile16];
+#pragma unroll
+      for (int t = 0; t < kTile16; ++t) wv[t] = *reinterpret_cast<const uint32_t *>(vsrc + t * L::kPitch);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty(st));
+      if (!live) continue;
+#pragma unroll
+      for (int t = 0; t < kTile16; ++t) v[t] = quot_word<T, kFast>(wv[t], vs);
+    } else {
+      float2 xv[kTile16];
+#pragma unroll
+      for (int t = 0; t < kTile16; ++t) xv[t] = *reinterpret_cast<const float2 *>(vsrc + t * L::kPitch);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty(st));
+      if (!live) continue;
+#pragma unroll
+      for (int t = 0; t < kTile16; ++t) v[t] = quot_f32<kFast>(xv[t], vs);
+    }
+    if (s >= max_slot) {
+      raise_device_error(VASR_PA_DERR_SLOT_RANGE);
+      s = -1;
+    }
+    // runs: kTPS consecutive slots from a multiple of kTPS
+    const int idx = lane & 15;
+    const int g0 = idx & ~(kTPS - 1);
+    const int64_t gfirst = __shfl_sync(0xffffffffu, s, g0);
+    const bool run = lane < kTile16 && s >= 0 && (gfirst & (kTPS - 1)) == 0 && s == gfirst + (idx - g0);
+    const uint32_t ball = __ballot_sync(0xffffffffu, run);
+    uint32_t row[2][4];  // [dim][tokens 4 i .. 4 i + 3], token 4 i in the low byte
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      row[0][i] = cvt_e4m3x2(v[4 * i].x, v[4 * i + 1].x) | (cvt_e4m3x2(v[4 * i + 2].x, v[4 * i + 3].x) << 16);
+      row[1][i] = cvt_e4m3x2(v[4 * i].y, v[4 * i + 1].y) | (cvt_e4m3x2(v[4 * i + 2].y, v[4 * i + 3].y) << 16);
+    }
+    const uint64_t vrow = (uint64_t)h * D + 2 * jp;
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) {
+      const int64_t gs = __shfl_sync(0xffffffffu, s, g * kTPS);
+      if (((ball >> (g * kTPS)) & ((1u << kTPS) - 1u)) == (1u << kTPS) - 1u) {
+        const uint64_t us = (uint64_t)gs;
+        unsigned char *dst = p.v_cache + (us / BS) * kpage + vrow * BS + us % BS;
+#pragma unroll
+        for (int d = 0; d < 2; ++d) {
+          if constexpr (kTPS == 16)
+            *reinterpret_cast<uint4 *>(dst + d * BS) = make_uint4(row[d][0], row[d][1], row[d][2], row[d][3]);
+          else
+            *reinterpret_cast<uint2 *>(dst + d * BS) = make_uint2(row[d][2 * g], row[d][2 * g + 1]);
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < kTPS; ++e) {
-          const int64_t sl = s_slot[g * kTPS + e];
-          if (sl < 0) continue;
-          const uint64_t us = (uint64_t)sl, blk = us / BS, off = us % BS;
-          p.v_cache[(blk * (uint64_t)p.num_kv_heads * D + row) * BS + off] = src[e * kPitch];
+          const int t = g * kTPS + e;
+          const int64_t ts = __shfl_sync(0xffffffffu, s, t);
+          if (ts < 0) continue;
+          const uint64_t us = (uint64_t)ts;
+          unsigned char *dst = p.v_cache + (us / BS) * kpage + vrow * BS + us % BS;
+#pragma unroll
+          for (int d = 0; d < 2; ++d) dst[d * BS] = (unsigned char)(row[d][t >> 2] >> (8 * (t & 3)));
         }
       }
     }
   }
+}
+
+template <typename T, int BS, int D, int HPT>
+__global__ void __launch_bounds__(kRingThreads) kv_append_fp8_ring_kernel(const AppendFp8Params p) {
+  extern __shared__ __align__(128) unsigned char ring_smem[];
+  using L = RingLayout<T, D, HPT>;
+  const uint32_t sbase = smem_addr(ring_smem);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < L::kStages; ++i) {
+      mbar_init(sbase + L::kBars + 8 * i, 33);  // producer lane 0 + 32 copy arrivals
+      mbar_init(sbase + L::kBars + 8 * (L::kStages + i), kRingConsumers / 32);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const QuantScale2 ks = quant_scale2<T>(__ldg(p.k_scale)), vs = quant_scale2<T>(__ldg(p.v_scale));
+  if (ks.fast && vs.fast)
+    fp8_ring_body<T, BS, D, HPT, true>(p, ks, vs, ring_smem, sbase);
+  else
+    fp8_ring_body<T, BS, D, HPT, false>(p, ks, vs, ring_smem, sbase);
 }
 
 // Decode-sized fp8 appends (a few tokens, one per page row): one warp per
@@ -1078,16 +1326,17 @@ int launch_append_fp8_t(const AppendArgs &a, cudaStream_t stream) {
     kv_append_fp8_token_kernel<T, BS, D><<<(unsigned)ctas, 128, 0, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
-  if (a.num_tokens >= 4096) {  // prefill chunks: 16-token tiles of 2 heads
+  if (a.num_tokens >= 4096) {  // prefill chunks: persistent ring CTAs over (16-token tile, head pair)
+    using L = RingLayout<T, D, 2>;
+    auto *kern = kv_append_fp8_ring_kernel<T, BS, D, 2>;
+    static std::atomic<uint64_t> attr_done{0};
     static std::atomic<int64_t> resident[64];
-    const int64_t tiles = (a.num_tokens + kTile16 - 1) / kTile16;
-    const int hg = (a.num_kv_heads + 1) / 2;
-    p.tiles_per_cta = tile16_per_cta(tiles * hg, resident_ctas(kv_append_fp8_tile16_kernel<T, BS, D, 2>,
-                                                                kAppendThreads, 0, resident));
-    const int64_t gx = (tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
-    if (gx > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
-    dim3 grid((unsigned)gx, (unsigned)hg);
-    kv_append_fp8_tile16_kernel<T, BS, D, 2><<<grid, kAppendThreads, 0, stream>>>(p);
+    if (!ensure_smem_attr(kern, L::kBytes, attr_done)) return VASR_PA_ELAUNCH;
+    const int64_t items = (a.num_tokens + kTile16 - 1) / kTile16 * ((a.num_kv_heads + 1) / 2);
+    int64_t ctas = resident_ctas(kern, kRingThreads, L::kBytes, resident);
+    if (ctas <= 0 || ctas > items) ctas = items;
+    if (ctas > 0x7fffffff) return VASR_PA_EINVAL_SHAPE;
+    kern<<<(unsigned)ctas, kRingThreads, L::kBytes, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
   const int tt = 8;  // mid-sized: 8-token tiles of up to 2 KB of heads (one byte per element)
