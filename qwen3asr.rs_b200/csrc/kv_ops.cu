@@ -947,8 +947,11 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
 //    exact (s >= 2^-60), quotient_rn's conditions, and one correction step
 //    gives RN(x / s);
 //  - |x / s| < 2^-11: the byte is a signed zero; the corrected value stays
-//    below 2^-10 in magnitude and takes t's sign (for x = -0 the step adds a
-//    +0 remainder to t = -0, which would give +0).
+//    below 2^-10 in magnitude with t's sign.
+// The remainder r = x - t s is computed rounding toward -inf: a nonzero r is
+// exact either way, and an exact zero comes out as -0, so that t + r inv
+// keeps the sign of a zero t (x = -0: -0 + -0; x = +0: -0 + +0 = +0), where a
+// round-to-nearest remainder (+0) would turn t = -0 into +0.
 // Other scales use quotient_rn element by element.
 struct QuantScale2 {
   float2 inv;      // (1 / s, 1 / s) rounded
@@ -1004,8 +1007,7 @@ __device__ __forceinline__ float clamp_f32(float x, float b) {
 // Two clamped values -> RN(x / s) each (fast scales).
 __device__ __forceinline__ float2 quot2_fast(float2 x, const QuantScale2 &q) {
   const float2 t = __fmul2_rn(x, q.inv);
-  const float2 v = __ffma2_rn(__ffma2_rn(t, q.ns, x), q.inv, t);
-  return make_float2(copysignf(v.x, t.x), copysignf(v.y, t.y));
+  return __ffma2_rn(__ffma2_rd(t, q.ns, x), q.inv, t);
 }
 __device__ __forceinline__ uint32_t cvt_e4m3x2(float a, float b) {  // a -> low byte
   return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
@@ -1103,17 +1105,21 @@ __device__ __forceinline__ void fp8_ring_body(const AppendFp8Params &p, const Qu
       const int h0 = pair * HPT;
       const int hc = min(HPT, p.num_kv_heads - h0);
       const int ntok = (int)min((int64_t)kTile16, p.num_tokens - t0);
-      const uint32_t row = (uint32_t)(hc * D * kES);
+      const int pieces = hc * D * kES / 16;  // 16-byte pieces of a token's row
       const uint32_t base = sbase + (uint32_t)(st * L::kStage);
-      if (lane == 0) mbar_arrive_expect_tx(full(st), 2u * (uint32_t)ntok * row);
-      __syncwarp();
-      if (lane < ntok) {
-        const int64_t tok = t0 + lane, col = (int64_t)h0 * D * kES;
-        bulk_g2s(base + (uint32_t)(lane * L::kPitch), p.key + tok * p.k_stride_bytes + col, row, full(st));
-        bulk_g2s(base + (uint32_t)((kTile16 + lane) * L::kPitch), p.value + tok * p.v_stride_bytes + col, row,
-                 full(st));
-        cp_async8(base + (uint32_t)(L::kSlots + lane * 8), p.slots + tok);
+      const int64_t col = (int64_t)h0 * D * kES;
+      const unsigned char *ksrc = p.key + t0 * p.k_stride_bytes + col;
+      const unsigned char *vsrc = p.value + t0 * p.v_stride_bytes + col;
+      for (int t = 0; t < ntok; ++t) {
+#pragma unroll
+        for (int c = lane; c < L::kRow / 16; c += 32) {
+          if (c < pieces) {
+            cp_async16(base + (uint32_t)(t * L::kPitch + c * 16), ksrc + t * p.k_stride_bytes + c * 16);
+            cp_async16(base + (uint32_t)((kTile16 + t) * L::kPitch + c * 16), vsrc + t * p.v_stride_bytes + c * 16);
+          }
+        }
       }
+      if (lane < ntok) cp_async8(base + (uint32_t)(L::kSlots + lane * 8), p.slots + t0 + lane);
       cp_async_arrive_noinc(full(st));  // one of the 32 lane arrivals of the phase
     }
     // the copies of the last stages issued land before shared memory is let go
@@ -1258,7 +1264,7 @@ __global__ void __launch_bounds__(kRingThreads) kv_append_fp8_ring_kernel(const 
   const uint32_t sbase = smem_addr(ring_smem);
   if (threadIdx.x == 0) {
     for (int i = 0; i < L::kStages; ++i) {
-      mbar_init(sbase + L::kBars + 8 * i, 33);  // producer lane 0 + 32 copy arrivals
+      mbar_init(sbase + L::kBars + 8 * i, 32);  // one arrival per producer lane, when its copies land
       mbar_init(sbase + L::kBars + 8 * (L::kStages + i), kRingConsumers / 32);
     }
     mbar_fence_init();
