@@ -956,8 +956,7 @@ __global__ void __launch_bounds__(kAppendThreads) kv_append_fp8_kernel(const App
 struct QuantScale2 {
   float2 inv;      // (1 / s, 1 / s) rounded
   float2 ns;       // (-s, -s)
-  uint32_t bhi;    // (B, B) and (-B, -B) as packed 16-bit source values
-  uint32_t blo;
+  uint32_t bhi;    // (B, B) as packed 16-bit source values
   float bf;        // B for f32 sources
   QuantScale one;
   bool fast;
@@ -978,30 +977,22 @@ __device__ __forceinline__ QuantScale2 quant_scale2(float s) {
   else if constexpr (std::is_same<T, __half>::value)
     h = (uint32_t)__half_as_ushort(__float2half_rn(b));
   q.bhi = h | (h << 16);
-  q.blo = q.bhi | 0x80008000u;
   return q;
 }
-// Clamp a packed pair of 16-bit source values to [-B, B] (NaN propagates).
+// Clamp a packed pair of 16-bit source values to [-B, B], NaN propagating:
+// one min of magnitudes whose result takes sign(x) xor sign(B) = sign(x).
 template <typename T>
 __device__ __forceinline__ uint32_t clamp_pair(uint32_t w, const QuantScale2 &q) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&w);
-    const uint32_t hi = q.bhi, lo = q.blo;
-    v = __hmin2_nan(__hmax2_nan(v, *reinterpret_cast<const __nv_bfloat162 *>(&lo)),
-                    *reinterpret_cast<const __nv_bfloat162 *>(&hi));
-    return *reinterpret_cast<uint32_t *>(&v);
-  } else {
-    __half2 v = *reinterpret_cast<__half2 *>(&w);
-    const uint32_t hi = q.bhi, lo = q.blo;
-    v = __hmin2_nan(__hmax2_nan(v, *reinterpret_cast<const __half2 *>(&lo)),
-                    *reinterpret_cast<const __half2 *>(&hi));
-    return *reinterpret_cast<uint32_t *>(&v);
-  }
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm("min.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(q.bhi));
+  else
+    asm("min.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(q.bhi));
+  return r;
 }
 __device__ __forceinline__ float clamp_f32(float x, float b) {
   float y;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(y) : "f"(x), "f"(-b));
-  asm("min.NaN.f32 %0, %0, %1;" : "+f"(y) : "f"(b));
+  asm("min.NaN.xorsign.abs.f32 %0, %1, %2;" : "=f"(y) : "f"(x), "f"(b));
   return y;
 }
 // Two clamped values -> RN(x / s) each (fast scales).
@@ -1135,7 +1126,11 @@ __device__ __forceinline__ void fp8_ring_body(const AppendFp8Params &p, const Qu
   const int kt = lane & 7, kc = (lane >> 3) + 4 * (warp & 1);  // K: tokens kt, kt + 8; 16-dim chunk
   const int jp = 32 * ((warp - 4) & 1) + lane;                // V: dims 2 jp, 2 jp + 1
   const int64_t max_slot = p.num_blocks * BS;
-  const uint64_t kpage = (uint64_t)p.num_kv_heads * D * BS;  // bytes of one block of the fp8 cache
+  // bytes of one block of the fp8 cache; the launcher keeps blocks and this below 2^32
+  const uint32_t kpage = (uint32_t)(p.num_kv_heads * D * BS);
+  auto block_base = [&](uint64_t slot) {  // byte offset of slot's block, and slot % BS
+    return (uint64_t)(uint32_t)(slot / BS) * kpage;
+  };
   int k = 0;
   for (; tile < tiles; advance(), ++k) {
     const int st = k % L::kStages;
@@ -1183,7 +1178,7 @@ __device__ __forceinline__ void fp8_ring_body(const AppendFp8Params &p, const Qu
           out[i] = cvt_e4m3x2(a.x, a.y) | (cvt_e4m3x2(b.x, b.y) << 16);
         }
         const uint64_t us = (uint64_t)sl[u];
-        const uint64_t dst = (us / BS) * kpage + (((uint64_t)h * (D / 16) + kc) * BS + us % BS) * 16;
+        const uint64_t dst = block_base(us) + (uint32_t)(((h * (D / 16) + kc) * BS + (int)(us % BS)) * 16);
         *reinterpret_cast<uint4 *>(p.k_cache + dst) = make_uint4(out[0], out[1], out[2], out[3]);
       }
       continue;
@@ -1227,13 +1222,14 @@ __device__ __forceinline__ void fp8_ring_body(const AppendFp8Params &p, const Qu
       row[0][i] = cvt_e4m3x2(v[4 * i].x, v[4 * i + 1].x) | (cvt_e4m3x2(v[4 * i + 2].x, v[4 * i + 3].x) << 16);
       row[1][i] = cvt_e4m3x2(v[4 * i].y, v[4 * i + 1].y) | (cvt_e4m3x2(v[4 * i + 2].y, v[4 * i + 3].y) << 16);
     }
-    const uint64_t vrow = (uint64_t)h * D + 2 * jp;
+    const uint32_t vrow = (uint32_t)(h * D + 2 * jp);
 #pragma unroll
     for (int g = 0; g < kGroups; ++g) {
-      const int64_t gs = __shfl_sync(0xffffffffu, s, g * kTPS);
+      // the group's first slot (the run check already fetched it when one group spans the tile)
+      const int64_t gs = kGroups == 1 ? gfirst : __shfl_sync(0xffffffffu, s, g * kTPS);
       if (((ball >> (g * kTPS)) & ((1u << kTPS) - 1u)) == (1u << kTPS) - 1u) {
         const uint64_t us = (uint64_t)gs;
-        unsigned char *dst = p.v_cache + (us / BS) * kpage + vrow * BS + us % BS;
+        unsigned char *dst = p.v_cache + block_base(us) + (uint32_t)(vrow * BS + us % BS);
 #pragma unroll
         for (int d = 0; d < 2; ++d) {
           if constexpr (kTPS == 16)
@@ -1248,7 +1244,7 @@ __device__ __forceinline__ void fp8_ring_body(const AppendFp8Params &p, const Qu
           const int64_t ts = __shfl_sync(0xffffffffu, s, t);
           if (ts < 0) continue;
           const uint64_t us = (uint64_t)ts;
-          unsigned char *dst = p.v_cache + (us / BS) * kpage + vrow * BS + us % BS;
+          unsigned char *dst = p.v_cache + block_base(us) + (uint32_t)(vrow * BS + us % BS);
 #pragma unroll
           for (int d = 0; d < 2; ++d) dst[d * BS] = (unsigned char)(row[d][t >> 2] >> (8 * (t & 3)));
         }
@@ -1332,7 +1328,8 @@ int launch_append_fp8_t(const AppendArgs &a, cudaStream_t stream) {
     kv_append_fp8_token_kernel<T, BS, D><<<(unsigned)ctas, 128, 0, stream>>>(p);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
-  if (a.num_tokens >= 4096) {  // prefill chunks: persistent ring CTAs over (16-token tile, head pair)
+  if (a.num_tokens >= 4096 && a.num_blocks <= 0xffffffffll &&
+      (int64_t)a.num_kv_heads * D * BS <= 0xffffffffll) {  // prefill chunks: persistent ring CTAs
     using L = RingLayout<T, D, 2>;
     auto *kern = kv_append_fp8_ring_kernel<T, BS, D, 2>;
     static std::atomic<uint64_t> attr_done{0};
