@@ -749,11 +749,11 @@ __global__ void __launch_bounds__(kCopyThreads) swap_blocks_kernel(const SwapPar
 // ====================================================== fp8 KV append
 // Pages of one-byte E4M3 values with per-tensor scales: cache = value / scale
 // (IEEE division), rounded to nearest even and saturated to +-448 by the
-// cuda_fp8.h conversion. Calls of 128 tokens or more use the tiling of
-// kv_append_kernel: a tile of tokens (all kv heads) is quantised into shared
-// memory as bytes; K goes out as
-// 16-byte chunks (16 dims of one token), V by runs of consecutive slots of
-// one page row, as one vector store when a run fills an aligned group of
+// cuda_fp8.h conversion. Calls of 4096 tokens or more use the ring kernel
+// below; calls of 128-4095 tokens the tiling of kv_append_kernel: a tile of
+// tokens (all kv heads) is quantised into shared memory as bytes; K goes out
+// as 16-byte chunks (16 dims of one token), V by runs of consecutive slots
+// of one page row, as one vector store when a run fills an aligned group of
 // min(16, BS) tokens.
 struct AppendFp8Params {
   const unsigned char *key;
@@ -771,7 +771,6 @@ struct AppendFp8Params {
   int tile_tokens;
   int heads_per_tile;
   int row_pitch;  // bytes of one staged token row (one byte per element) + 16
-  int tiles_per_cta;  // 16-token tiles: consecutive tiles one CTA handles in turn
 };
 
 // The quotient x / s as the IEEE division rounds it, RN(x / s), from a
