@@ -345,12 +345,17 @@ int32_t vasr_pa_gather_kv_cache_fp8(void *key_out, void *value_out,
 
 /*
  * paged_attention_varlen_prefill_fp8: the varlen prefill over fp8 pages for
- * bf16 / f16 queries (dtype). The pages of each sequence's context are first
- * written to a 16-bit scratch pool in the workspace (byte * scale in dtype,
- * the 16-bit page layouts), then the prefill runs on that pool — the same
- * numbers as gather_kv_cache_fp8 followed by attention, without the packed
- * copy. workspace_size: bytes for num_seqs x max_num_blocks_per_seq pages of
- * every kv head (K and V) plus a block table. The workspace is scratch (its
+ * bf16 / f16 queries (dtype). 16-token pages with num_heads / num_kv_heads
+ * in {1, 2, 4}: the tcgen05 kernel reads the fp8 pages itself, converting
+ * each byte exactly to f16 on its way into shared memory (the products run
+ * in f16 with f32 accumulation; k_scale scales the scores, v_scale the
+ * output), and the workspace is not touched. Other page sizes: the pages of
+ * each sequence's context are first written to a 16-bit scratch pool in the
+ * workspace (byte * scale in dtype, the 16-bit page layouts), then the
+ * prefill runs on that pool — the same numbers as gather_kv_cache_fp8
+ * followed by attention, without the packed copy. workspace_size: bytes for
+ * num_seqs x max_num_blocks_per_seq pages of every kv head (K and V) plus a
+ * block table; required in every case. The workspace is scratch (its
  * contents are overwritten): not the paged_attention workspace, whose
  * counters must stay zero. head_dim 128.
  */

@@ -370,12 +370,27 @@ int32_t vasr_pa_paged_attention_varlen_prefill_fp8(
       prefill_fp8_layout(num_seqs, num_kv_heads, head_dim, block_size, max_num_blocks_per_seq);
   if (workspace == nullptr || workspace_bytes < l.total || !aligned16(workspace))
     return VASR_PA_EINVAL_WORKSPACE;
+  const cudaStream_t st = to_stream(stream);
+  // 16-token pages, head_dim 128, GQA 1 / 2 / 4: the tcgen05 prefill reads the
+  // fp8 pages itself (converted to f16 on their way into shared memory); the
+  // workspace is left untouched. Other shapes: dequantised pages in the
+  // workspace, then the 16-bit prefill.
+  {
+    vasr::PrefillArgs f{out, query, key_cache, value_cache, block_tables, context_lens, cu_seqlens_q,
+                        num_seqs, total_q_tokens, max_query_len, num_heads, num_kv_heads, head_dim,
+                        block_size, num_blocks, max_num_blocks_per_seq, scale, softcapping,
+                        q_token_stride, dtype};
+    f.cache_dtype = VASR_PA_FP8_E4M3;
+    f.k_scale = k_scale;
+    f.v_scale = v_scale;
+    const int32_t r = vasr::launch_prefill_umma(f, st);
+    if (r != VASR_PA_ENOT_SUPPORTED) return r;
+  }
   unsigned char *ws = static_cast<unsigned char *>(workspace);
   vasr::DequantArgs d{key_cache, value_cache, block_tables, context_lens, num_seqs,
                       max_num_blocks_per_seq, num_kv_heads, head_dim, block_size, num_blocks,
                       dtype, k_scale, v_scale, ws + l.off_k, ws + l.off_v,
                       reinterpret_cast<uint32_t *>(ws + l.off_table)};
-  const cudaStream_t st = to_stream(stream);
   const int32_t r = vasr::launch_dequant_pages(d, st);
   if (r != VASR_PA_OK) return r;
   vasr::PrefillArgs a{out, query, ws + l.off_k, ws + l.off_v,

@@ -99,7 +99,10 @@ struct PrefillArgs {
   float scale;
   float softcapping;
   int64_t q_token_stride;
-  int dtype;
+  int dtype;                       // element type of query / out (and of the pages by default)
+  int cache_dtype = -1;            // VASR_PA_FP8_E4M3: one-byte pages, real K = byte * k_scale
+  const float *k_scale = nullptr;  // device scalars (fp8 pages)
+  const float *v_scale = nullptr;
 };
 
 struct FusedRopeArgs {
@@ -214,8 +217,8 @@ inline int64_t prefill_tiles_per_seq(const PrefillArgs &a, int positions) {
   const int64_t mq = a.max_query_len > 0 ? a.max_query_len : a.total_q_tokens;
   return (mq + positions - 1) / positions;
 }
-// tcgen05 kernel (bf16/f16, 16-token pages, head_dim 128, G in {1,2,4});
-// VASR_PA_ENOT_SUPPORTED for any other shape.
+// tcgen05 kernel (bf16/f16 queries, 16-token bf16/f16 or fp8 pages, head_dim
+// 128, G in {1,2,4}); VASR_PA_ENOT_SUPPORTED for any other shape.
 int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s);
 int launch_copy_blocks(void *const *k, void *const *v, int layers, const int64_t *mapping,
                        int64_t pairs, int64_t num_blocks, int64_t block_bytes, cudaStream_t s);

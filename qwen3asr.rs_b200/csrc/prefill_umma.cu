@@ -66,7 +66,8 @@ constexpr int kM = 128;                      // rows per CTA (UMMA M)
 constexpr int kNT = 64;                      // keys per tile (UMMA N of S)
 constexpr int kBS = 16;                      // tokens per page
 constexpr int kPagesPerTile = kNT / kBS;     // 4
-constexpr int kPageBytes = kD * kBS * 2;     // one head's K or V page
+constexpr int kPageBytes = kD * kBS * 2;     // one head's K or V page (16-bit; the staged image)
+constexpr int kPageBytesF8 = kD * kBS;       // one head's K or V page of fp8 bytes
 constexpr int kStages = 2;
 constexpr int kQBytes = kM * kD * 2;         // 32 KB
 constexpr int kKVTile = kNT * kD * 2;        // 16 KB
@@ -77,12 +78,14 @@ constexpr int kOffBar = kOffV + kStages * kKVTile;
 // One commit per MMA group: "Q K^T j done" both fills S j and frees K
 // stage j & 1; "P V j done" both frees V stage j & 1 and the S buffer of j.
 // K and V stages are full after 32 cp.async arrivals (one per loader lane).
+// kBarQ16: fp8 pages with bf16 queries — Q converted to f16 in place by the
+// 128 softmax threads (the MMAs then run in f16, exact for every E4M3 value).
 constexpr int kBarFullK = 0, kBarFullV = 2, kBarSFull = 4, kBarPFull = 6, kBarPvDone = 8,
-              kBarQ = 10;
+              kBarQ = 10, kBarQ16 = 11;
 constexpr int kBarEmptyK = kBarSFull, kBarEmptyV = kBarPvDone;
-constexpr int kNumBars = 11;
+constexpr int kNumBars = 12;
 __host__ __device__ constexpr uint32_t bar_count(int i) {
-  return (i == kBarPFull || i == kBarPFull + 1) ? 128u : (i < kBarSFull ? 32u : 1u);
+  return (i == kBarPFull || i == kBarPFull + 1 || i == kBarQ16) ? 128u : (i < kBarSFull ? 32u : 1u);
 }
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemUsed = kOffTmemSlot + 16;
@@ -277,6 +280,21 @@ __device__ __forceinline__ uint32_t pack2f<__half>(float lo, float hi) {
   __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&v);
 }
+// 16 fp8 E4M3 bytes -> 16 f16 values (exact) as two 16-byte chunks: lo =
+// bytes 0-7, hi = bytes 8-15, each byte's value at its own position.
+__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v16) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v16 & 0xffffu), __NV_E4M3);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ void e4m3x16_f16(const uint4 &v, uint4 &lo, uint4 &hi) {
+  lo = make_uint4(e4m3x2_f16x2(v.x), e4m3x2_f16x2(v.x >> 16), e4m3x2_f16x2(v.y), e4m3x2_f16x2(v.y >> 16));
+  hi = make_uint4(e4m3x2_f16x2(v.z), e4m3x2_f16x2(v.z >> 16), e4m3x2_f16x2(v.w), e4m3x2_f16x2(v.w >> 16));
+}
+// 8 bf16 values -> 8 f16 values (round to nearest; |x| above 65504 becomes inf)
+__device__ __forceinline__ uint32_t bf16x2_f16x2(uint32_t w) {
+  __half2 h = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  return *reinterpret_cast<uint32_t *>(&h);
+}
 
 // ---------------------------------------------- split items: cluster combine
 // Every thread of every CTA of the cluster: a full cluster barrier (arrive has
@@ -325,7 +343,8 @@ static_assert(kOffRed + kM * 8 <= kOffBar, "the combine staging fits in the Q, K
 // whose waits gave up) contributes m = -inf and zeros.
 template <typename T, int G>
 __device__ void combine_splits(unsigned char *smem, uint32_t sbase, uint32_t t_o, int r, bool have,
-                               float m, float l, int splits, int n_pos, T *out, int64_t row_stride) {
+                               float m, float l, int splits, int n_pos, T *out, int64_t row_stride,
+                               float v_mul) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -377,7 +396,7 @@ __device__ void combine_splits(unsigned char *smem, uint32_t sbase, uint32_t t_o
       acc.z = fmaf(v[s].z, w, acc.z);
       acc.w = fmaf(v[s].w, w, acc.w);
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const float inv = L > 0.f ? v_mul / L : 0.f;
     T *orow = out + (int64_t)(row / G) * row_stride + (int64_t)(row % G) * kD;
     *reinterpret_cast<uint2 *>(orow + 4 * lane) =
         make_uint2(pack2f<T>(acc.x * inv, acc.y * inv), pack2f<T>(acc.z * inv, acc.w * inv));
@@ -386,11 +405,17 @@ __device__ void combine_splits(unsigned char *smem, uint32_t sbase, uint32_t t_o
 }
 
 // kSplit: launched as clusters of `splits` CTAs per item (else splits == 1
-// and the split code compiles away)
-template <typename T, int G, bool kSplit>
+// and the split code compiles away). kF8: fp8 E4M3 pages with per-tensor
+// scales; the loader warps convert each page to f16 on its way into shared
+// memory (registers instead of cp.async), the MMAs run in f16 (P too), a
+// bf16 Q is converted to f16 in place, k_scale joins the score scale and
+// v_scale the output scale.
+template <typename T, int G, bool kSplit, bool kF8>
 __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
     prefill_umma_kernel(const PrefillArgs p, const int tiles, const int splits_arg,
                         const __grid_constant__ CUtensorMap q_map) {
+  using TM = typename std::conditional<kF8, __half, T>::type;  // MMA operand type
+  constexpr bool kQConv = kF8 && std::is_same<T, __nv_bfloat16>::value;
   const int splits = kSplit ? splits_arg : 1;
   constexpr int kPos = kM / G;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -509,20 +534,51 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
       const int pga = lane >> 4, pgb = pga + 2, tok = lane & (kBS - 1);
       const uint32_t ida = __shfl_sync(0xffffffffu, id, pga), idb = __shfl_sync(0xffffffffu, id, pgb);
       const unsigned char *kc = static_cast<const unsigned char *>(p.key_cache);
-      const unsigned char *src_a = kc + ((int64_t)ida * p.num_kv_heads + kvh) * kPageBytes + tok * 16;
-      const unsigned char *src_b = kc + ((int64_t)idb * p.num_kv_heads + kvh) * kPageBytes + tok * 16;
-      const uint32_t dst = sbase + kOffK + (j & 1) * kKVTile + lane * 16;
+      if constexpr (kF8) {
+        // fp8 pages ([16-dim chunk][token][16 bytes]): 512 pieces per tile, 16
+        // per lane; piece (h, c) = 16-dim chunk c of key h * 32 + lane becomes
+        // the f16 chunks 2 c and 2 c + 1 of that key. All loads go out first.
+        const uint4 *src_a =
+            reinterpret_cast<const uint4 *>(kc + ((int64_t)ida * p.num_kv_heads + kvh) * kPageBytesF8) + tok;
+        const uint4 *src_b =
+            reinterpret_cast<const uint4 *>(kc + ((int64_t)idb * p.num_kv_heads + kvh) * kPageBytesF8) + tok;
+        uint4 v[2][kD / 16];
 #pragma unroll
-      for (int c = 0; c < kD / 8; ++c) {
-        if (pga < np) cp_async16(dst + c * (kNT * 16), src_a + c * (kBS * 16));
-        if (pgb < np) cp_async16(dst + c * (kNT * 16) + 32 * 16, src_b + c * (kBS * 16));
+        for (int c = 0; c < kD / 16; ++c) {
+          v[0][c] = pga < np ? __ldg(src_a + c * kBS) : make_uint4(0u, 0u, 0u, 0u);
+          v[1][c] = pgb < np ? __ldg(src_b + c * kBS) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        unsigned char *dst = smem + kOffK + (j & 1) * kKVTile + lane * 16;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int c = 0; c < kD / 16; ++c) {
+            uint4 lo, hi;
+            e4m3x16_f16(v[h][c], lo, hi);
+            *reinterpret_cast<uint4 *>(dst + (2 * c) * (kNT * 16) + h * 32 * 16) = lo;
+            *reinterpret_cast<uint4 *>(dst + (2 * c + 1) * (kNT * 16) + h * 32 * 16) = hi;
+          }
+        fence_proxy_async_smem();  // generic stores, read by the MMA through the async proxy
+        mbar_arrive(B(kBarFullK + (j & 1)));  // one of 32 arrivals
+      } else {
+        const unsigned char *src_a = kc + ((int64_t)ida * p.num_kv_heads + kvh) * kPageBytes + tok * 16;
+        const unsigned char *src_b = kc + ((int64_t)idb * p.num_kv_heads + kvh) * kPageBytes + tok * 16;
+        const uint32_t dst = sbase + kOffK + (j & 1) * kKVTile + lane * 16;
+#pragma unroll
+        for (int c = 0; c < kD / 8; ++c) {
+          if (pga < np) cp_async16(dst + c * (kNT * 16), src_a + c * (kBS * 16));
+          if (pgb < np) cp_async16(dst + c * (kNT * 16) + 32 * 16, src_b + c * (kBS * 16));
+        }
+        cp_async_arrive_noinc(B(kBarFullK + (j & 1)));  // one of 32 arrivals, when this lane's copies land
       }
-      cp_async_arrive_noinc(B(kBarFullK + (j & 1)));  // one of 32 arrivals, when this lane's copies land
     };
+    // (fp8 conversions wait for their loads: after the CTA-wide sync, so
+    // that the other warps do not wait for them)
+    if constexpr (kF8) __syncthreads();
     if (n_loc > 0) load_k(0);
     if (n_loc > 1) load_k(1);
     int k_issued = min(n_loc, 2);
-    __syncthreads();
+    if constexpr (!kF8) __syncthreads();
     // Q K^T j completes in order; K j + 2 goes into its stage once it has.
     // Once a wait gives up, nothing more is issued: a stage whose reader has
     // not finished must not receive another copy.
@@ -556,6 +612,35 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
       int np;
       const uint32_t id = tile_page(jb + j, np);
       const unsigned char *vc = static_cast<const unsigned char *>(p.value_cache);
+      if constexpr (kF8) {
+        // fp8 pages ([dim][16 tokens]): 512 16-byte rows per tile, 16 per
+        // lane; row (pg, q) = dim q * 32 + lane of page pg becomes the two
+        // 16-byte halves of its 32-byte f16 row in the swizzled image
+        uint4 v[kPagesPerTile][kD / 32];
+#pragma unroll
+        for (int pg = 0; pg < kPagesPerTile; ++pg) {
+          const uint32_t idp = __shfl_sync(0xffffffffu, id, pg);
+          const uint4 *src =
+              reinterpret_cast<const uint4 *>(vc + ((int64_t)idp * p.num_kv_heads + kvh) * kPageBytesF8) + lane;
+#pragma unroll
+          for (int q = 0; q < kD / 32; ++q)
+            v[pg][q] = pg < np ? __ldg(src + q * 32) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        unsigned char *dst = smem + kOffV + (j & 1) * kKVTile;
+#pragma unroll
+        for (int pg = 0; pg < kPagesPerTile; ++pg)
+#pragma unroll
+          for (int q = 0; q < kD / 32; ++q) {
+            const int d = q * 32 + lane, sw = (d >> 2) & 1;
+            uint4 lo, hi;
+            e4m3x16_f16(v[pg][q], lo, hi);
+            *reinterpret_cast<uint4 *>(dst + pg * kPageBytes + d * 32 + (sw << 4)) = lo;
+            *reinterpret_cast<uint4 *>(dst + pg * kPageBytes + d * 32 + ((sw ^ 1) << 4)) = hi;
+          }
+        fence_proxy_async_smem();
+        mbar_arrive(B(kBarFullV + (j & 1)));  // one of 32 arrivals
+        return;
+      }
       const uint32_t dst = sbase + kOffV + (j & 1) * kKVTile;
 #pragma unroll
       for (int pg = 0; pg < kPagesPerTile; ++pg) {
@@ -606,7 +691,7 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
     // once P j is stored. Each warp's commits track only its own MMAs. The
     // split variant (CTAs of one or two key tiles) issues both from warp 4,
     // which measured faster there.
-    const uint32_t idesc_s = idesc_f16<T>(kNT), idesc_o = idesc_f16<T>(kD);
+    const uint32_t idesc_s = idesc_f16<TM>(kNT), idesc_o = idesc_f16<TM>(kD);
     // Descriptors are built once; a later operand differs only in its start
     // address, the low field of the descriptor (address / 16 < 2^14 for any
     // shared-memory address), so it is the base descriptor plus offset / 16.
@@ -670,7 +755,7 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
     };
     if constexpr (!kSplit) {  // two issuing warps
       if (warp == kSMmaWarp) {
-        wait_phase(B(kBarQ), 0, dead);
+        wait_phase(B(kQConv ? kBarQ16 : kBarQ), 0, dead);
         for (int j = 0; j < n_loc && !dead; ++j) {
           if (j >= 2) wait_pv_before_s(j);
           if (!dead) issue_s(j);
@@ -679,7 +764,7 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
         for (int j = 0; j < n_loc && !dead; ++j) issue_pv(j);
       }
     } else if (warp == kMmaWarp) {  // split items (one or two key tiles per CTA): warp 4 issues both
-      wait_phase(B(kBarQ), 0, dead);
+      wait_phase(B(kQConv ? kBarQ16 : kBarQ), 0, dead);
       if (n_loc > 0 && !dead) issue_s(0);
       if (n_loc > 1 && !dead) issue_s(1);
       for (int j = 0; j < n_loc && !dead; ++j) {
@@ -711,7 +796,24 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
   const int lim = row_ok ? min(base_pos + r / G, kv_end - 1) : -1;  // last visible key
   const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
   const bool use_softcap = (p.softcapping != 1.0f) && (p.softcapping > 0.f);
-  const float cx = use_softcap ? 1.f : p.scale * kLog2e;
+  // fp8 pages hold K / k_scale: the scale of the scores takes k_scale
+  const float qk_scale = kF8 ? p.scale * __ldg(p.k_scale) : p.scale;
+  const float cx = use_softcap ? 1.f : qk_scale * kLog2e;
+  if constexpr (kQConv) {
+    // Q (bf16, landed by TMA) -> f16 in place, 256 bytes per thread; the
+    // Q K^T issuer waits for all 128 threads
+    wait_phase(B(kBarQ), 0, dead);
+    if (!dead) {
+      uint4 *qs = reinterpret_cast<uint4 *>(smem + kOffQ);
+#pragma unroll 4
+      for (int i = r; i < kQBytes / 16; i += 128) {
+        const uint4 v = qs[i];
+        qs[i] = make_uint4(bf16x2_f16x2(v.x), bf16x2_f16x2(v.y), bf16x2_f16x2(v.z), bf16x2_f16x2(v.w));
+      }
+      fence_proxy_async_smem();
+    }
+    mbar_arrive(B(kBarQ16));
+  }
   float m = -INFINITY, l = 0.f;
   for (int j = 0; j < n_loc; ++j) {
     wait_phase(B(kBarSFull + (j & 1)), (j >> 1) & 1, dead);
@@ -730,7 +832,7 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
     if (use_softcap) {
 #pragma unroll
       for (int k = 0; k < kNT; ++k)
-        x[k] = p.softcapping * tanhf(x[k] * p.scale / p.softcapping) * kLog2e;
+        x[k] = p.softcapping * tanhf(x[k] * qk_scale / p.softcapping) * kLog2e;
     }
     if (!__all_sync(0xffffffffu, kmax >= kNT - 1)) {  // diagonal / last tile: mask
 #pragma unroll
@@ -751,7 +853,7 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
       const float p0 = ex2_approx(fmaf(x[2 * k], cx, -off));
       const float p1 = ex2_approx(fmaf(x[2 * k + 1], cx, -off));
       s4[k & 3] += p0 + p1;
-      pk[k] = pack2f<T>(p0, p1);
+      pk[k] = pack2f<TM>(p0, p1);
     }
     l = l * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
     if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -790,14 +892,16 @@ __global__ void __launch_bounds__(kThreadsFor(kSplit), 2)
   tc_fence_after();
   if constexpr (kSplit) {
     combine_splits<T, G>(smem, sbase, tmem + lane_base + kTmemO, r, n_loc > 0 && !dead, m, l, splits,
-                         n_pos, out + (q0 + i0) * row_stride + (int64_t)kvh * G * kD, row_stride);
+                         n_pos, out + (q0 + i0) * row_stride + (int64_t)kvh * G * kD, row_stride,
+                         kF8 ? __ldg(p.v_scale) : 1.f);
     if (warp == 0) {
       tc_fence_after();
       tmem_dealloc(tmem, kTmemCols);
     }
     return;
   }
-  const float inv = l > 0.f ? 1.f / l : 0.f;
+  // fp8 pages hold V / v_scale
+  const float inv = l > 0.f ? (kF8 ? __ldg(p.v_scale) : 1.f) / l : 0.f;
   // O / l (16-bit) is staged in the Q buffer, which no MMA reads any more:
   // row r at r * 256 bytes, its 16-byte chunk c at slot c ^ (r % 16), so a
   // warp's stores of one chunk of 32 rows and the later reads of one row
@@ -874,11 +978,11 @@ bool make_q_map(CUtensorMap *map, const PrefillArgs &a, int g) {
              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T, int G>
+template <typename T, int G, bool kF8>
 int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
   static std::atomic<uint64_t> attr_done{0}, attr_done_split{0};
-  if (!ensure_smem_attr(prefill_umma_kernel<T, G, false>, kSmemBytes, attr_done) ||
-      !ensure_smem_attr(prefill_umma_kernel<T, G, true>, kSmemBytes, attr_done_split))
+  if (!ensure_smem_attr(prefill_umma_kernel<T, G, false, kF8>, kSmemBytes, attr_done) ||
+      !ensure_smem_attr(prefill_umma_kernel<T, G, true, kF8>, kSmemBytes, attr_done_split))
     return VASR_PA_ELAUNCH;
   constexpr int kPos = kM / G;
   const int64_t tiles = prefill_tiles_per_seq(a, kPos);
@@ -907,8 +1011,8 @@ int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
     }
   }
   if (splits == 1) {
-    prefill_umma_kernel<T, G, false><<<dim3((unsigned)items), kThreadsFor(false), kSmemBytes, s>>>(a, (int)tiles, 1,
-                                                                                               qmap);
+    prefill_umma_kernel<T, G, false, kF8><<<dim3((unsigned)items), kThreadsFor(false), kSmemBytes, s>>>(
+        a, (int)tiles, 1, qmap);
     return cudaPeekAtLastError() == cudaSuccess ? VASR_PA_OK : VASR_PA_ELAUNCH;
   }
   cudaLaunchConfig_t cfg{};
@@ -923,9 +1027,17 @@ int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prefill_umma_kernel<T, G, true>, a, (int)tiles, splits, qmap) == cudaSuccess
+  return cudaLaunchKernelEx(&cfg, prefill_umma_kernel<T, G, true, kF8>, a, (int)tiles, splits, qmap) == cudaSuccess
              ? VASR_PA_OK
              : VASR_PA_ELAUNCH;
+}
+
+template <int G>
+int launch_dt(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
+  const bool bf = a.dtype == VASR_PA_BF16;
+  if (a.cache_dtype == VASR_PA_FP8_E4M3)
+    return bf ? launch_g<__nv_bfloat16, G, true>(a, qmap, s) : launch_g<__half, G, true>(a, qmap, s);
+  return bf ? launch_g<__nv_bfloat16, G, false>(a, qmap, s) : launch_g<__half, G, false>(a, qmap, s);
 }
 
 }  // namespace
@@ -933,6 +1045,9 @@ int launch_g(const PrefillArgs &a, const CUtensorMap &qmap, cudaStream_t s) {
 int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s) {
   if (a.head_dim != kD || a.block_size != kBS) return VASR_PA_ENOT_SUPPORTED;
   if (a.dtype != VASR_PA_BF16 && a.dtype != VASR_PA_F16) return VASR_PA_ENOT_SUPPORTED;
+  if (a.cache_dtype != -1 && a.cache_dtype != a.dtype &&
+      (a.cache_dtype != VASR_PA_FP8_E4M3 || !a.k_scale || !a.v_scale))
+    return VASR_PA_ENOT_SUPPORTED;
   const int g = a.num_heads / a.num_kv_heads;
   if (g != 1 && g != 2 && g != 4) return VASR_PA_ENOT_SUPPORTED;
   if (a.total_q_tokens >= (int64_t(1) << 31)) return VASR_PA_ENOT_SUPPORTED;
@@ -944,14 +1059,10 @@ int launch_prefill_umma(const PrefillArgs &a, cudaStream_t s) {
     return VASR_PA_ENOT_SUPPORTED;
   CUtensorMap qmap;
   if (!make_q_map(&qmap, a, g)) return VASR_PA_ELAUNCH;
-  const bool bf = a.dtype == VASR_PA_BF16;
   switch (g) {
-    case 1:
-      return bf ? launch_g<__nv_bfloat16, 1>(a, qmap, s) : launch_g<__half, 1>(a, qmap, s);
-    case 2:
-      return bf ? launch_g<__nv_bfloat16, 2>(a, qmap, s) : launch_g<__half, 2>(a, qmap, s);
-    default:
-      return bf ? launch_g<__nv_bfloat16, 4>(a, qmap, s) : launch_g<__half, 4>(a, qmap, s);
+    case 1: return launch_dt<1>(a, qmap, s);
+    case 2: return launch_dt<2>(a, qmap, s);
+    default: return launch_dt<4>(a, qmap, s);
   }
 }
 

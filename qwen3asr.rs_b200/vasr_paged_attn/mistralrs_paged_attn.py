@@ -269,8 +269,10 @@ def paged_attention_varlen_prefill(q: torch.Tensor, key_cache: torch.Tensor, val
                                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Causal chunked prefill: packed q ``[T, Hq, D]`` against each sequence's pages.
 
-    fp8 (E4M3) pages need k_scale / v_scale; the pages are scaled into a 16-bit
-    scratch pool in the stream's workspace first."""
+    fp8 (E4M3) pages need k_scale / v_scale. 16-token pages at GQA 1 / 2 / 4 are
+    read by the tcgen05 kernel directly (bytes converted to f16 in shared
+    memory); other page sizes are scaled into a 16-bit scratch pool in the
+    stream's workspace first."""
     dev = _require_cuda(q, key_cache, value_cache, block_tables, context_lens, cu_seqlens_q)
     nb, hkv, d, bs = cache_geometry(key_cache, value_cache)
     if q.dim() != 3 or q.shape[2] != d or q.stride(2) != 1 or q.stride(1) != d:

@@ -185,15 +185,47 @@ def test_fp8_gather_requires_scales(cuda_device):
         pa.gather_kv_cache(kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), None, None, t, cu)
 
 
-@pytest.mark.parametrize("bs", [16, 32])
-def test_fp8_prefill_matches_oracle(cuda_device, bs):
-    """Varlen prefill over fp8 pages: the oracle runs the same causal mask on the dequantised pages."""
-    rng = np.random.default_rng(500 + bs)
+@pytest.mark.parametrize("bs,hq", [(16, 16), (32, 16), (16, 8), (16, 32)])
+def test_fp8_prefill_matches_oracle(cuda_device, bs, hq):
+    """Varlen prefill over fp8 pages: the oracle runs the same causal mask on the dequantised pages.
+    16-token pages (GQA 1 / 2 / 4) take the tcgen05 kernel, which converts the bytes exactly and
+    applies the scales to the scores and the output: the oracle sees byte x scale in f32. Other
+    page sizes go through the workspace's 16-bit pool of bf16(byte x scale)."""
+    rng = np.random.default_rng(500 + bs + hq)
     cached = np.array([0, 37, 256, 5], np.int64)
     chunk = np.array([90, 64, 100, 1], np.int64)
     ctx = cached + chunk
     ks, vs = 0.02, 0.015
     tables, kc, vc = _fp8_decode_case(rng, ctx, bs, ks, vs)
+    cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+    q = torch.from_numpy(rng.standard_normal((int(cu[-1]), hq, D)).astype(np.float32)).to(torch.bfloat16)
+    sk, sv = _scales(cuda_device, ks, vs)
+    out = pa.paged_attention_varlen_prefill(
+        q.to(cuda_device), torch.from_numpy(kc).to(cuda_device).view(torch.float8_e4m3fn),
+        torch.from_numpy(vc).to(cuda_device).view(torch.float8_e4m3fn),
+        torch.from_numpy(tables.astype(np.int32)).to(cuda_device),
+        torch.from_numpy(ctx.astype(np.int32)).to(cuda_device), torch.from_numpy(cu).to(cuda_device),
+        sk, sv, D ** -0.5).float().cpu().numpy()
+    kf = np.ascontiguousarray(ref.fp8_e4m3_decode(kc) * np.float32(ks))
+    vf = np.ascontiguousarray(ref.fp8_e4m3_decode(vc) * np.float32(vs))
+    if bs != 16:  # the 16-bit pool holds bf16(byte * scale): the oracle sees the same rounded pages
+        kf = torch.from_numpy(kf).to(torch.bfloat16).float().numpy()
+        vf = torch.from_numpy(vf).to(torch.bfloat16).float().numpy()
+    exp = ref.prefill_varlen(np.ascontiguousarray(q.float().numpy()), kf, vf,
+                             np.ascontiguousarray(tables.astype(np.uint32)), ctx.astype(np.uint32),
+                             cu.astype(np.uint32), D ** -0.5)
+    assert np.abs(out - exp).max() <= 2e-2
+
+
+def test_fp8_prefill_long_context_split(cuda_device):
+    """A launch of few items over a long fp8 context: the cluster-split variant of the tcgen05
+    kernel (key tiles shared by the CTAs of a cluster, combined in distributed shared memory)."""
+    rng = np.random.default_rng(77)
+    cached = np.array([1490, 768], np.int64)
+    chunk = np.array([12, 7], np.int64)
+    ctx = cached + chunk
+    ks, vs = 0.03, 0.01
+    tables, kc, vc = _fp8_decode_case(rng, ctx, 16, ks, vs)
     cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
     q = torch.from_numpy(rng.standard_normal((int(cu[-1]), HQ, D)).astype(np.float32)).to(torch.bfloat16)
     sk, sv = _scales(cuda_device, ks, vs)
@@ -205,9 +237,6 @@ def test_fp8_prefill_matches_oracle(cuda_device, bs):
         sk, sv, D ** -0.5).float().cpu().numpy()
     kf = np.ascontiguousarray(ref.fp8_e4m3_decode(kc) * np.float32(ks))
     vf = np.ascontiguousarray(ref.fp8_e4m3_decode(vc) * np.float32(vs))
-    # the 16-bit pool holds bf16(byte * scale): the oracle sees the same rounded pages
-    kf = torch.from_numpy(kf).to(torch.bfloat16).float().numpy()
-    vf = torch.from_numpy(vf).to(torch.bfloat16).float().numpy()
     exp = ref.prefill_varlen(np.ascontiguousarray(q.float().numpy()), kf, vf,
                              np.ascontiguousarray(tables.astype(np.uint32)), ctx.astype(np.uint32),
                              cu.astype(np.uint32), D ** -0.5)
