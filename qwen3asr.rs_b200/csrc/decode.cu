@@ -23,7 +23,7 @@
 #define VASR_G2_NST_FP8 8
 #endif
 #ifndef VASR_G2_MINB_FP8
-#define VASR_G2_MINB_FP8 4
+#define VASR_G2_MINB_FP8 5
 #endif
 // GQA-2 bf16 / f16 pages: tensor-core score and P.V tiles (decode_mma.cuh)
 #ifndef VASR_DECODE_MMA

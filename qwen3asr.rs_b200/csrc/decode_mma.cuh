@@ -81,11 +81,20 @@ __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t v16) {
 // One stage of a warp's tokens (n_valid of them, kNTT tiles of 16 at sk / sv
 // in shared memory) through the tensor cores: per 16-token tile S = Q Kᵀ,
 // the running-max softmax update of rows 0 / 1 (lanes 0-7) and O += P V.
+// fp8 pages: O is kept transposed, O^T[16 dims x 8 heads] += V^T P^T per
+// 16-dim tile (V page rows as the A operand, P's score fragments as the B
+// operand unchanged), so all four accumulators of a tile are real (lane
+// (grp, 0): dims grp and grp + 8 of heads 0 and 1) and a tile takes half the
+// MMAs and registers of O[16 x 8 dims] with rows 2-15 padding.
+template <typename TC, int D>
+constexpr int dec_o_tiles() { return std::is_same<TC, __nv_fp8_e4m3>::value ? D / 16 : D / 8; }
+
 template <typename T, int BS, int D, typename TC, int kNTT, int kPB>
 __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_valid,
                                               const uint32_t (&qa)[D / 16][2], float c_log2,
                                               bool use_softcap, float scale, float softcap,
-                                              float (&o)[D / 8][4], float &m_used, float &l_part) {
+                                              float (&o)[dec_o_tiles<TC, D>()][4], float &m_used,
+                                              float &l_part) {
   constexpr bool kFp8 = std::is_same<TC, __nv_fp8_e4m3>::value;
   using TM = typename std::conditional<kFp8, __half, T>::type;  // MMA operand type
   constexpr int kKS = D / 16;
@@ -144,10 +153,21 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
       const float alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
       m_used = m_new;
       l_part *= alpha;
+      if constexpr (kFp8) {  // O^T: heads 0 / 1 are the columns; their alphas live in lanes 0 / 4
+        const float a0 = __shfl_sync(0xffffffffu, alpha, 0), a1 = __shfl_sync(0xffffffffu, alpha, 4);
 #pragma unroll
-      for (int j = 0; j < D / 8; ++j) {
-        o[j][0] *= alpha;
-        o[j][1] *= alpha;
+        for (int j = 0; j < D / 16; ++j) {
+          o[j][0] *= a0;
+          o[j][1] *= a1;
+          o[j][2] *= a0;
+          o[j][3] *= a1;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < D / 8; ++j) {
+          o[j][0] *= alpha;
+          o[j][1] *= alpha;
+        }
       }
     }
     const float off = (m_used == -INFINITY) ? 0.f : m_used;
@@ -168,18 +188,25 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
       const int tk = t0 + 4 * tig;
       const uint32_t mlo = (tk < n_valid ? 0xffffu : 0u) | (tk + 1 < n_valid ? 0xffff0000u : 0u);
       const uint32_t mhi = (tk + 2 < n_valid ? 0xffffu : 0u) | (tk + 3 < n_valid ? 0xffff0000u : 0u);
+      // O^T += V^T P^T: matrices 2 hf (dims 16 (2 dq + hf) + 0..7) and
+      // 2 hf + 1 (+ 8..15) of the x4 are the A rows grp / grp + 8; the
+      // token pairs (4 tig, 4 tig + 1) and (4 tig + 2, 4 tig + 3) are the
+      // permuted k pairs of P's fragments (pa0, pa2), here the B operand
 #pragma unroll
       for (int dq = 0; dq < D / 32; ++dq) {
         uint32_t r[4];
         dec_ldmatrix_x4(vrow + dq * 32 * BS, r[0], r[1], r[2], r[3]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t b0 = fp8x2_to_h2(r[j]), b1 = fp8x2_to_h2(r[j] >> 16);
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t a0 = fp8x2_to_h2(r[2 * hf]), a2 = fp8x2_to_h2(r[2 * hf] >> 16);
+          uint32_t a1 = fp8x2_to_h2(r[2 * hf + 1]), a3 = fp8x2_to_h2(r[2 * hf + 1] >> 16);
           if (tail) {
-            b0 &= mlo;
-            b1 &= mhi;
+            a0 &= mlo;
+            a1 &= mlo;
+            a2 &= mhi;
+            a3 &= mhi;
           }
-          dec_mma<TM>(o[dq * 4 + j], pa0, 0u, pa2, 0u, b0, b1);
+          dec_mma<TM>(o[dq * 2 + hf], a0, a1, a2, a3, pa0, pa2);
         }
       }
       continue;
@@ -331,9 +358,9 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
   const float v_mul = p.v_scale ? __ldg(p.v_scale) : 1.f;
   const float c_log2 = k_mul * kLog2e;
   const bool use_softcap = (p.softcap != 1.0f) && (p.softcap > 0.f);
-  float o[D / 8][4];
+  float o[dec_o_tiles<TC, D>()][4];
 #pragma unroll
-  for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  for (int j = 0; j < dec_o_tiles<TC, D>(); ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_used = -INFINITY, l_part = 0.f;  // row grp (lanes 0-7 meaningful)
   bool aborted = false;
   int u_abort = 0;
@@ -371,11 +398,21 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
     m_used = -INFINITY;
     l_row = 0.f;
   }
-  if (grp < G) {
+  if (grp < G && tig == 0) {
+    cm[warp * G + grp] = m_used;
+    cl[warp * G + grp] = l_row;
+  }
+  if constexpr (kFp8) {  // O^T: lane (grp, 0) holds dims grp, grp + 8 of each 16-dim tile, both heads
     if (tig == 0) {
-      cm[warp * G + grp] = m_used;
-      cl[warp * G + grp] = l_row;
+#pragma unroll
+      for (int j = 0; j < D / 16; ++j) {
+        co[(warp * G) * D + j * 16 + grp] = aborted ? 0.f : o[j][0];
+        co[(warp * G + 1) * D + j * 16 + grp] = aborted ? 0.f : o[j][1];
+        co[(warp * G) * D + j * 16 + grp + 8] = aborted ? 0.f : o[j][2];
+        co[(warp * G + 1) * D + j * 16 + grp + 8] = aborted ? 0.f : o[j][3];
+      }
     }
+  } else if (grp < G) {
 #pragma unroll
     for (int j = 0; j < D / 8; ++j) {
       co[(warp * G + grp) * D + j * 8 + tig * 2] = aborted ? 0.f : o[j][0];
