@@ -12,11 +12,13 @@
 //                                  n-tiles, K read by ldmatrix straight from
 //                                  the K page ([D/8][bs][8]: a row of 8 dims
 //                                  of one token is one 16-byte ldmatrix row)
-//   O[16 x 128] += P[16 x 16] V    16 n-tiles of 8 dims, V read by ldmatrix
-//                                  from the V page ([D][bs]: 8 tokens of one
-//                                  dim per row)
-// ~100 instructions per 16 tokens. Only lanes 0-7 (rows 0 and 1) carry
-// results. The softmax keeps a per-row running maximum that moves only when
+//   O^T[128 x 8] += V^T P^T        8 m-tiles of 16 dims, V^T (the V page,
+//                                  [D][bs]: dim rows of the tile's tokens) as
+//                                  the A operand by ldmatrix, P's score
+//                                  fragments as the B operand (columns 0, 1
+//                                  = the two heads)
+// ~90 instructions per 16 tokens. Rows 0 and 1 of S live in lanes 0-7; O^T's
+// columns 0 and 1 in lanes with tig = 0. The softmax keeps a per-row running maximum that moves only when
 // a tile's maximum exceeds it by more than 2^8 (O is then rescaled), exact in
 // real arithmetic because numerator and denominator share the offset.
 // Tokens past the split's end are masked in S and their V entries zeroed in
@@ -80,14 +82,14 @@ __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t v16) {
 
 // One stage of a warp's tokens (n_valid of them, kNTT tiles of 16 at sk / sv
 // in shared memory) through the tensor cores: per 16-token tile S = Q Kᵀ,
-// the running-max softmax update of rows 0 / 1 (lanes 0-7) and O += P V.
-// fp8 pages: O is kept transposed, O^T[16 dims x 8 heads] += V^T P^T per
-// 16-dim tile (V page rows as the A operand, P's score fragments as the B
-// operand unchanged), so all four accumulators of a tile are real (lane
-// (grp, 0): dims grp and grp + 8 of heads 0 and 1) and a tile takes half the
-// MMAs and registers of O[16 x 8 dims] with rows 2-15 padding.
+// the running-max softmax update of rows 0 / 1 (lanes 0-7) and O^T += V^T P^T.
+// O is kept transposed, O^T[16 dims x 8 heads] += V^T P^T per 16-dim tile
+// (V page rows as the A operand, P's score fragments as the B operand
+// unchanged), so all four accumulators of a tile are real (lane (grp, 0):
+// dims grp and grp + 8 of heads 0 and 1) and a tile takes half the MMAs and
+// registers of O[16 x 8 dims] with rows 2-15 padding.
 template <typename TC, int D>
-constexpr int dec_o_tiles() { return std::is_same<TC, __nv_fp8_e4m3>::value ? D / 16 : D / 8; }
+constexpr int dec_o_tiles() { return D / 16; }
 
 template <typename T, int BS, int D, typename TC, int kNTT, int kPB>
 __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_valid,
@@ -153,7 +155,7 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
       const float alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
       m_used = m_new;
       l_part *= alpha;
-      if constexpr (kFp8) {  // O^T: heads 0 / 1 are the columns; their alphas live in lanes 0 / 4
+      {  // O^T: heads 0 / 1 are the columns; their alphas live in lanes 0 / 4
         const float a0 = __shfl_sync(0xffffffffu, alpha, 0), a1 = __shfl_sync(0xffffffffu, alpha, 4);
 #pragma unroll
         for (int j = 0; j < D / 16; ++j) {
@@ -161,12 +163,6 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
           o[j][1] *= a1;
           o[j][2] *= a0;
           o[j][3] *= a1;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < D / 8; ++j) {
-          o[j][0] *= alpha;
-          o[j][1] *= alpha;
         }
       }
     }
@@ -177,11 +173,11 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
       pv[e] = exp2f(x[e] - off);
       l_part += pv[e];
     }
-    // P as the A operand (rows 8-15 zero): k = tokens of the tile
+    // P's fragments (rows = heads, k = tokens of the tile): the B operand of V^T P^T
     const uint32_t pa0 = dec_pack2<TM>(pv[0], pv[1]), pa2 = dec_pack2<TM>(pv[2], pv[3]);
     const bool tail = (t0 + 16 > n_valid);
     if constexpr (kFp8) {
-      // ---- O += P V: one ldmatrix row = the tile's 16 tokens of one dim;
+      // ---- O^T += V^T P^T: one ldmatrix row = the tile's 16 tokens of one dim;
       // matrix j of an x4 = 8 dims, lane tig holds tokens 4 tig .. 4 tig + 3
       const int vd = (lane >> 3) * 8 + (lane & 7);
       const uint32_t vrow = sv + (t0 / BS) * kPB + vd * BS + t0 % BS;
@@ -211,7 +207,7 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
       }
       continue;
     }
-    // ---- O += P V: V rows = dims, 8 tokens per ldmatrix row
+    // ---- O^T += V^T P^T: V rows = dims, 8 tokens per ldmatrix row
     const int vd = (lane & 7) + (lane >> 4) * 8;
     const int vtok = t0 + ((lane >> 3) & 1) * 8;
     const uint32_t vrow = sv + (vtok / BS) * kPB + (vd * BS + vtok % BS) * 2;
@@ -228,8 +224,10 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
         b1 &= m1;
         b3 &= m1;
       }
-      dec_mma<TM>(o[2 * dp], pa0, 0u, pa2, 0u, b0, b1);
-      dec_mma<TM>(o[2 * dp + 1], pa0, 0u, pa2, 0u, b2, b3);
+      // O^T += V^T P^T: the x4's matrices (dims 0-7 / 8-15 x tokens 0-7 /
+      // 8-15) are the A fragments of the 16 x 16 V^T tile, P's score
+      // fragments the B operand
+      dec_mma<TM>(o[dp], b0, b2, b1, b3, pa0, pa2);
     }
   }
 }
@@ -402,7 +400,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
     cm[warp * G + grp] = m_used;
     cl[warp * G + grp] = l_row;
   }
-  if constexpr (kFp8) {  // O^T: lane (grp, 0) holds dims grp, grp + 8 of each 16-dim tile, both heads
+  {  // O^T: lane (grp, 0) holds dims grp, grp + 8 of each 16-dim tile, both heads
     if (tig == 0) {
 #pragma unroll
       for (int j = 0; j < D / 16; ++j) {
@@ -411,12 +409,6 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
         co[(warp * G) * D + j * 16 + grp + 8] = aborted ? 0.f : o[j][2];
         co[(warp * G + 1) * D + j * 16 + grp + 8] = aborted ? 0.f : o[j][3];
       }
-    }
-  } else if (grp < G) {
-#pragma unroll
-    for (int j = 0; j < D / 8; ++j) {
-      co[(warp * G + grp) * D + j * 8 + tig * 2] = aborted ? 0.f : o[j][0];
-      co[(warp * G + grp) * D + j * 8 + tig * 2 + 1] = aborted ? 0.f : o[j][1];
     }
   }
   __syncthreads();
