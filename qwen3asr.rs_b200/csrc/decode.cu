@@ -25,6 +25,12 @@
 #ifndef VASR_G2_MINB_FP8
 #define VASR_G2_MINB_FP8 5
 #endif
+// fp8 pages, grids of at least two waves at this occupancy: the same kernel
+// at 6 CTAs per SM with the query fragments in shared memory (one wave: the
+// extra CTA per SM slows the longest splits, which set the time)
+#ifndef VASR_G2_MINB_FP8_WIDE
+#define VASR_G2_MINB_FP8_WIDE 6
+#endif
 // GQA-2 bf16 / f16 pages: tensor-core score and P.V tiles (decode_mma.cuh)
 #ifndef VASR_DECODE_MMA
 #define VASR_DECODE_MMA 1
@@ -142,6 +148,14 @@ int launch_decode_g2(const DecodeArgs &a, cudaStream_t stream) {
     static std::atomic<uint64_t> attr_done{0};
     if (!ensure_smem_attr(kern, C::kSmemBytes, attr_done)) return VASR_PA_ELAUNCH;
     dim3 grid((unsigned)w.max_splits, (unsigned)a.num_kv_heads, (unsigned)a.num_seqs);
+    if constexpr (kFp8Pages && VASR_G2_MINB_FP8_WIDE > kMinB) {
+      auto wide = paged_decode_mma_kernel<T, BS, D, kNST, VASR_G2_MINB_FP8_WIDE, TC>;
+      static std::atomic<uint64_t> attr_wide{0};
+      static std::atomic<int64_t> resident[64];
+      if (!ensure_smem_attr(wide, C::kSmemBytes, attr_wide)) return VASR_PA_ELAUNCH;
+      const int64_t slots = resident_ctas(wide, C::kThreads, C::kSmemBytes, resident);
+      if (slots > 0 && (int64_t)grid.x * grid.y * grid.z >= 2 * slots) kern = wide;
+    }
     if (VASR_DECODE_PDL && a.overlap_append) {
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = grid;

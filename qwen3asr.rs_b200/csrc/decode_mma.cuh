@@ -74,6 +74,12 @@ __device__ __forceinline__ uint32_t dec_pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
+__device__ __forceinline__ uint2 dec_lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
 // fp8 E4M3 pair -> f16 pair (exact), as one 32-bit A/B fragment register
 __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t v16) {
   __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v16 & 0xffffu), __NV_E4M3);
@@ -91,9 +97,11 @@ __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t v16) {
 template <typename TC, int D>
 constexpr int dec_o_tiles() { return D / 16; }
 
-template <typename T, int BS, int D, typename TC, int kNTT, int kPB>
+// kQSmem (fp8 pages, 6 CTAs per SM): the query fragments are read from
+// shared memory per k-step instead of held in registers.
+template <typename T, int BS, int D, typename TC, int kNTT, int kPB, bool kQSmem>
 __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_valid,
-                                              const uint32_t (&qa)[D / 16][2], float c_log2,
+                                              const uint32_t (&qa)[D / 16][2], uint32_t sq, float c_log2,
                                               bool use_softcap, float scale, float softcap,
                                               float (&o)[dec_o_tiles<TC, D>()][4], float &m_used,
                                               float &l_part) {
@@ -117,12 +125,18 @@ __device__ __forceinline__ void dec_mma_stage(uint32_t sk, uint32_t sv, int n_va
       for (int kp = 0; kp < kKS / 2; ++kp) {
         uint32_t r0, r1, r2, r3;
         dec_ldmatrix_x4(krow + kp * 2 * (BS * 16), r0, r1, r2, r3);
-        dec_mma<TM>(sacc[0], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r0), fp8x2_to_h2(r0 >> 16));
-        dec_mma<TM>(sacc[1], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, fp8x2_to_h2(r1), fp8x2_to_h2(r1 >> 16));
-        dec_mma<TM>(sacc[0], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r2),
-                    fp8x2_to_h2(r2 >> 16));
-        dec_mma<TM>(sacc[1], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, fp8x2_to_h2(r3),
-                    fp8x2_to_h2(r3 >> 16));
+        uint2 q0 = make_uint2(qa[2 * kp][0], qa[2 * kp][1]), q1 = make_uint2(qa[2 * kp + 1][0], qa[2 * kp + 1][1]);
+        if constexpr (kQSmem) {  // lanes 0-7 hold the two heads' rows; the other rows are zero
+          q0 = q1 = make_uint2(0u, 0u);
+          if (lane < 8) {
+            q0 = dec_lds64(sq + (uint32_t)(((2 * kp) * 8 + lane) * 8));
+            q1 = dec_lds64(sq + (uint32_t)(((2 * kp + 1) * 8 + lane) * 8));
+          }
+        }
+        dec_mma<TM>(sacc[0], q0.x, 0u, q0.y, 0u, fp8x2_to_h2(r0), fp8x2_to_h2(r0 >> 16));
+        dec_mma<TM>(sacc[1], q0.x, 0u, q0.y, 0u, fp8x2_to_h2(r1), fp8x2_to_h2(r1 >> 16));
+        dec_mma<TM>(sacc[0], q1.x, 0u, q1.y, 0u, fp8x2_to_h2(r2), fp8x2_to_h2(r2 >> 16));
+        dec_mma<TM>(sacc[1], q1.x, 0u, q1.y, 0u, fp8x2_to_h2(r3), fp8x2_to_h2(r3 >> 16));
       }
     } else {
       const int ktok = t0 + (lane & 7) + (lane >> 4) * 8;
@@ -351,6 +365,23 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
     }
   }
 
+  // fp8 pages at 6 CTAs per SM: lanes 0-7's query fragments go to shared
+  // memory (the P staging area of the CUDA-core kernel, unused here) and are
+  // read per k-step, which leaves the registers to the sixth CTA
+  constexpr bool kQSmem = kFp8 && MINB >= 6;
+  const uint32_t s_q = s_base + C::kOffP;
+  if constexpr (kQSmem) {
+    static_assert(C::kWarps * G * C::kST * 4 >= kKS * 8 * 8, "query fragments fit the P area");
+    if (warp == 0 && lane < 8) {
+#pragma unroll
+      for (int ks = 0; ks < kKS; ++ks)
+        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(s_q + (uint32_t)((ks * 8 + lane) * 8)),
+                     "r"(qa[ks][0]), "r"(qa[ks][1])
+                     : "memory");
+    }
+    __syncthreads();
+  }
+
   // fp8 pages hold K / k_scale and V / v_scale
   const float k_mul = p.k_scale ? p.scale * __ldg(p.k_scale) : p.scale;
   const float v_mul = p.v_scale ? __ldg(p.v_scale) : 1.f;
@@ -373,7 +404,7 @@ __global__ void __launch_bounds__(128, MINB) paged_decode_mma_kernel(const Decod
     const int n_valid = min(C::kST, tok_end - (tok_begin + u * C::kST));
     const uint32_t sk = s_base + C::kOffK + s * C::kSP * C::kPB;
     const uint32_t sv = s_base + C::kOffV + s * C::kSP * C::kPB;
-    dec_mma_stage<T, BS, D, TC, C::kNTT, C::kPB>(sk, sv, n_valid, qa, c_log2, use_softcap, p.scale,
+    dec_mma_stage<T, BS, D, TC, C::kNTT, C::kPB, kQSmem>(sk, sv, n_valid, qa, s_q, c_log2, use_softcap, p.scale,
                                                   p.softcap, o, m_used, l_part);
     __syncwarp();
     const int nu = u + C::kNST;

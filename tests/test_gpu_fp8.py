@@ -98,6 +98,31 @@ def test_fp8_decode_matches_oracle(cuda_device, bs):
     assert np.abs(out - exp).max() <= 2e-2
 
 
+def test_fp8_decode_multi_wave_grid(cuda_device):
+    """A launch of at least two waves at six CTAs per SM (64 sequences, max_context_len 4096 as an
+    upper bound: four splits per (sequence, kv head), 2048 CTAs) takes the fp8 decode's wide
+    instantiation (query fragments in shared memory); splits past a sequence's end exit."""
+    rng = np.random.default_rng(777)
+    ctx = rng.integers(20, 700, size=64).astype(np.int64)
+    ctx[:3] = [1, 16, 699]
+    ks, vs = 0.02, 0.015
+    tables, kc, vc = _fp8_decode_case(rng, ctx, 16, ks, vs)
+    q = torch.from_numpy(rng.standard_normal((len(ctx), HQ, D)).astype(np.float32)).to(torch.bfloat16)
+    sk, sv = _scales(cuda_device, ks, vs)
+    out = pa.paged_attention(q.to(cuda_device), sk, sv,
+                             torch.from_numpy(kc).to(cuda_device).view(torch.float8_e4m3fn),
+                             torch.from_numpy(vc).to(cuda_device).view(torch.float8_e4m3fn),
+                             torch.from_numpy(tables.astype(np.int32)).to(cuda_device),
+                             torch.from_numpy(ctx.astype(np.int32)).to(cuda_device), None,
+                             4096, D ** -0.5, 1.0, None).float().cpu().numpy()
+    kf = np.ascontiguousarray(ref.fp8_e4m3_decode(kc) * np.float32(ks))
+    vf = np.ascontiguousarray(ref.fp8_e4m3_decode(vc) * np.float32(vs))
+    exp = ref.paged_attention(np.ascontiguousarray(q.float().numpy()), kf, vf,
+                              np.ascontiguousarray(tables.astype(np.uint32)), ctx.astype(np.uint32),
+                              D ** -0.5)
+    assert np.abs(out - exp).max() <= 2e-2
+
+
 def test_fp8_append_then_decode(cuda_device):
     """Append bf16 K/V into fp8 pages on the GPU, then decode; the oracle quantises the same values."""
     rng = np.random.default_rng(9)
