@@ -372,7 +372,9 @@ pub fn paged_attention_varlen_prefill(
         dev_ptr(cu_seqlens_q, &s)? as *const u32,
     );
     let st = if is_fp8(key_cache) {
-        // the live pages are scaled into a 16-bit scratch pool first
+        // the library needs the workspace only for page sizes its tcgen05
+        // kernel does not read directly (it converts 16-token fp8 pages
+        // itself); the entry point asks for it in every case
         let (k_sc, v_sc) = scales(k_scale, v_scale)?;
         let need = unsafe {
             ffi::vasr_pa_paged_attention_varlen_prefill_fp8_workspace_size(
