@@ -98,7 +98,8 @@ def test_fp8_decode_matches_oracle(cuda_device, bs):
     assert np.abs(out - exp).max() <= 2e-2
 
 
-def test_fp8_decode_multi_wave_grid(cuda_device):
+@pytest.mark.parametrize("bs", [16, 32])
+def test_fp8_decode_multi_wave_grid(cuda_device, bs):
     """A launch of at least two waves at six CTAs per SM (64 sequences, max_context_len 4096 as an
     upper bound: four splits per (sequence, kv head), 2048 CTAs) takes the fp8 decode's wide
     instantiation (query fragments in shared memory); splits past a sequence's end exit."""
@@ -106,7 +107,7 @@ def test_fp8_decode_multi_wave_grid(cuda_device):
     ctx = rng.integers(20, 700, size=64).astype(np.int64)
     ctx[:3] = [1, 16, 699]
     ks, vs = 0.02, 0.015
-    tables, kc, vc = _fp8_decode_case(rng, ctx, 16, ks, vs)
+    tables, kc, vc = _fp8_decode_case(rng, ctx, bs, ks, vs)
     q = torch.from_numpy(rng.standard_normal((len(ctx), HQ, D)).astype(np.float32)).to(torch.bfloat16)
     sk, sv = _scales(cuda_device, ks, vs)
     out = pa.paged_attention(q.to(cuda_device), sk, sv,
